@@ -1,0 +1,403 @@
+#!/usr/bin/env python
+"""Benchmark of the gsplat_core hot path on B200.
+
+A step is one forward + backward pass of the 3DGS training step over the
+benchmark scene (gsplat_core.pipeline.TrainingStep): projection, SH colour
+glue, tile intersection (count, scan, encode, radix sort, offsets),
+rasterize forward and backward, projection backward, SH backward.
+
+Default workload (N=1): BASELINE config 3 -- 1M Gaussians, SH degree 3,
+one 1297x840 camera.  With --gpus N (torchrun, one rank per GPU) every rank
+renders its own camera of the same scene (weak scaling) and the
+per-Gaussian gradients are summed with one NCCL all-reduce per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is Mpix/s over all ranks; ms/step and
+intersections sorted/s ride along.  The reference arm times the
+reference's own CPU code (eval_cpu compiled from the reference sources,
+oracle/_ref) -- or the C restatement when that build is absent -- on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gsplat-mlx_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd ms/step and Mpix/s at 1M Gaussians SH3; intersections sorted/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return PEAKS_FALLBACK, "fallback"
+
+
+def scene_for(rank, world, seed):
+    """Config 3; rank r > 0 views the same scene from its own camera."""
+    from gsplat_core import synthetic as S
+    sc = S.config3(seed=seed)
+    if rank > 0:
+        th = 2.0 * np.pi * rank / max(world, 1)
+        p0 = np.array([0.0, -1.0, -3.87298])
+        rot = np.array([[np.cos(th), 0, np.sin(th)], [0, 1, 0], [-np.sin(th), 0, np.cos(th)]])
+        sc.viewmats = S.look_at(rot @ p0)[None]
+    return sc
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the
+    timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(max(smax)) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+
+def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
+    """Bytes each stage must move at minimum (the roofline convention)."""
+    return {
+        # means/quats/scales in (40 B), 2D outputs out (36 B) per Gaussian
+        "projection_fwd": n * (40 + 36),
+        # means + campos in, colours out for all; coefficient rows of visible
+        "sh_fwd": n * (12 + 8 + 12) + visible * K * 12,
+        "isect_count_scan": n * (16 + 4) + n * 8,
+        "isect_encode": n * 24 + m * 12,
+        "isect_sort": m * 24 * sort_passes,
+        "isect_offset": m * 8,
+        # per intersection: flatten id + Gaussian record; per pixel: outputs
+        "rasterize_fwd": m * 40 + pixels * 20,
+        "rasterize_bwd": m * (40 + 36) + pixels * 20,
+        "projection_bwd": n * (8 + 12 + 8 + 4 + 12) + n * (40 + 40),
+        "sh_bwd": n * (12 + 12 + 12) + visible * K * 12 + n * K * 12,
+    }[stage]
+
+
+def our_kernel_launches(sort_passes):
+    # projection fwd 1, glue fwd 1, count 1, scan 3, encode 1,
+    # sort passes x (upsweep + 3 scan + downsweep), offset 1,
+    # rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
+    return 1 + 1 + 1 + 3 + 1 + sort_passes * 5 + 1 + 1 + 1 + 1 + 1
+
+
+# ------------------------------------------------------------------ CPU arms
+
+def cpu_step(checker, sc, vrc, vra, stride):
+    """One reference-CPU step on a bounded sample: projection, SH colours
+    and the intersection pipeline over all Gaussians; rasterize fwd+bwd on
+    every `stride`-th tile (tile masks), with the raster time scaled by
+    `stride`.  Returns (seconds, extrapolated seconds, intersections)."""
+    t0 = time.perf_counter()
+    p = checker.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
+                         quats=sc.quats[None], scales=sc.scales[None])
+    campos = -(sc.viewmats[0, :3, :3].T @ sc.viewmats[0, :3, 3])
+    dirs = (sc.means - campos).astype(np.float32)
+    dirs /= np.maximum(np.linalg.norm(dirs, axis=-1, keepdims=True), 1e-8)
+    colors = np.clip(checker.sh_fwd(sc.sh_degree, dirs, sc.coeffs) + 0.5, 0, 1)[None]
+    m2 = p["means2d"].reshape(1, -1, 2)
+    it = checker.isect_tile(m2, p["radii"].reshape(1, -1, 2), p["depths"].reshape(1, -1), 1,
+                            sc.tile_size, sc.tile_width, sc.tile_height)
+    offs = checker.isect_offset(it["isect_ids"], 1, sc.tile_width, sc.tile_height)
+    t1 = time.perf_counter()
+    masks = np.zeros((1, sc.tile_height, sc.tile_width), bool)
+    masks.reshape(-1)[::stride] = True
+    kw = dict(means2d=m2, conics=p["conics"].reshape(1, -1, 3), colors=colors,
+              opacities=sc.opacities[None], tile_offsets=offs, flatten_ids=it["flatten_ids"],
+              width=sc.width, height=sc.height, tile_size=sc.tile_size, masks=masks)
+    rf = checker.raster_fwd(**kw)
+    rb = checker.raster_bwd(render_alphas=rf["render_alphas"], last_ids=rf["last_ids"],
+                            v_render_colors=vrc, v_render_alphas=vra, **kw)
+    t2 = time.perf_counter()
+    checker.sh_bwd(sc.sh_degree, dirs, sc.coeffs, rb["v_colors"][0])
+    checker.proj_bwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
+                     p["radii"], p["conics"], rb["v_means2d"][None],
+                     np.zeros(p["depths"].shape, np.float32), rb["v_conics"][None],
+                     quats=sc.quats[None], scales=sc.scales[None])
+    t3 = time.perf_counter()
+    full = (t1 - t0) + (t2 - t1) * stride + (t3 - t2)
+    return t3 - t0, full, int(it["isect_ids"].size)
+
+
+def make_checker():
+    from oracle.oracle import Oracle, Reference
+    if Reference.available():
+        return Reference(), "reference"
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "oracle"], check=False)
+    return Oracle(), "port"
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from gsplat_core import synthetic as S
+    checker, kind = make_checker()
+    sc = scene_for(0, 1, args.seed)
+    vrc, vra = S.cotangents(args.seed, 1, sc.height, sc.width)
+    stride = args.cpu_stride
+    for _ in range(args.warmup):
+        cpu_step(checker, sc, vrc, vra, stride)
+    fulls = []
+    m = 0
+    for _ in range(args.steps):
+        _, full, m = cpu_step(checker, sc, vrc, vra, stride)
+        fulls.append(full)
+    ms = 1e3 * float(np.mean(fulls))
+    pixels = sc.width * sc.height
+    value = pixels / (ms / 1e3) / 1e6
+    sample = (f"config 3 step; projection/SH/intersect on all {sc.n} Gaussians, rasterize "
+              f"fwd+bwd on every {stride}th of {sc.tile_width * sc.tile_height} tiles, raster "
+              f"time scaled x{stride} (extrapolated)")
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Mpix/s",
+           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 3 shapes)",
+           "config": {"workload": "cfg3: N=1M SH3, 1 camera 1297x840, tile 16",
+                      "gaussians": sc.n, "isects": m},
+           "intersections_sorted_per_s": round(m / (ms / 1e3), 1),
+           "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": 1,
+                            "kind": kind, "sample": sample},
+           "e2e": {"value": round(value, 4), "unit": "Mpix/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from gsplat_core import pipeline, synthetic as S
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    sc = scene_for(rank, world, args.seed)
+    vrc_np, vra_np = S.cotangents(args.seed + rank, 1, sc.height, sc.width)
+    host = {"means": sc.means, "quats": sc.quats, "scales": sc.scales,
+            "opacities": sc.opacities, "coeffs": sc.coeffs, "viewmats": sc.viewmats,
+            "Ks": sc.Ks, "v_render_colors": vrc_np, "v_render_alphas": vra_np}
+    order = list(host)
+    d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in host.items()}
+    pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in host.items()}
+    step = pipeline.TrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], 1, sc.width, sc.height,
+                                 device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def one(inp):
+        flat, m = step.run(*[inp[k] for k in order])
+        if world > 1:
+            dist.all_reduce(flat)
+        return m
+
+    for _ in range(args.warmup):
+        one(d)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # ---- timed region: K steps, device-resident inputs, L2 flushed between
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # older torch: fall back to the ordinal
+        gpu_id = str(local)
+    clocks = ClockSampler(gpu_id)
+    clocks.start()
+    time.sleep(0.3)
+    step.events = []
+    stage_ms = {}
+    step_ms = []
+    m = 0
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        s_ev = torch.cuda.Event(enable_timing=True)
+        e_ev = torch.cuda.Event(enable_timing=True)
+        step.events = []
+        s_ev.record()
+        m = one(d)
+        e_ev.record()
+        torch.cuda.synchronize()
+        step_ms.append(s_ev.elapsed_time(e_ev))
+        evs = step.events
+        for (n0, a), (n1, b) in zip(evs[:-1], evs[1:]):
+            stage_ms.setdefault(n1, []).append(a.elapsed_time(b))
+    step.events = None
+    clk = clocks.stop()
+    local_ms = float(np.sum(step_ms))
+    t = torch.tensor([local_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_step = total_ms / args.steps
+    pixels = sc.width * sc.height * world
+    value = pixels * args.steps / (total_ms / 1e3) / 1e6
+
+    # ---- e2e: host (pinned) inputs copied in, gradients copied out, each step
+    grad_host = torch.empty(step.grad_flat.shape, dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values())
+    d2h = grad_host.numel() * 4
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.fill_(1.0)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s_ev = torch.cuda.Event(enable_timing=True)
+        e_ev = torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        dev_in = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
+        one(dev_in)
+        grad_host.copy_(step.grad_flat, non_blocking=True)
+        e_ev.record()
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(s_ev.elapsed_time(e_ev))
+    t = torch.tensor([float(np.sum(e2e_ms))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = pixels * args.steps / (float(t.item()) / 1e3) / 1e6
+
+    if rank == 0:
+        peaks, peak_kind = load_peaks()
+        hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+        visible = int(((step.radii[..., 0] > 0) & (step.radii[..., 1] > 0)).sum().item())
+        K = sc.coeffs.shape[1]
+        passes = (step.key_bits + 7) // 8
+        avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
+        top = max(avg, key=avg.get)
+        bytes_top = algorithmic_bytes(top, sc.n, visible, m, sc.width * sc.height, K, passes)
+        achieved = bytes_top / (avg[top] / 1e3) / 1e9
+        stages = {}
+        for k, v in avg.items():
+            b = algorithmic_bytes(k, sc.n, visible, m, sc.width * sc.height, K, passes)
+            stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
+                         "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            checker, kind = make_checker()
+            sc0 = scene_for(0, 1, args.seed)
+            _, full, _ = cpu_step(checker, sc0, vrc_np, vra_np, args.cpu_stride)
+            cpu = {"value": round(sc0.width * sc0.height / full / 1e6, 4), "unit": "Mpix/s",
+                   "cores": 1, "kind": kind,
+                   "sample": (f"one config-3 step; rasterize fwd+bwd on every "
+                              f"{args.cpu_stride}th tile, raster time scaled "
+                              f"x{args.cpu_stride} (extrapolated); other stages in full")}
+        out = {
+            "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, BASELINE config 3 distributions)",
+            "config": {"workload": "cfg3: N=1M SH3 Gaussians, 1 camera 1297x840 per GPU, tile 16",
+                       "gaussians": sc.n, "visible": visible, "isects": m,
+                       "parallelism": f"camera-sharded dp{world}" if world > 1 else "single",
+                       "l2": "flushed (256 MB write) between timed steps"},
+            "intersections_sorted_per_s": round(m * world / (ms_step / 1e3), 1),
+            "stages_ms": stages,
+            "roofline": {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "peak_source": peak_kind, "traffic": None,
+                         "algorithmic_bytes": int(bytes_top)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": our_kernel_launches(passes) * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-stride", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

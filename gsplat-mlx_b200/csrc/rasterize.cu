@@ -1,0 +1,503 @@
+// Rasterize to pixels (3DGS): front-to-back alpha compositing, forward and
+// backward.
+//
+// Per-pixel semantics: gsplat_rasterize.cpp:249-569 (CPU) ==
+// metal/gsplat_rasterize.metal:31-251 -- sigma = 0.5(c0 dx^2 + c2 dy^2) +
+// c1 dx dy at the pixel centre, alpha = min(0.99, o e^-sigma), skip when
+// sigma < 0 or alpha < 1/255, stop before compositing once T(1-alpha) <=
+// 1e-4, last_id = last composited intersection.
+//
+// B200 mapping: one CTA per (image, tile), one thread per pixel.  The
+// tile's intersection range is walked in batches of BLOCK Gaussians staged
+// in shared memory (the Metal kernel re-reads device memory per pixel).
+// Forward CTAs stop as soon as every pixel of the tile is saturated.  The
+// backward walks batches back to front from the CTA's largest last_id; per
+// Gaussian, the gradient terms of a warp's 32 pixels are summed with a
+// butterfly transpose-reduction (16 shuffles for up to 16 terms), added
+// into per-batch shared accumulators, and flushed with one global atomicAdd
+// per term per Gaussian per tile (the Metal kernel issues 5-8 global
+// atomics per pixel x Gaussian pair).
+#include "common.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr float kAlphaThreshold = 1.0f / 255.0f;
+constexpr float kMaxAlpha = 0.99f;
+constexpr float kTransmittanceThreshold = 1.0e-4f;
+constexpr float kMinOneMinusAlpha = 1.0e-6f;
+constexpr int kMaxChannels = 64;
+
+struct RArgs {
+  int I, N, CH, W, H, ts, tw, th;
+  int64_t n_isects;
+  const float* means2d;
+  const float* conics;
+  const float* colors;
+  const float* opacities;
+  const float* backgrounds;
+  const uint8_t* masks;
+  const int32_t* tile_offsets;
+  const int32_t* flatten_ids;
+};
+
+__device__ __forceinline__ void tile_range(const RArgs& a, int64_t tile, int& start, int& end) {
+  const int64_t n_tiles_total = (int64_t)a.I * a.tw * a.th;
+  start = __ldg(a.tile_offsets + tile);
+  end = (tile + 1 == n_tiles_total) ? (int)a.n_isects : __ldg(a.tile_offsets + tile + 1);
+}
+
+// ------------------------------------------------------------------ forward
+// CH > 0: channel count known at compile time (colours staged in smem and
+// accumulated in registers); CH == 0: runtime channel count up to 64.
+template <int CH>
+__global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
+                                  float* __restrict__ render_alphas,
+                                  int32_t* __restrict__ last_ids) {
+  extern __shared__ float smem[];
+  const int BLOCK = blockDim.x;
+  const int ch = CH > 0 ? CH : a.CH;
+  float2* s_xy = reinterpret_cast<float2*>(smem);
+  float4* s_co = reinterpret_cast<float4*>(smem + 2 * BLOCK);  // conic xyz, opacity
+  float* s_col = smem + 6 * BLOCK;                              // [BLOCK][ch]
+
+  const int64_t tile = blockIdx.x;
+  const int T = a.tw * a.th;
+  const int image = (int)(tile / T);
+  const int t = (int)(tile - (int64_t)image * T);
+  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const int tid = threadIdx.x;
+  const int ly = tid / a.ts, lx = tid - ly * a.ts;
+  const int x = tile_x * a.ts + lx, y = tile_y * a.ts + ly;
+  const bool inside = tid < a.ts * a.ts && x < a.W && y < a.H;
+  const int64_t pix = ((int64_t)image * a.H + y) * a.W + x;
+
+  if (a.masks && !a.masks[tile]) {
+    if (inside) {
+      for (int c = 0; c < ch; ++c)
+        render_colors[pix * ch + c] = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
+      render_alphas[pix] = 0.0f;
+      last_ids[pix] = 0;
+    }
+    return;
+  }
+  int start, end;
+  tile_range(a, tile, start, end);
+  const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+  float Tr = 1.0f;
+  int cur = 0;
+  bool done = !inside;
+  float acc[CH > 0 ? CH : 1];
+#pragma unroll
+  for (int c = 0; c < (CH > 0 ? CH : 1); ++c) acc[c] = 0.0f;
+  if (CH == 0 && inside)
+    for (int c = 0; c < ch; ++c) render_colors[pix * ch + c] = 0.0f;
+
+  for (int b0 = start; b0 < end; b0 += BLOCK) {
+    if (__syncthreads_count(!done) == 0) break;
+    const int idx = b0 + tid;
+    if (idx < end) {
+      const int g = __ldg(a.flatten_ids + idx);
+      s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+      s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
+                              __ldg(a.conics + (int64_t)g * 3 + 2), __ldg(a.opacities + g));
+      for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
+    }
+    __syncthreads();
+    const int cnt = min(BLOCK, end - b0);
+    for (int j = 0; j < cnt && !done; ++j) {
+      const float2 m = s_xy[j];
+      const float4 co = s_co[j];
+      const float dx = m.x - px, dy = m.y - py;
+      const float sigma = 0.5f * (co.x * dx * dx + co.z * dy * dy) + co.y * dx * dy;
+      const float alpha = fminf(kMaxAlpha, co.w * __expf(-sigma));
+      if (sigma < 0.0f || alpha < kAlphaThreshold) continue;
+      const float next_T = Tr * (1.0f - alpha);
+      if (next_T <= kTransmittanceThreshold) {
+        done = true;
+        break;
+      }
+      const float vis = alpha * Tr;
+      if (CH > 0) {
+#pragma unroll
+        for (int c = 0; c < (CH > 0 ? CH : 1); ++c) acc[c] += s_col[j * (CH > 0 ? CH : 1) + c] * vis;
+      } else {
+        for (int c = 0; c < ch; ++c) render_colors[pix * ch + c] += s_col[j * ch + c] * vis;
+      }
+      cur = b0 + j;
+      Tr = next_T;
+    }
+  }
+  if (inside) {
+    render_alphas[pix] = 1.0f - Tr;
+    if (CH > 0) {
+#pragma unroll
+      for (int c = 0; c < (CH > 0 ? CH : 1); ++c) {
+        const float bg = a.backgrounds ? __ldg(a.backgrounds + image * CH + c) : 0.0f;
+        render_colors[pix * CH + c] = acc[c] + Tr * bg;
+      }
+    } else {
+      for (int c = 0; c < ch; ++c) {
+        const float bg = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
+        render_colors[pix * ch + c] += Tr * bg;
+      }
+    }
+    last_ids[pix] = cur;
+  }
+}
+
+// ------------------------------------------------------------------ backward
+
+// Sum NV (<= 16) per-lane values over the warp.  After the call, lane l
+// with (l & 1) == 0 holds the warp total of value index red_index(l).
+template <int NV>
+__device__ __forceinline__ float butterfly_reduce(float (&v)[16], int lane) {
+  static_assert(NV <= 16, "at most 16 values");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool hi = lane & 16;
+    const float send = hi ? v[i] : v[i + 8];
+    const float keep = hi ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 8;
+    const float send = hi ? v[i] : v[i + 4];
+    const float keep = hi ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 4;
+    const float send = hi ? v[i] : v[i + 2];
+    const float keep = hi ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? v[0] : v[1];
+    const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return v[0];
+}
+
+__device__ __forceinline__ int red_index(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
+// Gradient terms per Gaussian: [0,1] v_xy, [2,3,4] v_conic, [5] v_opacity,
+// [6,7] |v_xy| (absgrad), [8..8+CH) v_colors.  With CH <= 4 everything fits
+// the 16-term butterfly; larger channel counts reduce colours separately.
+template <int CH>
+__global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alphas,
+                                  const int32_t* __restrict__ last_ids,
+                                  const float* __restrict__ v_render_colors,
+                                  const float* __restrict__ v_render_alphas, int absgrad,
+                                  float* __restrict__ v_means2d_abs, float* __restrict__ v_means2d,
+                                  float* __restrict__ v_conics, float* __restrict__ v_colors,
+                                  float* __restrict__ v_opacities,
+                                  float* __restrict__ v_backgrounds) {
+  extern __shared__ float smem[];
+  constexpr int CHS = CH > 0 ? CH : 1;
+  const int BLOCK = blockDim.x;
+  const int ch = CH > 0 ? CH : a.CH;
+  const int NT = 8 + ch;  // gradient terms per Gaussian
+  float2* s_xy = reinterpret_cast<float2*>(smem);
+  float4* s_co = reinterpret_cast<float4*>(smem + 2 * BLOCK);
+  float* s_col = smem + 6 * BLOCK;         // [BLOCK][ch]
+  float* s_acc = s_col + BLOCK * ch;       // [BLOCK][NT]
+  __shared__ int s_last;
+  __shared__ float s_bg[kMaxChannels];
+
+  const int64_t tile = blockIdx.x;
+  const int T = a.tw * a.th;
+  const int image = (int)(tile / T);
+  const int t = (int)(tile - (int64_t)image * T);
+  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int ly = tid / a.ts, lx = tid - ly * a.ts;
+  const int x = tile_x * a.ts + lx, y = tile_y * a.ts + ly;
+  const bool inside = tid < a.ts * a.ts && x < a.W && y < a.H;
+  const int64_t pix = ((int64_t)image * a.H + y) * a.W + x;
+
+  if (a.masks && !a.masks[tile]) return;
+  int start, end;
+  tile_range(a, tile, start, end);
+
+  const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+  const float T_final = inside ? 1.0f - __ldg(render_alphas + pix) : 1.0f;
+  float Tr = T_final;
+  const int my_last = inside ? min(end - 1, __ldg(last_ids + pix)) : -1;
+  const float v_ra = inside ? __ldg(v_render_alphas + pix) : 0.0f;
+  float v_rc[CHS];
+  float buf[CHS];
+  float v_rc_dyn[CH > 0 ? 1 : kMaxChannels];
+  float buf_dyn[CH > 0 ? 1 : kMaxChannels];
+  if (CH > 0) {
+#pragma unroll
+    for (int c = 0; c < CHS; ++c) {
+      v_rc[c] = inside ? __ldg(v_render_colors + pix * CHS + c) : 0.0f;
+      buf[c] = 0.0f;
+    }
+  } else {
+    for (int c = 0; c < ch; ++c) {
+      v_rc_dyn[c] = inside ? __ldg(v_render_colors + pix * ch + c) : 0.0f;
+      buf_dyn[c] = 0.0f;
+    }
+  }
+  // v_backgrounds += T_final * v_render_colors, reduced over the CTA.
+  if (tid < ch) s_bg[tid] = 0.0f;
+  if (tid == 0) s_last = -1;
+  __syncthreads();
+  if (v_backgrounds) {
+    for (int c = 0; c < ch; ++c) {
+      const float v = warp_sum(inside ? T_final * (CH > 0 ? v_rc[c < CHS ? c : 0] : v_rc_dyn[c]) : 0.0f);
+      if (lane == 0) atomicAdd(&s_bg[c], v);
+    }
+  }
+  // Background dot product used by every v_alpha of this pixel.
+  float bg_dot = 0.0f;
+  if (a.backgrounds) {
+    for (int c = 0; c < ch; ++c)
+      bg_dot += __ldg(a.backgrounds + image * ch + c) * (CH > 0 ? v_rc[c < CHS ? c : 0] : v_rc_dyn[c]);
+  }
+  if (inside) atomicMax(&s_last, my_last);
+  __syncthreads();
+  if (v_backgrounds && tid < ch && s_bg[tid] != 0.0f)
+    atomicAdd(v_backgrounds + image * ch + tid, s_bg[tid]);
+  const int cta_last = s_last;
+
+  for (int b_end = cta_last + 1; b_end > start; b_end -= BLOCK) {
+    const int b0 = max(start, b_end - BLOCK);
+    const int cnt = b_end - b0;
+    __syncthreads();
+    if (tid < cnt) {
+      const int g = __ldg(a.flatten_ids + b0 + tid);
+      s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+      s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
+                              __ldg(a.conics + (int64_t)g * 3 + 2), __ldg(a.opacities + g));
+      for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
+    }
+    for (int i = tid; i < cnt * NT; i += BLOCK) s_acc[i] = 0.0f;
+    __syncthreads();
+    for (int j = cnt - 1; j >= 0; --j) {
+      const int idx = b0 + j;
+      bool valid = idx <= my_last;
+      float vis = 0.0f, alpha = 0.0f, dx = 0.0f, dy = 0.0f;
+      const float2 m = s_xy[j];
+      const float4 co = s_co[j];
+      if (valid) {
+        dx = m.x - px;
+        dy = m.y - py;
+        const float sigma = 0.5f * (co.x * dx * dx + co.z * dy * dy) + co.y * dx * dy;
+        vis = __expf(-sigma);
+        alpha = fminf(kMaxAlpha, co.w * vis);
+        valid = !(sigma < 0.0f || alpha < kAlphaThreshold);
+      }
+      if (!__any_sync(0xffffffffu, valid)) continue;
+      float g[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) g[i] = 0.0f;
+      float gdyn_scale = 0.0f;  // fac, for the runtime-channel colour terms
+      if (valid) {
+        const float ra = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
+        Tr *= ra;
+        const float fac = alpha * Tr;
+        float v_alpha = 0.0f;
+        if (CH > 0) {
+#pragma unroll
+          for (int c = 0; c < CHS; ++c) {
+            const float col = s_col[j * CHS + c];
+            g[8 + c] = fac * v_rc[c];
+            v_alpha += (col * Tr - buf[c] * ra) * v_rc[c];
+            buf[c] += col * fac;
+          }
+        } else {
+          gdyn_scale = fac;
+          for (int c = 0; c < ch; ++c) {
+            const float col = s_col[j * ch + c];
+            v_alpha += (col * Tr - buf_dyn[c] * ra) * v_rc_dyn[c];
+            buf_dyn[c] += col * fac;
+          }
+        }
+        v_alpha += T_final * ra * v_ra;
+        if (a.backgrounds) v_alpha += -T_final * ra * bg_dot;
+        if (co.w * vis <= kMaxAlpha) {
+          const float v_sigma = -co.w * vis * v_alpha;
+          const float vx = v_sigma * (co.x * dx + co.y * dy);
+          const float vy = v_sigma * (co.y * dx + co.z * dy);
+          g[0] = vx;
+          g[1] = vy;
+          g[2] = 0.5f * v_sigma * dx * dx;
+          g[3] = v_sigma * dx * dy;
+          g[4] = 0.5f * v_sigma * dy * dy;
+          g[5] = vis * v_alpha;
+          g[6] = fabsf(vx);
+          g[7] = fabsf(vy);
+        }
+      }
+      const float r = butterfly_reduce<16>(g, lane);
+      const int ri = red_index(lane);
+      const int nfix = CH > 0 ? 8 + CHS : 8;
+      if ((lane & 1) == 0 && ri < nfix && r != 0.0f) atomicAdd(&s_acc[j * NT + ri], r);
+      if (CH == 0) {
+        for (int c = 0; c < ch; ++c) {
+          const float v = warp_sum(valid ? gdyn_scale * v_rc_dyn[c] : 0.0f);
+          if (lane == 0 && v != 0.0f) atomicAdd(&s_acc[j * NT + 8 + c], v);
+        }
+      }
+    }
+    __syncthreads();
+    // Flush this batch: one global atomic per non-zero term.
+    for (int i = tid; i < cnt * NT; i += BLOCK) {
+      const float v = s_acc[i];
+      if (v == 0.0f) continue;
+      const int j = i / NT, k = i - j * NT;
+      const int64_t gg = __ldg(a.flatten_ids + b0 + j);
+      if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
+      else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
+      else if (k == 5) atomicAdd(v_opacities + gg, v);
+      else if (k < 8) {
+        if (absgrad) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);
+      } else atomicAdd(v_colors + gg * ch + (k - 8), v);
+    }
+  }
+}
+
+int smem_bytes(int block, int ch, bool bwd) {
+  return (int)sizeof(float) * (block * (6 + ch) + (bwd ? block * (8 + ch) : 0));
+}
+
+template <int CH>
+int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cudaStream_t s) {
+  const int smem = smem_bytes(block, a.CH, false);
+  cudaFuncSetAttribute(raster_fwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int64_t tiles = (int64_t)a.I * a.tw * a.th;
+  raster_fwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, rc, ra, li);
+  return launch_status("rasterize_fwd");
+}
+
+template <int CH>
+int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, const float* vrc,
+               const float* vra, int absgrad, float* vabs, float* vm, float* vc, float* vcol,
+               float* vop, float* vbg, cudaStream_t s) {
+  const int smem = smem_bytes(block, a.CH, true);
+  cudaFuncSetAttribute(raster_bwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int64_t tiles = (int64_t)a.I * a.tw * a.th;
+  raster_bwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, ra, li, vrc, vra, absgrad, vabs, vm,
+                                                             vc, vcol, vop, vbg);
+  return launch_status("rasterize_bwd");
+}
+
+int check_raster(const gs_raster_params* p) {
+  if (!p) return invalid("rasterize: params missing");
+  if (p->I <= 0 || p->N < 0 || p->channels <= 0 || p->image_width < 0 || p->image_height < 0 ||
+      p->n_isects < 0)
+    return invalid("rasterize: bad params");
+  if (p->tile_size <= 0 || p->tile_size > 32)
+    return invalid("rasterize: tile_size must be in 1..32");
+  if (p->tile_width <= 0 || p->tile_height <= 0) return invalid("rasterize: bad tile grid");
+  if ((int64_t)p->tile_width * p->tile_size < p->image_width ||
+      (int64_t)p->tile_height * p->tile_size < p->image_height)
+    return invalid("rasterize: tile grid does not cover the image");
+  if (p->n_isects > INT32_MAX) {
+    set_error("rasterize: more than 2^31 intersections");
+    return GS_ERR_OVERFLOW;
+  }
+  if ((int64_t)p->I * p->tile_width * p->tile_height > INT32_MAX)
+    return invalid("rasterize: too many tiles");
+  return GS_OK;
+}
+
+RArgs make_args(const gs_raster_params* p, const float* means2d, const float* conics,
+                const float* colors, const float* opacities, const float* backgrounds,
+                const uint8_t* masks, const int32_t* tile_offsets, const int32_t* flatten_ids) {
+  return RArgs{p->I, p->N, p->channels, p->image_width, p->image_height, p->tile_size,
+               p->tile_width, p->tile_height, p->n_isects, means2d, conics, colors, opacities,
+               p->use_backgrounds ? backgrounds : nullptr, p->use_masks ? masks : nullptr,
+               tile_offsets, flatten_ids};
+}
+
+}  // namespace
+}  // namespace gsb
+
+using namespace gsb;
+
+extern "C" int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,
+                                const float* conics, const float* colors, const float* opacities,
+                                const float* backgrounds, const uint8_t* masks,
+                                const int32_t* tile_offsets, const int32_t* flatten_ids,
+                                float* render_colors, float* render_alphas, int32_t* last_ids,
+                                gs_stream_t stream) {
+  if (int rc = check_raster(p)) return rc;
+  if (p->channels > kMaxChannels) return invalid("rasterize: at most 64 channels");
+  if ((int64_t)p->image_width * p->image_height == 0) return GS_OK;
+  if (!render_colors || !render_alphas || !last_ids || !tile_offsets)
+    return invalid("rasterize_fwd: missing output buffer");
+  if (p->n_isects > 0 && (!means2d || !conics || !colors || !opacities || !flatten_ids))
+    return invalid("rasterize_fwd: missing input buffer");
+  if ((p->use_backgrounds && !backgrounds) || (p->use_masks && !masks))
+    return invalid("rasterize_fwd: missing backgrounds/masks");
+  if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_fwd: means2d must be 8-byte aligned");
+  const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                            flatten_ids);
+  const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
+  cudaStream_t s = as_stream(stream);
+  switch (p->channels) {
+    case 1: return launch_fwd<1>(a, block, render_colors, render_alphas, last_ids, s);
+    case 2: return launch_fwd<2>(a, block, render_colors, render_alphas, last_ids, s);
+    case 3: return launch_fwd<3>(a, block, render_colors, render_alphas, last_ids, s);
+    case 4: return launch_fwd<4>(a, block, render_colors, render_alphas, last_ids, s);
+    default: return launch_fwd<0>(a, block, render_colors, render_alphas, last_ids, s);
+  }
+}
+
+extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
+                                const float* conics, const float* colors, const float* opacities,
+                                const float* backgrounds, const uint8_t* masks,
+                                const int32_t* tile_offsets, const int32_t* flatten_ids,
+                                const float* render_alphas, const int32_t* last_ids,
+                                const float* v_render_colors, const float* v_render_alphas,
+                                float* v_means2d_abs, float* v_means2d, float* v_conics,
+                                float* v_colors, float* v_opacities, float* v_backgrounds,
+                                gs_stream_t stream) {
+  if (int rc = check_raster(p)) return rc;
+  if (p->channels > kMaxChannels) return invalid("rasterize_bwd: at most 64 channels");
+  if (!v_means2d || !v_conics || !v_colors || !v_opacities)
+    return invalid("rasterize_bwd: missing gradient buffer");
+  if (p->absgrad && !v_means2d_abs) return invalid("rasterize_bwd: v_means2d_abs missing");
+  if ((p->use_backgrounds && (!backgrounds || !v_backgrounds)) || (p->use_masks && !masks))
+    return invalid("rasterize_bwd: missing backgrounds/masks");
+  cudaStream_t s = as_stream(stream);
+  const int64_t nG = (int64_t)p->I * p->N;
+  const size_t f = sizeof(float);
+  if (nG > 0) {
+    if (cudaMemsetAsync(v_means2d, 0, f * 2 * nG, s) || cudaMemsetAsync(v_conics, 0, f * 3 * nG, s) ||
+        cudaMemsetAsync(v_colors, 0, f * p->channels * nG, s) ||
+        cudaMemsetAsync(v_opacities, 0, f * nG, s) ||
+        (p->absgrad && cudaMemsetAsync(v_means2d_abs, 0, f * 2 * nG, s)))
+      return launch_status("rasterize_bwd: zero gradients");
+  }
+  if (p->use_backgrounds && cudaMemsetAsync(v_backgrounds, 0, f * p->I * p->channels, s))
+    return launch_status("rasterize_bwd: zero v_backgrounds");
+  if ((int64_t)p->image_width * p->image_height == 0) return launch_status("rasterize_bwd");
+  if (!tile_offsets || !render_alphas || !last_ids || !v_render_colors || !v_render_alphas)
+    return invalid("rasterize_bwd: missing input buffer");
+  if (p->n_isects > 0 && (!means2d || !conics || !colors || !opacities || !flatten_ids))
+    return invalid("rasterize_bwd: missing input buffer");
+  if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_bwd: means2d must be 8-byte aligned");
+  const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                            flatten_ids);
+  const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
+  float* vbg = p->use_backgrounds ? v_backgrounds : nullptr;
+  switch (p->channels) {
+    case 1: return launch_bwd<1>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
+    case 2: return launch_bwd<2>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
+    case 3: return launch_bwd<3>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
+    case 4: return launch_bwd<4>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
+    default: return launch_bwd<0>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
+  }
+}

@@ -1,0 +1,511 @@
+// Spherical harmonics (degree 0..4), forward and backward, plus the fused
+// colour glue of the reference trainers.
+//
+// Basis and VJP math: gsplat_spherical_harmonics.cpp:116-425 (identical to
+// metal/gsplat_spherical_harmonics.metal:15-308).  One thread per element;
+// the degree is a template parameter so the basis is fully unrolled.  The
+// ops stream the coefficient rows (K*12 bytes per element, 192 B at SH3) and
+// are HBM-bound.
+#include "common.cuh"
+
+namespace gsb {
+namespace {
+
+constexpr float kC0 = 0.2820947917738781f;
+constexpr float kC1 = 0.48860251190292f;
+
+// Basis values b[0..(D+1)^2) of the unit direction (x, y, z); the zero-norm
+// guard of the reference (only the DC term) is applied by the caller.
+template <int D>
+__device__ __forceinline__ void basis(float x, float y, float z, float* b) {
+  b[0] = kC0;
+  if (D < 1) return;
+  b[1] = -kC1 * y;
+  b[2] = kC1 * z;
+  b[3] = -kC1 * x;
+  if (D < 2) return;
+  const float z2 = z * z;
+  const float t0b = -1.092548430592079f * z;
+  const float c1 = x * x - y * y, s1 = 2.0f * x * y;
+  b[4] = 0.5462742152960395f * s1;
+  b[5] = t0b * y;
+  b[6] = 0.9461746957575601f * z2 - 0.3153915652525201f;
+  b[7] = t0b * x;
+  b[8] = 0.5462742152960395f * c1;
+  if (D < 3) return;
+  const float t0c = -2.285228997322329f * z2 + 0.4570457994644658f;
+  const float t1b = 1.445305721320277f * z;
+  const float c2 = x * c1 - y * s1, s2 = x * s1 + y * c1;
+  b[9] = -0.5900435899266435f * s2;
+  b[10] = t1b * s1;
+  b[11] = t0c * y;
+  b[12] = z * (1.865881662950577f * z2 - 1.119528997770346f);
+  b[13] = t0c * x;
+  b[14] = t1b * c1;
+  b[15] = -0.5900435899266435f * c2;
+  if (D < 4) return;
+  const float t0d = z * (-4.683325804901025f * z2 + 2.007139630671868f);
+  const float t1c = 3.31161143515146f * z2 - 0.47308734787878f;
+  const float t2b = -1.770130769779931f * z;
+  const float c3 = x * c2 - y * s2, s3 = x * s2 + y * c2;
+  b[16] = 0.6258357354491763f * s3;
+  b[17] = t2b * s2;
+  b[18] = t1c * s1;
+  b[19] = t0d * y;
+  b[20] = 1.984313483298443f * z * b[12] - 1.006230589874905f * b[6];
+  b[21] = t0d * x;
+  b[22] = t1c * c1;
+  b[23] = t2b * c2;
+  b[24] = 0.6258357354491763f * c3;
+}
+
+// colour = sum_b basis_b * coeff_b, accumulated per degree band like the
+// reference (gsplat_spherical_harmonics.cpp:189-286).
+template <int D>
+__device__ __forceinline__ void sh_color(const float* d, const float* __restrict__ co, float out[3]) {
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) out[ch] = kC0 * __ldg(co + ch);
+  if (D < 1) return;
+  const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  if (norm == 0.0f) return;
+  const float x = d[0] / norm, y = d[1] / norm, z = d[2] / norm;
+  float b[25];
+  basis<D>(x, y, z, b);
+  constexpr int bands[5] = {1, 4, 9, 16, 25};
+#pragma unroll
+  for (int l = 1; l <= D; ++l) {
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int k = bands[l - 1]; k < bands[l]; ++k) acc += b[k] * __ldg(co + k * 3 + ch);
+      out[ch] += acc;
+    }
+  }
+}
+
+// gsplat_spherical_harmonics.cpp:288-425: d colour / d dir (un-normalised).
+template <int D>
+__device__ __forceinline__ void sh_dir_vjp(const float* d, const float* __restrict__ co,
+                                           const float vc[3], float vd[3]) {
+  vd[0] = vd[1] = vd[2] = 0.0f;
+  if (D < 1) return;
+  const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+  if (norm == 0.0f) return;
+  const float inorm = 1.0f / norm;
+  const float x = d[0] * inorm, y = d[1] * inorm, z = d[2] * inorm;
+  constexpr int A = (D + 1) * (D + 1);
+  float dx[25], dy[25], dz[25];
+#pragma unroll
+  for (int i = 0; i < A; ++i) dx[i] = dy[i] = dz[i] = 0.0f;
+  dx[3] = -kC1;
+  dy[1] = -kC1;
+  dz[2] = kC1;
+  const float z2 = z * z;
+  const float t0b = -1.092548430592079f * z;
+  const float c1 = x * x - y * y, s1 = 2.0f * x * y;
+  const float t0b_z = -1.092548430592079f;
+  const float c1_x = 2.0f * x, c1_y = -2.0f * y;
+  const float s1_x = 2.0f * y, s1_y = 2.0f * x;
+  const float p6_z = 2.0f * 0.9461746957575601f * z;
+  if (D >= 2) {
+    dx[4] = 0.5462742152960395f * s1_x;
+    dy[4] = 0.5462742152960395f * s1_y;
+    dy[5] = t0b;
+    dz[5] = t0b_z * y;
+    dz[6] = p6_z;
+    dx[7] = t0b;
+    dz[7] = t0b_z * x;
+    dx[8] = 0.5462742152960395f * c1_x;
+    dy[8] = 0.5462742152960395f * c1_y;
+  }
+  const float t0c = -2.285228997322329f * z2 + 0.4570457994644658f;
+  const float t1b = 1.445305721320277f * z;
+  const float c2 = x * c1 - y * s1, s2 = x * s1 + y * c1;
+  const float p12 = z * (1.865881662950577f * z2 - 1.119528997770346f);
+  const float t0c_z = -2.285228997322329f * 2.0f * z;
+  const float t1b_z = 1.445305721320277f;
+  const float c2_x = c1 + x * c1_x - y * s1_x;
+  const float c2_y = x * c1_y - s1 - y * s1_y;
+  const float s2_x = s1 + x * s1_x + y * c1_x;
+  const float s2_y = x * s1_y + c1 + y * c1_y;
+  const float p12_z = 3.0f * 1.865881662950577f * z2 - 1.119528997770346f;
+  if (D >= 3) {
+    dx[9] = -0.5900435899266435f * s2_x;
+    dy[9] = -0.5900435899266435f * s2_y;
+    dx[10] = t1b * s1_x;
+    dy[10] = t1b * s1_y;
+    dz[10] = t1b_z * s1;
+    dy[11] = t0c;
+    dz[11] = t0c_z * y;
+    dz[12] = p12_z;
+    dx[13] = t0c;
+    dz[13] = t0c_z * x;
+    dx[14] = t1b * c1_x;
+    dy[14] = t1b * c1_y;
+    dz[14] = t1b_z * c1;
+    dx[15] = -0.5900435899266435f * c2_x;
+    dy[15] = -0.5900435899266435f * c2_y;
+  }
+  if (D >= 4) {
+    const float t0d = z * (-4.683325804901025f * z2 + 2.007139630671868f);
+    const float t1c = 3.31161143515146f * z2 - 0.47308734787878f;
+    const float t2b = -1.770130769779931f * z;
+    const float t0d_z = 3.0f * -4.683325804901025f * z2 + 2.007139630671868f;
+    const float t1c_z = 2.0f * 3.31161143515146f * z;
+    const float t2b_z = -1.770130769779931f;
+    const float c3_x = c2 + x * c2_x - y * s2_x;
+    const float c3_y = x * c2_y - s2 - y * s2_y;
+    const float s3_x = s2 + y * c2_x + x * s2_x;
+    const float s3_y = x * s2_y + c2 + y * c2_y;
+    dx[16] = 0.6258357354491763f * s3_x;
+    dy[16] = 0.6258357354491763f * s3_y;
+    dx[17] = t2b * s2_x;
+    dy[17] = t2b * s2_y;
+    dz[17] = t2b_z * s2;
+    dx[18] = t1c * s1_x;
+    dy[18] = t1c * s1_y;
+    dz[18] = t1c_z * s1;
+    dy[19] = t0d;
+    dz[19] = t0d_z * y;
+    dz[20] = 1.984313483298443f * (p12 + z * p12_z) - 1.006230589874905f * p6_z;
+    dx[21] = t0d;
+    dz[21] = t0d_z * x;
+    dx[22] = t1c * c1_x;
+    dy[22] = t1c * c1_y;
+    dz[22] = t1c_z * c1;
+    dx[23] = t2b * c2_x;
+    dy[23] = t2b * c2_y;
+    dz[23] = t2b_z * c2;
+    dx[24] = 0.6258357354491763f * c3_x;
+    dy[24] = 0.6258357354491763f * c3_y;
+  }
+  float vn0 = 0.0f, vn1 = 0.0f, vn2 = 0.0f;
+#pragma unroll
+  for (int k = 1; k < A; ++k) {
+    const float vb = __ldg(co + k * 3) * vc[0] + __ldg(co + k * 3 + 1) * vc[1] +
+                     __ldg(co + k * 3 + 2) * vc[2];
+    vn0 += dx[k] * vb;
+    vn1 += dy[k] * vb;
+    vn2 += dz[k] * vb;
+  }
+  const float dot = vn0 * x + vn1 * y + vn2 * z;
+  vd[0] = (vn0 - dot * x) * inorm;
+  vd[1] = (vn1 - dot * y) * inorm;
+  vd[2] = (vn2 - dot * z) * inorm;
+}
+
+// v_coeffs row of one element: basis * v_colors for active bases, zeros for
+// the rest of the K rows (the reference zero-fills its output).
+template <int D>
+__device__ __forceinline__ void write_vcoeffs(const float* d, const float vc[3], int K,
+                                              float* __restrict__ out, bool accumulate) {
+  constexpr int A = (D + 1) * (D + 1);
+  float b[25];
+  b[0] = kC0;
+#pragma unroll
+  for (int k = 1; k < A; ++k) b[k] = 0.0f;
+  if (D >= 1) {
+    const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+    if (norm != 0.0f) basis<D>(d[0] / norm, d[1] / norm, d[2] / norm, b);
+  }
+#pragma unroll
+  for (int k = 0; k < A; ++k)
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) {
+      const float v = b[k] * vc[ch];
+      if (accumulate) out[k * 3 + ch] += v;
+      else out[k * 3 + ch] = v;
+    }
+  if (!accumulate)
+    for (int i = A * 3; i < K * 3; ++i) out[i] = 0.0f;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) sh_fwd_kernel(int64_t n, int K,
+                                                     const float* __restrict__ dirs,
+                                                     const float* __restrict__ coeffs,
+                                                     const uint8_t* __restrict__ masks,
+                                                     float* __restrict__ colors) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float c[3] = {0.0f, 0.0f, 0.0f};
+    if (!masks || masks[e]) {
+      const float d[3] = {__ldg(dirs + e * 3), __ldg(dirs + e * 3 + 1), __ldg(dirs + e * 3 + 2)};
+      sh_color<D>(d, coeffs + e * (int64_t)K * 3, c);
+    }
+    colors[e * 3] = c[0];
+    colors[e * 3 + 1] = c[1];
+    colors[e * 3 + 2] = c[2];
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) sh_bwd_kernel(int64_t n, int K,
+                                                     const float* __restrict__ dirs,
+                                                     const float* __restrict__ coeffs,
+                                                     const uint8_t* __restrict__ masks,
+                                                     const float* __restrict__ v_colors,
+                                                     float* __restrict__ v_dirs,
+                                                     float* __restrict__ v_coeffs) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    float* vco = v_coeffs + e * (int64_t)K * 3;
+    if (masks && !masks[e]) {
+      for (int i = 0; i < K * 3; ++i) vco[i] = 0.0f;
+      if (v_dirs) v_dirs[e * 3] = v_dirs[e * 3 + 1] = v_dirs[e * 3 + 2] = 0.0f;
+      continue;
+    }
+    const float d[3] = {__ldg(dirs + e * 3), __ldg(dirs + e * 3 + 1), __ldg(dirs + e * 3 + 2)};
+    const float vc[3] = {__ldg(v_colors + e * 3), __ldg(v_colors + e * 3 + 1),
+                         __ldg(v_colors + e * 3 + 2)};
+    write_vcoeffs<D>(d, vc, K, vco, false);
+    if (v_dirs) {
+      float vd[3];
+      sh_dir_vjp<D>(d, coeffs + e * (int64_t)K * 3, vc, vd);
+      v_dirs[e * 3] = vd[0];
+      v_dirs[e * 3 + 1] = vd[1];
+      v_dirs[e * 3 + 2] = vd[2];
+    }
+  }
+}
+
+// ------------------------------------------------------------ fused glue
+// scripts/test/scanner_points_training_utils.py:1005-1034 -- per Gaussian,
+// looping over the C cameras: u = means - campos_c, d = u / max(|u|, 1e-8),
+// colour = clip(SH(d) + 0.5, 0, 1).
+
+__device__ __forceinline__ void campos_of(const float* __restrict__ view, float cp[3]) {
+  const float R[9] = {__ldg(view + 0), __ldg(view + 1), __ldg(view + 2),
+                      __ldg(view + 4), __ldg(view + 5), __ldg(view + 6),
+                      __ldg(view + 8), __ldg(view + 9), __ldg(view + 10)};
+  const float t[3] = {__ldg(view + 3), __ldg(view + 7), __ldg(view + 11)};
+#pragma unroll
+  for (int i = 0; i < 3; ++i) cp[i] = -(R[i] * t[0] + R[3 + i] * t[1] + R[6 + i] * t[2]);
+}
+
+__device__ __forceinline__ bool visible(const uint8_t* __restrict__ masks,
+                                        const int32_t* __restrict__ radii, int64_t e) {
+  if (masks && !masks[e]) return false;
+  if (radii) {
+    const int2 r = __ldg(reinterpret_cast<const int2*>(radii) + e);
+    if (r.x <= 0 || r.y <= 0) return false;
+  }
+  return true;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) glue_fwd_kernel(int C, int N, int K,
+                                                       const float* __restrict__ means,
+                                                       const float* __restrict__ viewmats,
+                                                       const float* __restrict__ coeffs,
+                                                       const uint8_t* __restrict__ masks,
+                                                       const int32_t* __restrict__ radii,
+                                                       float* __restrict__ colors) {
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1), __ldg(means + n * 3 + 2)};
+    for (int c = 0; c < C; ++c) {
+      const int64_t e = (int64_t)c * N + n;
+      float out[3] = {0.0f, 0.0f, 0.0f};
+      if (visible(masks, radii, e)) {
+        float cp[3];
+        campos_of(viewmats + (int64_t)c * 16, cp);
+        const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+        const float s = fmaxf(sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]), 1.0e-8f);
+        const float d[3] = {u[0] / s, u[1] / s, u[2] / s};
+        sh_color<D>(d, coeffs + n * (int64_t)K * 3, out);
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) out[ch] = fminf(fmaxf(out[ch] + 0.5f, 0.0f), 1.0f);
+      }
+      colors[e * 3] = out[0];
+      colors[e * 3 + 1] = out[1];
+      colors[e * 3 + 2] = out[2];
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
+                                                       const float* __restrict__ means,
+                                                       const float* __restrict__ viewmats,
+                                                       const float* __restrict__ coeffs,
+                                                       const uint8_t* __restrict__ masks,
+                                                       const int32_t* __restrict__ radii,
+                                                       const float* __restrict__ v_colors,
+                                                       float* __restrict__ v_means,
+                                                       float* __restrict__ v_coeffs) {
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1), __ldg(means + n * 3 + 2)};
+    const float* co = coeffs + n * (int64_t)K * 3;
+    float* vco = v_coeffs + n * (int64_t)K * 3;
+    float vm[3] = {0.0f, 0.0f, 0.0f};
+    bool first = true;
+    for (int c = 0; c < C; ++c) {
+      const int64_t e = (int64_t)c * N + n;
+      if (!visible(masks, radii, e)) continue;
+      float cp[3];
+      campos_of(viewmats + (int64_t)c * 16, cp);
+      const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+      const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
+      const float mm = fmaxf(s, 1.0e-8f);
+      const float d[3] = {u[0] / mm, u[1] / mm, u[2] / mm};
+      float x[3];
+      sh_color<D>(d, co, x);
+      float vc[3];
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        const float v = x[ch] + 0.5f;
+        vc[ch] = (v > 0.0f && v < 1.0f) ? __ldg(v_colors + e * 3 + ch) : 0.0f;
+      }
+      write_vcoeffs<D>(d, vc, K, vco, !first);
+      first = false;
+      float vd[3];
+      sh_dir_vjp<D>(d, co, vc, vd);
+      const float dot = vd[0] * u[0] + vd[1] * u[1] + vd[2] * u[2];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        float vu = vd[i] / mm;
+        if (s > 1.0e-8f) vu -= (u[i] / s) * dot / (mm * mm);
+        vm[i] += vu;
+      }
+    }
+    if (first) {
+      for (int i = 0; i < K * 3; ++i) vco[i] = 0.0f;
+    } else {
+      constexpr int A = (D + 1) * (D + 1);
+      for (int i = A * 3; i < K * 3; ++i) vco[i] = 0.0f;
+    }
+    v_means[n * 3] += vm[0];
+    v_means[n * 3 + 1] += vm[1];
+    v_means[n * 3 + 2] += vm[2];
+  }
+}
+
+template <template <int> class Launch, typename... Args>
+int by_degree(int degree, Args... args) {
+  switch (degree) {
+    case 0: return Launch<0>::run(args...);
+    case 1: return Launch<1>::run(args...);
+    case 2: return Launch<2>::run(args...);
+    case 3: return Launch<3>::run(args...);
+    case 4: return Launch<4>::run(args...);
+    default: return invalid("spherical_harmonics supports degree 0..4.");
+  }
+}
+
+template <int D>
+struct FwdL {
+  static int run(const gs_sh_params* p, const float* dirs, const float* coeffs,
+                 const uint8_t* masks, float* colors, cudaStream_t s) {
+    sh_fwd_kernel<D><<<grid_for(p->n, 256), 256, 0, s>>>(p->n, p->K, dirs, coeffs,
+                                                         p->use_masks ? masks : nullptr, colors);
+    return launch_status("sh_fwd");
+  }
+};
+
+template <int D>
+struct BwdL {
+  static int run(const gs_sh_params* p, const float* dirs, const float* coeffs,
+                 const uint8_t* masks, const float* v_colors, float* v_dirs, float* v_coeffs,
+                 cudaStream_t s) {
+    sh_bwd_kernel<D><<<grid_for(p->n, 256), 256, 0, s>>>(
+        p->n, p->K, dirs, coeffs, p->use_masks ? masks : nullptr, v_colors, v_dirs, v_coeffs);
+    return launch_status("sh_bwd");
+  }
+};
+
+template <int D>
+struct GlueFwdL {
+  static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
+                 const float* coeffs, const uint8_t* masks, const int32_t* radii, float* colors,
+                 cudaStream_t s) {
+    glue_fwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(
+        p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii, colors);
+    return launch_status("sh_glue_fwd");
+  }
+};
+
+template <int D>
+struct GlueBwdL {
+  static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
+                 const float* coeffs, const uint8_t* masks, const int32_t* radii,
+                 const float* v_colors, float* v_means, float* v_coeffs, cudaStream_t s) {
+    glue_bwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(p->C, p->N, p->K, means, viewmats,
+                                                           coeffs, p->use_masks ? masks : nullptr,
+                                                           radii, v_colors, v_means, v_coeffs);
+    return launch_status("sh_glue_bwd");
+  }
+};
+
+int check_sh(const gs_sh_params* p) {
+  if (!p || p->n < 0) return invalid("spherical_harmonics: bad params");
+  if (p->degrees_to_use < 0 || p->degrees_to_use > 4)
+    return invalid("spherical_harmonics_forward supports degree 0..4.");
+  if (p->K < (p->degrees_to_use + 1) * (p->degrees_to_use + 1))
+    return invalid("coeffs has fewer SH bases than degrees_to_use requires.");
+  return GS_OK;
+}
+
+int check_glue(const gs_sh_glue_params* p) {
+  if (!p || p->C < 0 || p->N < 0) return invalid("sh_glue: bad params");
+  if (p->degrees_to_use < 0 || p->degrees_to_use > 4)
+    return invalid("sh_glue: degree must be 0..4");
+  if (p->K < (p->degrees_to_use + 1) * (p->degrees_to_use + 1))
+    return invalid("sh_glue: coeffs has fewer SH bases than the degree requires");
+  return GS_OK;
+}
+
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gs_sh_fwd(const gs_sh_params* p, const float* dirs, const float* coeffs,
+                         const uint8_t* masks, float* colors, gs_stream_t stream) {
+  using namespace gsb;
+  if (int rc = check_sh(p)) return rc;
+  if (p->n == 0) return GS_OK;
+  if (!dirs || !coeffs || !colors || (p->use_masks && !masks))
+    return invalid("sh_fwd: missing buffer");
+  return by_degree<FwdL>(p->degrees_to_use, p, dirs, coeffs, masks, colors, as_stream(stream));
+}
+
+extern "C" int gs_sh_bwd(const gs_sh_params* p, const float* dirs, const float* coeffs,
+                         const uint8_t* masks, const float* v_colors, float* v_dirs,
+                         float* v_coeffs, gs_stream_t stream) {
+  using namespace gsb;
+  if (int rc = check_sh(p)) return rc;
+  if (p->n == 0) return GS_OK;
+  if (!dirs || !coeffs || !v_colors || !v_coeffs || (p->use_masks && !masks))
+    return invalid("sh_bwd: missing buffer");
+  return by_degree<BwdL>(p->degrees_to_use, p, dirs, coeffs, masks, v_colors, v_dirs, v_coeffs,
+                         as_stream(stream));
+}
+
+extern "C" int gs_sh_glue_fwd(const gs_sh_glue_params* p, const float* means,
+                              const float* viewmats, const float* coeffs, const uint8_t* masks,
+                              const int32_t* radii, float* colors, gs_stream_t stream) {
+  using namespace gsb;
+  if (int rc = check_glue(p)) return rc;
+  if ((int64_t)p->C * p->N == 0) return GS_OK;
+  if (!means || !viewmats || !coeffs || !colors || (p->use_masks && !masks))
+    return invalid("sh_glue_fwd: missing buffer");
+  if (reinterpret_cast<uintptr_t>(radii) % 8) return invalid("sh_glue_fwd: radii must be 8-byte aligned");
+  return by_degree<GlueFwdL>(p->degrees_to_use, p, means, viewmats, coeffs, masks, radii, colors,
+                             as_stream(stream));
+}
+
+extern "C" int gs_sh_glue_bwd(const gs_sh_glue_params* p, const float* means,
+                              const float* viewmats, const float* coeffs, const uint8_t* masks,
+                              const int32_t* radii, const float* v_colors, float* v_means_accum,
+                              float* v_coeffs, gs_stream_t stream) {
+  using namespace gsb;
+  if (int rc = check_glue(p)) return rc;
+  if (p->N == 0) return GS_OK;
+  if (!means || !viewmats || !coeffs || !v_colors || !v_means_accum || !v_coeffs ||
+      (p->use_masks && !masks))
+    return invalid("sh_glue_bwd: missing buffer");
+  if (reinterpret_cast<uintptr_t>(radii) % 8) return invalid("sh_glue_bwd: radii must be 8-byte aligned");
+  return by_degree<GlueBwdL>(p->degrees_to_use, p, means, viewmats, coeffs, masks, radii,
+                             v_colors, v_means_accum, v_coeffs, as_stream(stream));
+}

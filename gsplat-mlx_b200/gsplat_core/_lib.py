@@ -1,0 +1,123 @@
+"""ctypes binding of libgsplat_b200.so (the C ABI declared in
+include/gsplat_b200.h).
+
+The shared library is the product's compute path; there is no fallback.
+Loading fails loudly when the library is missing or when no CUDA device is
+usable for a call.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("GSPLAT_B200_LIB", os.path.join(_HERE, "libgsplat_b200.so"))
+
+_vp = ct.c_void_p
+_i32 = ct.c_int32
+_i64 = ct.c_int64
+_f = ct.c_float
+_sz = ct.c_size_t
+
+GS_OK = 0
+GS_ERR_INVALID = 1
+GS_ERR_UNSUPPORTED = 2
+GS_ERR_OVERFLOW = 3
+GS_ERR_CUDA = 4
+GS_ERR_WORKSPACE = 5
+
+
+class QS2CParams(ct.Structure):
+    _fields_ = [("n", _i64), ("compute_covar", _i32), ("compute_preci", _i32), ("triu", _i32)]
+
+
+class ProjectionParams(ct.Structure):
+    _fields_ = [("B", _i32), ("C", _i32), ("N", _i32), ("image_width", _i32),
+                ("image_height", _i32), ("eps2d", _f), ("near_plane", _f), ("far_plane", _f),
+                ("radius_clip", _f), ("calc_compensations", _i32), ("camera_model", _i32),
+                ("use_covars", _i32), ("use_opacities", _i32)]
+
+
+class SHParams(ct.Structure):
+    _fields_ = [("n", _i64), ("K", _i32), ("degrees_to_use", _i32), ("use_masks", _i32)]
+
+
+class SHGlueParams(ct.Structure):
+    _fields_ = [("C", _i32), ("N", _i32), ("K", _i32), ("degrees_to_use", _i32),
+                ("use_masks", _i32)]
+
+
+class IsectParams(ct.Structure):
+    _fields_ = [("I", _i32), ("N", _i32), ("tile_size", _i32), ("tile_width", _i32),
+                ("tile_height", _i32)]
+
+
+class RasterParams(ct.Structure):
+    _fields_ = [("I", _i32), ("N", _i32), ("channels", _i32), ("image_width", _i32),
+                ("image_height", _i32), ("tile_size", _i32), ("tile_width", _i32),
+                ("tile_height", _i32), ("n_isects", _i64), ("use_backgrounds", _i32),
+                ("use_masks", _i32), ("absgrad", _i32)]
+
+
+_P = ct.POINTER
+
+# (name, restype, argtypes); every exported symbol of include/gsplat_b200.h.
+SIGNATURES = {
+    "gs_status_string": (ct.c_char_p, [ct.c_int]),
+    "gs_last_error": (ct.c_char_p, []),
+    "gs_version": (ct.c_int, []),
+    "gs_floor_log2_plus_one": (_i32, [_i32]),
+    "gs_quat_scale_to_covar_fwd": (ct.c_int, [_P(QS2CParams), _vp, _vp, _vp, _vp, _vp]),
+    "gs_quat_scale_to_covar_bwd": (ct.c_int, [_P(QS2CParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gs_projection_fwd": (ct.c_int, [_P(ProjectionParams)] + [_vp] * 13),
+    "gs_projection_bwd": (ct.c_int, [_P(ProjectionParams)] + [_vp] * 20),
+    "gs_sh_fwd": (ct.c_int, [_P(SHParams), _vp, _vp, _vp, _vp, _vp]),
+    "gs_sh_bwd": (ct.c_int, [_P(SHParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gs_sh_glue_fwd": (ct.c_int, [_P(SHGlueParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gs_sh_glue_bwd": (ct.c_int, [_P(SHGlueParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gs_isect_tile_count": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp]),
+    "gs_isect_scan_workspace_size": (_sz, [_i64]),
+    "gs_isect_scan": (ct.c_int, [_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gs_isect_tile_encode": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "gs_isect_sort_workspace_size": (_sz, [_i64]),
+    "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "gs_rasterize_fwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 12),
+    "gs_rasterize_bwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 19),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ct.CDLL:
+    """Load the native library once and declare every entry point."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"gsplat_b200 native library not found at {path}; build it with "
+            f"`python gsplat-mlx_b200/build.py` (there is no CPU fallback)")
+    lib = ct.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class GsplatError(RuntimeError):
+    """Error status returned by the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+def check(status: int, what: str) -> None:
+    if status != GS_OK:
+        lib = load()
+        msg = lib.gs_last_error().decode(errors="replace")
+        kind = lib.gs_status_string(status).decode()
+        raise GsplatError(status, f"{what}: {msg} [{kind}]" if msg else f"{what} [{kind}]")

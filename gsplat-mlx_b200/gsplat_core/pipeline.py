@@ -1,0 +1,218 @@
+"""Fused training step over the gsplat_core operators.
+
+One ``TrainingStep.run()`` is the forward and backward pass that the
+reference trainers build per batch of cameras (render_sh_model and the
+autograd of sh_loss_fn, scripts/test/scanner_points_training_utils.py:
+1050-1122 and 2076-2119):
+
+  projection fwd -> SH colour glue fwd -> count -> scan -> (host read of the
+  intersection count) -> encode -> radix sort -> tile offsets ->
+  rasterize fwd -> rasterize bwd -> projection bwd -> SH glue bwd
+
+with the cotangents of the rendered colours / alphas given.  Every stage is
+a native kernel of libgsplat_b200.so called through its C ABI on one CUDA
+stream; device buffers come from torch and are allocated once per shape.
+The per-Gaussian gradients land in one flat buffer
+``[v_means | v_quats | v_scales | v_opacities | v_coeffs]`` so that a
+multi-GPU step can all-reduce them in a single collective.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+
+import torch
+
+from . import _lib
+from ._lib import (IsectParams, ProjectionParams, RasterParams, SHGlueParams, check)
+
+
+def _p(t):
+    return None if t is None else ct.c_void_p(t.data_ptr())
+
+
+def _s():
+    return ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+# ------------------------------------------------------------- SH colour glue
+
+def sh_colors(degree, means, viewmats, coeffs, masks=None, radii=None):
+    """colors [C,N,3] = clip(SH(normalize(means - campos_c)) + 0.5, 0, 1)
+    (sh_colors_for_camera, scanner_points_training_utils.py:1011-1034),
+    fused into one kernel.  Entries masked out / culled get 0."""
+    C = viewmats.numel() // 16
+    N = means.shape[0]
+    K = coeffs.shape[-2]
+    out = torch.empty((C, N, 3), dtype=torch.float32, device=means.device)
+    p = SHGlueParams(C, N, K, int(degree), int(masks is not None))
+    check(_lib.load().gs_sh_glue_fwd(ct.byref(p), _p(means), _p(viewmats), _p(coeffs), _p(masks),
+                                     _p(radii), _p(out), _s()), "sh_colors")
+    return out
+
+
+def sh_colors_backward(degree, means, viewmats, coeffs, masks, v_colors, v_means_accum,
+                       radii=None, v_coeffs=None):
+    """Reverse mode of sh_colors as MLX autograd forms it; adds into
+    v_means_accum [N,3] and returns v_coeffs [N,K,3] (summed over cameras)."""
+    C = viewmats.numel() // 16
+    N = means.shape[0]
+    K = coeffs.shape[-2]
+    if v_coeffs is None:
+        v_coeffs = torch.empty_like(coeffs)
+    p = SHGlueParams(C, N, K, int(degree), int(masks is not None))
+    check(_lib.load().gs_sh_glue_bwd(ct.byref(p), _p(means), _p(viewmats), _p(coeffs), _p(masks),
+                                     _p(radii), _p(v_colors), _p(v_means_accum), _p(v_coeffs),
+                                     _s()), "sh_colors_backward")
+    return v_coeffs
+
+
+# ------------------------------------------------------------- training step
+
+class TrainingStep:
+    """Preallocated forward+backward of the 3DGS hot path for one batch of
+    C cameras of one scene (B = 1, I = C images)."""
+
+    def __init__(self, n, sh_degree, K, cameras, width, height, tile_size=16, eps2d=0.3,
+                 near_plane=0.01, far_plane=1e10, device=None, use_background=True):
+        self.dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.N, self.deg, self.K, self.C = int(n), int(sh_degree), int(K), int(cameras)
+        self.W, self.H, self.ts = int(width), int(height), int(tile_size)
+        self.tw = (self.W + self.ts - 1) // self.ts
+        self.th = (self.H + self.ts - 1) // self.ts
+        self.eps2d, self.near, self.far = float(eps2d), float(near_plane), float(far_plane)
+        self.lib = _lib.load()
+        f32, i32 = torch.float32, torch.int32
+        C, N = self.C, self.N
+        e = lambda shape, dt=f32: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
+        # forward state
+        self.means2d, self.depths = e((C, N, 2)), e((C, N))
+        self.conics, self.radii = e((C, N, 3)), e((C, N, 2), i32)
+        self.colors = e((C, N, 3))
+        self.opac_cn = e((C, N)) if C > 1 else None
+        self.tiles_per_gauss, self.g_offsets = e((C, N), i32), e((C, N), i32)
+        self.total = torch.zeros((1,), dtype=torch.int64, device=self.dev)
+        self.total_host = torch.zeros((1,), dtype=torch.int64, pin_memory=True)
+        self.scan_ws = e((max(1, self.lib.gs_isect_scan_workspace_size(C * N)),), torch.uint8)
+        self.tile_offsets = e((C, self.th, self.tw), i32)
+        self.render_colors = e((C, self.H, self.W, 3))
+        self.render_alphas = e((C, self.H, self.W, 1))
+        self.last_ids = e((C, self.H, self.W), i32)
+        self.backgrounds = torch.zeros((C, 3), dtype=f32, device=self.dev) if use_background else None
+        self.v_backgrounds = e((C, 3)) if use_background else None
+        # intersections (grown on demand)
+        self.capacity = 0
+        self.m = 0
+        # backward state
+        self.v_means2d, self.v_conics = e((C, N, 2)), e((C, N, 3))
+        self.v_colors, self.v_opac_cn = e((C, N, 3)), e((C, N))
+        self.v_depths = torch.zeros((C, N), dtype=f32, device=self.dev)
+        sizes = [3 * N, 4 * N, 3 * N, N, self.K * 3 * N]
+        self.grad_flat = e((sum(sizes),))
+        views = torch.split(self.grad_flat, sizes)
+        self.v_means = views[0].view(N, 3)
+        self.v_quats = views[1].view(N, 4)
+        self.v_scales = views[2].view(N, 3)
+        self.v_opacities = views[3].view(N)
+        self.v_coeffs = views[4].view(N, self.K, 3)
+        n_tiles = self.tw * self.th
+        self.key_bits = 32 + self.lib.gs_floor_log2_plus_one(n_tiles) + \
+            self.lib.gs_floor_log2_plus_one(C)
+        self.events = None
+
+    def _ensure_capacity(self, m):
+        if m <= self.capacity:
+            return
+        cap = max(int(m * 1.25) + 1024, 1 << 16)
+        e = lambda shape, dt: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
+        self.isect_ids = e((cap,), torch.int64)
+        self.flatten_ids = e((cap,), torch.int32)
+        self.sorted_ids = e((cap,), torch.int64)
+        self.sorted_flatten = e((cap,), torch.int32)
+        self.sort_ws = e((self.lib.gs_isect_sort_workspace_size(cap),), torch.uint8)
+        self.capacity = cap
+
+    def _mark(self, name):
+        if self.events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.events.append((name, ev))
+
+    def run(self, means, quats, scales, opacities, coeffs, viewmats, Ks, v_render_colors,
+            v_render_alphas):
+        """Forward and backward; returns the flat gradient buffer (a view of
+        self.grad_flat) and the intersection count of this step."""
+        L, s = self.lib, _s()
+        C, N = self.C, self.N
+        self._mark("start")
+        pp = ProjectionParams(1, C, N, self.W, self.H, self.eps2d, self.near, self.far, 0.0, 0, 0,
+                              0, 0)
+        check(L.gs_projection_fwd(ct.byref(pp), _p(means), None, _p(quats), _p(scales), None,
+                                  _p(viewmats), _p(Ks), _p(self.means2d), _p(self.depths),
+                                  _p(self.conics), None, _p(self.radii), s), "projection_fwd")
+        self._mark("projection_fwd")
+        gp = SHGlueParams(C, N, self.K, self.deg, 0)
+        check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
+                               _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
+        self._mark("sh_fwd")
+        ip = IsectParams(C, N, self.ts, self.tw, self.th)
+        check(L.gs_isect_tile_count(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                    _p(self.tiles_per_gauss), s), "isect_count")
+        check(L.gs_isect_scan(C * N, _p(self.tiles_per_gauss), _p(self.g_offsets),
+                              _p(self.total), _p(self.scan_ws), self.scan_ws.numel(), s),
+              "isect_scan")
+        self.total_host.copy_(self.total, non_blocking=True)
+        self._mark("isect_count_scan")
+        torch.cuda.current_stream().synchronize()  # the reference's host read of the total
+        m = int(self.total_host.item())
+        if m >= 2 ** 31:
+            raise RuntimeError(f"{m} intersections exceed the int32 index range")
+        self._ensure_capacity(m)
+        self.m = m
+        check(L.gs_isect_tile_encode(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                     _p(self.depths), _p(self.g_offsets), m, _p(self.isect_ids),
+                                     _p(self.flatten_ids), s), "isect_encode")
+        self._mark("isect_encode")
+        check(L.gs_isect_sort(m, self.key_bits, _p(self.isect_ids), _p(self.flatten_ids),
+                              _p(self.sorted_ids), _p(self.sorted_flatten), _p(self.sort_ws),
+                              self.sort_ws.numel(), s), "isect_sort")
+        self._mark("isect_sort")
+        check(L.gs_isect_offset(m, _p(self.sorted_ids), C, self.tw, self.th,
+                                _p(self.tile_offsets), s), "isect_offset")
+        self._mark("isect_offset")
+        if C > 1:
+            self.opac_cn.copy_(opacities.view(1, N).expand(C, N))
+            opac = self.opac_cn
+        else:
+            opac = opacities
+        rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
+                          int(self.backgrounds is not None), 0, 0)
+        check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(self.colors),
+                                 _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
+                                 _p(self.sorted_flatten), _p(self.render_colors),
+                                 _p(self.render_alphas), _p(self.last_ids), s), "rasterize_fwd")
+        self._mark("rasterize_fwd")
+        v_opac = self.v_opacities if C == 1 else self.v_opac_cn
+        check(L.gs_rasterize_bwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(self.colors),
+                                 _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
+                                 _p(self.sorted_flatten), _p(self.render_alphas),
+                                 _p(self.last_ids), _p(v_render_colors), _p(v_render_alphas),
+                                 None, _p(self.v_means2d), _p(self.v_conics), _p(self.v_colors),
+                                 _p(v_opac), _p(self.v_backgrounds), s), "rasterize_bwd")
+        self._mark("rasterize_bwd")
+        if C > 1:
+            torch.sum(self.v_opac_cn, dim=0, out=self.v_opacities)
+        check(L.gs_projection_bwd(ct.byref(pp), _p(means), None, _p(quats), _p(scales),
+                                  _p(viewmats), _p(Ks), _p(self.radii), _p(self.conics), None,
+                                  _p(self.v_means2d), _p(self.v_depths), _p(self.v_conics), None,
+                                  _p(self.v_means), None, _p(self.v_quats), _p(self.v_scales),
+                                  None, s), "projection_bwd")
+        self._mark("projection_bwd")
+        check(L.gs_sh_glue_bwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
+                               _p(self.radii), _p(self.v_colors), _p(self.v_means),
+                               _p(self.v_coeffs), s), "sh_glue_bwd")
+        self._mark("sh_bwd")
+        return self.grad_flat, m
+
+    def gradients(self):
+        return {"v_means": self.v_means, "v_quats": self.v_quats, "v_scales": self.v_scales,
+                "v_opacities": self.v_opacities, "v_coeffs": self.v_coeffs}

@@ -1,0 +1,248 @@
+/*
+ * gsplat_b200 -- C ABI of the B200 (sm_100a) implementation of gsplat-mlx's
+ * five differentiable 3D Gaussian Splatting operators.
+ *
+ * Every entry point:
+ *   - takes raw DEVICE pointers (float32 / int32 / int64 / uint8-as-bool,
+ *     dense row-major, the reference's layouts), a pointer to a POD
+ *     parameter struct and a CUDA stream (cudaStream_t passed as void*);
+ *   - enqueues its kernels on that stream and returns without waiting;
+ *   - writes every element of every output it is given (the reference
+ *     zero-fills its outputs before eval, e.g. gsplat_rasterize.cpp:575-578;
+ *     here culled / masked entries are written as exact zeros on device);
+ *   - never allocates device memory: scratch is passed in by the caller as a
+ *     workspace whose size the matching *_workspace_size() function returns;
+ *   - returns GS_OK or an error status; gs_last_error() then holds a message
+ *     (thread-local).  Invalid shapes / sizes are rejected before any launch,
+ *     as the reference's front-ends throw std::runtime_error
+ *     (e.g. gsplat_projection.cpp:115-141).
+ *
+ * Each function names the reference interface it replaces (file:line inside
+ * the gsplat-mlx repository).  In the reference, the Metal dispatch blocks of
+ * the Primitive::eval_gpu methods are the call sites these entries replace.
+ */
+#ifndef GSPLAT_B200_H
+#define GSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* gs_stream_t; /* a cudaStream_t; NULL is the legacy stream */
+
+enum gs_status {
+  GS_OK = 0,
+  GS_ERR_INVALID = 1,     /* bad shape / argument (reference: runtime_error) */
+  GS_ERR_UNSUPPORTED = 2, /* path the reference also rejects (packed, ...)   */
+  GS_ERR_OVERFLOW = 3,    /* int32 index limits of the operator surface      */
+  GS_ERR_CUDA = 4,        /* a CUDA launch / runtime error                   */
+  GS_ERR_WORKSPACE = 5,   /* workspace pointer missing or too small          */
+  GS_ERR_DEVICE = 6       /* a kernel reported a failed on-device check      */
+};
+
+const char* gs_status_string(int status);
+const char* gs_last_error(void);
+int gs_version(void); /* major*10000 + minor*100 + patch */
+
+/* ------------------------------------------------------------------ */
+/* quat/scale -> covariance / precision                                */
+/* Replaces GSPlatQuatScaleToCovarPreci{,Backward}::eval_gpu,          */
+/* gsplat_quat_scale_to_covar.cpp:471-558; params mirror               */
+/* QuatScaleToCovarPreciKernelParams, :27-32.                          */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int64_t n;             /* number of (quat, scale) pairs                */
+  int32_t compute_covar; /* fwd: write covars; bwd: v_covars is given    */
+  int32_t compute_preci; /* fwd: write precis; bwd: v_precis is given    */
+  int32_t triu;          /* 1: [n,6] upper triangle; 0: [n,3,3]          */
+} gs_qs2c_params;
+
+int gs_quat_scale_to_covar_fwd(const gs_qs2c_params* p, const float* quats,
+                               const float* scales, float* covars,
+                               float* precis, gs_stream_t stream);
+int gs_quat_scale_to_covar_bwd(const gs_qs2c_params* p, const float* quats,
+                               const float* scales, const float* v_covars,
+                               const float* v_precis, float* v_quats,
+                               float* v_scales, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* fully fused EWA projection                                          */
+/* Replaces GSPlatProjectionEWA3DGSFused{,Backward}::eval_gpu,         */
+/* gsplat_projection.cpp:655-855; params mirror ProjectionKernelParams */
+/* (:26-40) and ProjectionEWA3DGSFusedParams (gsplat_projection.h:12). */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int32_t B, C, N;
+  int32_t image_width, image_height;
+  float eps2d, near_plane, far_plane, radius_clip;
+  int32_t calc_compensations;
+  int32_t camera_model; /* 0 pinhole, 1 orthographic, 2 fisheye (fwd only) */
+  int32_t use_covars;   /* 1: covars [B,N,6]; 0: quats [B,N,4] + scales    */
+  int32_t use_opacities;
+} gs_projection_params;
+
+/* Outputs: means2d [B,C,N,2], depths [B,C,N], conics [B,C,N,3],
+ * compensations [B,C,N] (only when calc_compensations), radii [B,C,N,2]. */
+int gs_projection_fwd(const gs_projection_params* p, const float* means,
+                      const float* covars, const float* quats,
+                      const float* scales, const float* opacities,
+                      const float* viewmats, const float* Ks, float* means2d,
+                      float* depths, float* conics, float* compensations,
+                      int32_t* radii, gs_stream_t stream);
+/* v_viewmats may be NULL (reference: viewmats_requires_grad == false).
+ * v_compensations may be NULL; it is read only when calc_compensations. */
+int gs_projection_bwd(const gs_projection_params* p, const float* means,
+                      const float* covars, const float* quats,
+                      const float* scales, const float* viewmats,
+                      const float* Ks, const int32_t* radii,
+                      const float* conics, const float* compensations,
+                      const float* v_means2d, const float* v_depths,
+                      const float* v_conics, const float* v_compensations,
+                      float* v_means, float* v_covars, float* v_quats,
+                      float* v_scales, float* v_viewmats, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* spherical harmonics, degree 0..4                                    */
+/* Replaces GSPlatSphericalHarmonics{,Backward}::eval_gpu,             */
+/* gsplat_spherical_harmonics.cpp:557-646; params mirror               */
+/* SphericalHarmonicsKernelParams, :26-31.                             */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int64_t n;              /* prod(dirs.shape[:-1])                        */
+  int32_t K;              /* coeffs.shape[-2] (>= (degree+1)^2)           */
+  int32_t degrees_to_use; /* 0..4                                         */
+  int32_t use_masks;      /* masks [n] uint8 given                        */
+} gs_sh_params;
+
+int gs_sh_fwd(const gs_sh_params* p, const float* dirs, const float* coeffs,
+              const uint8_t* masks, float* colors, gs_stream_t stream);
+/* v_dirs may be NULL (reference: compute_v_dirs == false). */
+int gs_sh_bwd(const gs_sh_params* p, const float* dirs, const float* coeffs,
+              const uint8_t* masks, const float* v_colors, float* v_dirs,
+              float* v_coeffs, gs_stream_t stream);
+
+/* Fused SH colour glue of the reference trainers
+ * (scripts/test/scanner_points_training_utils.py:1005-1034):
+ *   colors[c,n] = clip(SH(normalize(means[n] - campos_c), coeffs[n]) + 0.5, 0, 1)
+ * with campos_c = -R_c^T t_c.  Entries can be skipped: by masks [C,N]
+ * (uint8, optional) and/or by radii [C,N,2] (int32, optional; an entry is
+ * visible when both radii are > 0, the projection's culling result).  A
+ * skipped entry gets colour 0 and no gradient -- the rasterizer never reads
+ * the colour of a culled Gaussian, so the rendered image and every gradient
+ * are unchanged.  The backward adds the reverse mode of the composition
+ * (clip masks, SH, normalisation) into v_means [N,3] and writes v_coeffs
+ * [N,K,3] summed over the C cameras.  */
+typedef struct {
+  int32_t C, N, K, degrees_to_use;
+  int32_t use_masks;
+} gs_sh_glue_params;
+
+int gs_sh_glue_fwd(const gs_sh_glue_params* p, const float* means,
+                   const float* viewmats, const float* coeffs,
+                   const uint8_t* masks, const int32_t* radii, float* colors,
+                   gs_stream_t stream);
+int gs_sh_glue_bwd(const gs_sh_glue_params* p, const float* means,
+                   const float* viewmats, const float* coeffs,
+                   const uint8_t* masks, const int32_t* radii,
+                   const float* v_colors, float* v_means_accum,
+                   float* v_coeffs, gs_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* tile intersection                                                   */
+/* Replaces GSPlatIntersectTileCount / GSPlatIntersectTileEncode /     */
+/* GSPlatIntersectOffset ::eval_gpu (gsplat_intersect.cpp:342-382,     */
+/* :488-539, :644-681), MLX cumsum in gsplat_intersect_tile_offsets    */
+/* (:196-211) and MLX argsort+take in gsplat_intersect_tile_sort       */
+/* (:266-286).  Params mirror IntersectTileCountKernelParams /         */
+/* IntersectTileEncodeKernelParams (:29-51).                           */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int32_t I;          /* images (B*C)                                    */
+  int32_t N;          /* Gaussians per image                             */
+  int32_t tile_size, tile_width, tile_height;
+} gs_isect_params;
+
+/* tiles_per_gauss [I,N] int32 */
+int gs_isect_tile_count(const gs_isect_params* p, const float* means2d,
+                        const int32_t* radii, int32_t* tiles_per_gauss,
+                        gs_stream_t stream);
+
+/* Exclusive prefix sum of n int32 counts into offsets (int32, as the
+ * reference's cumsum), and the 64-bit total into *total_device (a device
+ * int64).  Totals of 2^31 or more are an overflow of the reference's int32
+ * offsets; the caller checks *total_device. */
+size_t gs_isect_scan_workspace_size(int64_t n);
+int gs_isect_scan(int64_t n, const int32_t* counts, int32_t* offsets,
+                  int64_t* total_device, void* workspace,
+                  size_t workspace_bytes, gs_stream_t stream);
+
+/* isect_ids [n_isects] int64 (image|tile|depth bits), flatten_ids int32 */
+int gs_isect_tile_encode(const gs_isect_params* p, const float* means2d,
+                         const int32_t* radii, const float* depths,
+                         const int32_t* offsets, int64_t n_isects,
+                         int64_t* isect_ids, int32_t* flatten_ids,
+                         gs_stream_t stream);
+
+/* Stable ascending sort of (isect_ids, flatten_ids) by the signed 64-bit
+ * key, equal keys kept in input order -- the result of MLX's argsort+take.
+ * key_bits = 32 + tile_bits + image_bits is the number of low key bits
+ * that can be non-zero (the rest must be zero); 1..64.  */
+size_t gs_isect_sort_workspace_size(int64_t n_isects);
+int gs_isect_sort(int64_t n_isects, int32_t key_bits, const int64_t* isect_ids,
+                  const int32_t* flatten_ids, int64_t* sorted_isect_ids,
+                  int32_t* sorted_flatten_ids, void* workspace,
+                  size_t workspace_bytes, gs_stream_t stream);
+
+/* tile_offsets [I, tile_height, tile_width] int32 from sorted isect_ids:
+ * lower bound of (image << tile_bits | tile) in isect_ids >> 32. */
+int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,
+                    int32_t tile_width, int32_t tile_height,
+                    int32_t* tile_offsets, gs_stream_t stream);
+
+/* Helper of the staged pipeline: tile_bits = floor(log2(n)) + 1, the
+ * reference's floor_log2_plus_one (gsplat_intersect.cpp:60-65). */
+int32_t gs_floor_log2_plus_one(int32_t value);
+
+/* ------------------------------------------------------------------ */
+/* rasterize to pixels (3DGS)                                          */
+/* Replaces GSPlatRasterizeToPixels3DGS{,Backward}::eval_gpu,          */
+/* gsplat_rasterize.cpp:572-724; params mirror                         */
+/* RasterizeToPixels3DGSKernelParams, :28-40.                          */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int32_t I, N, channels;
+  int32_t image_width, image_height;
+  int32_t tile_size, tile_width, tile_height;
+  int64_t n_isects;
+  int32_t use_backgrounds, use_masks;
+  int32_t absgrad; /* bwd: write v_means2d_abs */
+} gs_raster_params;
+
+/* render_colors [I,H,W,ch], render_alphas [I,H,W,1], last_ids [I,H,W] */
+int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,
+                     const float* conics, const float* colors,
+                     const float* opacities, const float* backgrounds,
+                     const uint8_t* masks, const int32_t* tile_offsets,
+                     const int32_t* flatten_ids, float* render_colors,
+                     float* render_alphas, int32_t* last_ids,
+                     gs_stream_t stream);
+/* Gradient outputs are zeroed on the stream, then accumulated. */
+int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
+                     const float* conics, const float* colors,
+                     const float* opacities, const float* backgrounds,
+                     const uint8_t* masks, const int32_t* tile_offsets,
+                     const int32_t* flatten_ids, const float* render_alphas,
+                     const int32_t* last_ids, const float* v_render_colors,
+                     const float* v_render_alphas, float* v_means2d_abs,
+                     float* v_means2d, float* v_conics, float* v_colors,
+                     float* v_opacities, float* v_backgrounds,
+                     gs_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSPLAT_B200_H */

@@ -1,0 +1,449 @@
+"""GPU parity of every operator against the CPU oracle and the golden
+fixtures (the reference's own outputs).  Integer results (radii, tile
+counts, keys, sort order, offsets) must be bit-exact; float forward values
+within 1e-5 abs / 1e-4 rel; gradients within 1e-3 rel.
+
+Rasterization decides per pixel x Gaussian whether alpha clears 1/255 and
+whether T(1-alpha) drops to 1e-4; a GPU exp() and the C library's exp()
+may round differently right at those thresholds.  The oracle flags pixels
+whose decision lies within rounding of a threshold (near_threshold); those
+pixels are excluded from forward comparisons and get zero cotangents in
+backward comparisons, and the test asserts they are rare.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from _util import assert_exact, assert_fwd_close, assert_grad_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def T(x, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+# ---------------------------------------------------------------- quat/scale
+
+@pytest.mark.parametrize("triu", [True, False])
+@pytest.mark.parametrize("covar,preci", [(True, True), (True, False), (False, True)])
+def test_quat_scale_fwd_bwd(gs, oracle, cuda, triu, covar, preci):
+    rng = np.random.default_rng(3)
+    n = 10_007
+    q = rng.normal(size=(n, 4)).astype(np.float32)
+    s = np.exp(rng.uniform(-3, 1, size=(n, 3))).astype(np.float32)
+    f = gs.quat_scale_to_covar_preci_forward({"quats": T(q), "scales": T(s)}, covar, preci, triu)
+    e = oracle.qs2c_fwd(q, s, covar, preci, triu)
+    for k in ("covars", "precis"):
+        assert tuple(f[k].shape) == e[k].shape
+        assert_fwd_close(f[k], e[k], k, atol=1e-5 * max(1.0, np.abs(e[k]).max()))
+    shape = (n, 6) if triu else (n, 3, 3)
+    vc = rng.normal(size=shape).astype(np.float32) if covar else None
+    vp = rng.normal(size=shape).astype(np.float32) if preci else None
+    cot = {}
+    if covar:
+        cot["v_covars"] = T(vc)
+    if preci:
+        cot["v_precis"] = T(vp)
+    b = gs.quat_scale_to_covar_preci_backward({"quats": T(q), "scales": T(s)}, cot, triu)
+    eb = oracle.qs2c_bwd(q, s, vc, vp, triu)
+    assert_grad_close(b["v_quats"], eb["v_quats"], "v_quats")
+    assert_grad_close(b["v_scales"], eb["v_scales"], "v_scales")
+
+
+def test_quat_scale_golden_and_zero_cotangents(gs, golden, cuda):
+    d = golden("ops")
+    q, s = T(d["qs_quats"]), T(d["qs_scales"])
+    for triu in (0, 1):
+        f = gs.quat_scale_to_covar_preci_forward({"quats": q, "scales": s}, True, True, bool(triu))
+        assert_fwd_close(f["covars"], d[f"qs_triu{triu}_covars"], "covars golden", atol=1e-4)
+        assert_fwd_close(f["precis"], d[f"qs_triu{triu}_precis"], "precis golden", atol=1e-4)
+        b = gs.quat_scale_to_covar_preci_backward(
+            {"quats": q, "scales": s},
+            {"v_covars": T(d[f"qs_triu{triu}_vc"]), "v_precis": T(d[f"qs_triu{triu}_vp"])},
+            bool(triu))
+        assert_grad_close(b["v_quats"], d[f"qs_triu{triu}_v_quats"], "v_quats golden")
+        assert_grad_close(b["v_scales"], d[f"qs_triu{triu}_v_scales"], "v_scales golden")
+    z = gs.quat_scale_to_covar_preci_backward({"quats": q, "scales": s}, {}, True)
+    assert float(z["v_quats"].abs().max()) == 0.0 and float(z["v_scales"].abs().max()) == 0.0
+    e = gs.quat_scale_to_covar_preci_forward({"quats": q[:0], "scales": s[:0]})
+    assert tuple(e["covars"].shape) == (0, 6)
+
+
+# ---------------------------------------------------------------- projection
+
+def _scene_subset(cfg, n, seed=0):
+    from gsplat_core import synthetic as S
+    sc = getattr(S, cfg)(seed=seed) if cfg != "config3" else S.config3(seed=seed, n=max(n, 10))
+    rng = np.random.default_rng(seed + 1)
+    idx = np.sort(rng.choice(sc.n, size=min(n, sc.n), replace=False))
+    return sc, idx
+
+
+@pytest.mark.parametrize("cfg,n,use_opac,comp", [
+    ("config1", 10_000, False, False), ("config1", 10_000, True, True),
+    ("config3", 200_000, False, False), ("config3", 200_000, True, False),
+])
+def test_projection_fwd_exact(gs, oracle, cuda, cfg, n, use_opac, comp):
+    sc, idx = _scene_subset(cfg, n)
+    means, quats, scales = sc.means[idx][None], sc.quats[idx][None], sc.scales[idx][None]
+    opac = sc.opacities[idx][None] if use_opac else None
+    W, H = sc.width, sc.height
+    inputs = {"means": T(means), "quats": T(quats), "scales": T(scales),
+              "viewmats": T(sc.viewmats[None]), "Ks": T(sc.Ks[None])}
+    if use_opac:
+        inputs["opacities"] = T(opac)
+    g = gs.projection_ewa_3dgs_fused_forward(inputs, W, H, calc_compensations=comp)
+    e = oracle.proj_fwd(means, sc.viewmats[None], sc.Ks[None], W, H, quats=quats, scales=scales,
+                        opacities=opac, calc_compensations=comp)
+    # Compiled without FMA contraction in the reference's operation order:
+    # everything but the log() of the opacity-aware extent is bit-identical.
+    if use_opac:
+        rg, re = to_np(g["radii"]), e["radii"]
+        diff = (rg != re).any(-1)
+        assert diff.mean() < 1e-4, f"radii differ on {diff.sum()} entries"
+        ok = ~diff
+        assert_exact(rg[ok], re[ok], "radii")
+    else:
+        assert_exact(g["radii"], e["radii"], "radii")
+        assert_exact(g["means2d"], e["means2d"], "means2d")
+        assert_exact(g["depths"], e["depths"], "depths")
+        assert_exact(g["conics"], e["conics"], "conics")
+    assert_fwd_close(g["means2d"], e["means2d"], "means2d")
+    assert_fwd_close(g["depths"], e["depths"], "depths")
+    assert_fwd_close(g["conics"], e["conics"], "conics", atol=1e-5 * max(1, np.abs(e["conics"]).max()))
+    if comp:
+        assert_fwd_close(g["compensations"], e["compensations"], "compensations")
+    else:
+        assert tuple(g["compensations"].shape) == (0,)
+
+
+def test_projection_golden_and_covars(gs, golden, cuda):
+    d = golden("ops")
+    W, H = int(d["pc_width"]), int(d["pc_height"])
+    inputs = {"means": T(d["pc_means"]), "covars": T(d["pc_covars"]),
+              "viewmats": T(d["pc_viewmats"]), "Ks": T(d["pc_Ks"])}
+    g = gs.projection_ewa_3dgs_fused_forward(inputs, W, H, near_plane=2.4, far_plane=3.9)
+    for k in ("radii", "means2d", "depths", "conics"):
+        assert_exact(g[k], d["pc_" + k], "golden proj " + k)
+    b = gs.projection_ewa_3dgs_fused_backward(
+        inputs, {"radii": g["radii"], "conics": g["conics"]},
+        {"v_means2d": T(d["pc_vm2"]), "v_depths": T(d["pc_vd"]), "v_conics": T(d["pc_vco"])},
+        W, H, viewmats_requires_grad=True)
+    for k in ("v_means", "v_covars", "v_viewmats"):
+        assert_grad_close(b[k], d["pcb_" + k], "golden proj bwd " + k)
+
+
+@pytest.mark.parametrize("cfg,n,comp,vm", [("config1", 10_000, True, True),
+                                           ("config3", 100_000, False, True),
+                                           ("config3", 100_000, True, False)])
+def test_projection_bwd(gs, oracle, cuda, cfg, n, comp, vm):
+    sc, idx = _scene_subset(cfg, n)
+    means, quats, scales = sc.means[idx][None], sc.quats[idx][None], sc.scales[idx][None]
+    W, H = sc.width, sc.height
+    e = oracle.proj_fwd(means, sc.viewmats[None], sc.Ks[None], W, H, quats=quats, scales=scales,
+                        calc_compensations=comp)
+    rng = np.random.default_rng(9)
+    vm2 = rng.normal(size=e["means2d"].shape).astype(np.float32)
+    vd = rng.normal(size=e["depths"].shape).astype(np.float32)
+    vco = rng.normal(size=e["conics"].shape).astype(np.float32) * 1e-3
+    vcp = rng.normal(size=e["depths"].shape).astype(np.float32) if comp else None
+    fo = {"radii": T(e["radii"]), "conics": T(e["conics"])}
+    cot = {"v_means2d": T(vm2), "v_depths": T(vd), "v_conics": T(vco)}
+    if comp:
+        fo["compensations"] = T(e["compensations"])
+        cot["v_compensations"] = T(vcp)
+    b = gs.projection_ewa_3dgs_fused_backward(
+        {"means": T(means), "quats": T(quats), "scales": T(scales),
+         "viewmats": T(sc.viewmats[None]), "Ks": T(sc.Ks[None])}, fo, cot, W, H,
+        viewmats_requires_grad=vm)
+    eb = oracle.proj_bwd(means, sc.viewmats[None], sc.Ks[None], W, H, e["radii"], e["conics"],
+                         vm2, vd, vco, quats=quats, scales=scales,
+                         compensations=e["compensations"] if comp else None,
+                         v_compensations=vcp, viewmats_requires_grad=vm)
+    for k, v in eb.items():
+        assert_grad_close(b[k], v, "proj bwd " + k, atol_frac=1e-4 if k == "v_viewmats" else 1e-5)
+    if not vm:
+        assert "v_viewmats" not in b
+
+
+@pytest.mark.parametrize("model", [1, 2])
+def test_projection_other_camera_models(gs, oracle, cuda, model):
+    """Orthographic / fisheye forward follow metal/gsplat_projection.metal:
+    156-201 (the reference CPU path has no counterpart: unpinned)."""
+    sc, idx = _scene_subset("config1", 5000)
+    means, quats, scales = sc.means[idx][None], sc.quats[idx][None], sc.scales[idx][None]
+    K = sc.Ks.copy()
+    if model == 1:
+        K[:, 0, 0] = K[:, 1, 1] = 60.0
+    g = gs.projection_ewa_3dgs_fused_forward(
+        {"means": T(means), "quats": T(quats), "scales": T(scales),
+         "viewmats": T(sc.viewmats[None]), "Ks": T(K[None])}, sc.width, sc.height,
+        camera_model=model)
+    e = oracle.proj_fwd(means, sc.viewmats[None], K[None], sc.width, sc.height, quats=quats,
+                        scales=scales, camera_model=model)
+    diff = (to_np(g["radii"]) != e["radii"]).any(-1)
+    assert diff.mean() < 1e-3
+    ok = ~diff
+    assert (e["radii"][..., 0] > 0).sum() > 100
+    assert_fwd_close(to_np(g["means2d"])[ok], e["means2d"][ok], "means2d", atol=1e-3)
+    assert_fwd_close(to_np(g["conics"])[ok], e["conics"][ok], "conics",
+                     atol=1e-4 * max(1, np.abs(e["conics"]).max()), rtol=1e-3)
+
+
+def test_projection_errors(gs, cuda):
+    m = torch.zeros((1, 4, 3), device=cuda)
+    v = torch.eye(4, device=cuda)[None, None]
+    K = torch.eye(3, device=cuda)[None, None]
+    with pytest.raises(RuntimeError, match="covars or quats"):
+        gs.projection_ewa_3dgs_fused_forward({"means": m, "viewmats": v, "Ks": K}, 8, 8)
+    with pytest.raises(RuntimeError, match="pinhole only"):
+        gs.projection_ewa_3dgs_fused_backward(
+            {"means": m, "viewmats": v, "Ks": K, "covars": torch.zeros((1, 4, 6), device=cuda)},
+            {"radii": torch.zeros((1, 1, 4, 2), dtype=torch.int32, device=cuda),
+             "conics": torch.zeros((1, 1, 4, 3), device=cuda)},
+            {"v_means2d": torch.zeros((1, 1, 4, 2), device=cuda),
+             "v_depths": torch.zeros((1, 1, 4), device=cuda),
+             "v_conics": torch.zeros((1, 1, 4, 3), device=cuda)}, 8, 8, camera_model=1)
+
+
+# ---------------------------------------------------------------- SH
+
+@pytest.mark.parametrize("deg", [0, 1, 2, 3, 4])
+def test_sh_golden(gs, golden, cuda, deg):
+    d = golden("ops")
+    inputs = {"dirs": T(d["sh_dirs"]), "coeffs": T(d["sh_coeffs"]), "masks": T(d["sh_masks"])}
+    c = gs.spherical_harmonics_forward(deg, inputs)
+    assert_fwd_close(c, d[f"sh_deg{deg}_colors"], f"sh fwd deg{deg}")
+    b = gs.spherical_harmonics_backward(deg, inputs, {"v_colors": T(d["sh_vcol"])})
+    assert_grad_close(b["v_coeffs"], d[f"sh_deg{deg}_v_coeffs"], f"sh v_coeffs deg{deg}")
+    assert_grad_close(b["v_dirs"], d[f"sh_deg{deg}_v_dirs"], f"sh v_dirs deg{deg}")
+
+
+@pytest.mark.parametrize("deg,K", [(3, 16), (2, 16), (1, 4), (4, 25)])
+def test_sh_large(gs, oracle, cuda, deg, K):
+    rng = np.random.default_rng(deg)
+    n = 200_003
+    dirs = rng.normal(size=(n, 3)).astype(np.float32)
+    co = rng.normal(0, 0.3, size=(n, K, 3)).astype(np.float32)
+    vc = rng.normal(size=(n, 3)).astype(np.float32)
+    c = gs.spherical_harmonics_forward(deg, {"dirs": T(dirs), "coeffs": T(co)})
+    assert_fwd_close(c, oracle.sh_fwd(deg, dirs, co), "sh fwd")
+    b = gs.spherical_harmonics_backward(deg, {"dirs": T(dirs), "coeffs": T(co)}, {"v_colors": T(vc)},
+                                        compute_v_dirs=False)
+    eb = oracle.sh_bwd(deg, dirs, co, vc, compute_v_dirs=False)
+    assert "v_dirs" not in b
+    assert_grad_close(b["v_coeffs"], eb["v_coeffs"], "sh v_coeffs")
+
+
+def test_sh_glue(gs, oracle, cuda):
+    """Fused colour glue (scanner_points_training_utils.py:1005-1034) against
+    the composition restated in the oracle, with and without masks."""
+    from gsplat_core import pipeline
+    sc, idx = _scene_subset("config3", 50_000)
+    means, coeffs = sc.means[idx], sc.coeffs[idx]
+    views = np.concatenate([sc.viewmats, sc.viewmats @ np.diag([1, 1, 1, 1]).astype(np.float32)])
+    views[1, :3, 3] += np.array([0.3, -0.2, 0.5], np.float32)
+    rng = np.random.default_rng(2)
+    masks = rng.uniform(size=(2, means.shape[0])) > 0.3
+    for m in (None, masks):
+        col = pipeline.sh_colors(3, T(means), T(views), T(coeffs), None if m is None else T(m))
+        e = oracle.sh_glue_fwd(3, means, views, coeffs, m)
+        assert_fwd_close(col, e, "glue fwd")
+        vout = rng.normal(size=e.shape).astype(np.float32)
+        vm0 = rng.normal(size=means.shape).astype(np.float32)
+        v_means = T(vm0.copy())
+        vco = pipeline.sh_colors_backward(3, T(means), T(views), T(coeffs),
+                                          None if m is None else T(m), T(vout), v_means)
+        eb = oracle.sh_glue_bwd(3, means, views, coeffs, vout, m)
+        assert_grad_close(vco, eb["v_coeffs"], "glue v_coeffs")
+        assert_grad_close(to_np(v_means) - vm0, eb["v_means"], "glue v_means", atol_frac=1e-4)
+
+
+# ---------------------------------------------------------------- intersect
+
+def _isect_inputs(oracle, cfg, n, seed=0):
+    sc, idx = _scene_subset(cfg, n, seed)
+    e = oracle.proj_fwd(sc.means[idx][None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
+                        quats=sc.quats[idx][None], scales=sc.scales[idx][None])
+    return sc, e["means2d"].reshape(1, -1, 2), e["radii"].reshape(1, -1, 2), e["depths"].reshape(1, -1)
+
+
+@pytest.mark.parametrize("cfg,n", [("config1", 10_000), ("config3", 300_000)])
+@pytest.mark.parametrize("sort", [True, False])
+def test_intersect_exact(gs, oracle, cuda, cfg, n, sort):
+    sc, m2, rad, dep = _isect_inputs(oracle, cfg, n)
+    tw, th = sc.tile_width, sc.tile_height
+    g = gs.intersect_tile_forward({"means2d": T(m2), "radii": T(rad), "depths": T(dep)}, 1,
+                                  sc.tile_size, tw, th, sort=sort)
+    e = oracle.isect_tile(m2, rad, dep, 1, sc.tile_size, tw, th, sort=sort)
+    for k in ("tiles_per_gauss", "isect_ids", "flatten_ids"):
+        assert_exact(g[k], e[k], k)
+    if sort:
+        o = gs.intersect_offset_forward(g["isect_ids"], 1, tw, th)
+        assert_exact(o, oracle.isect_offset(e["isect_ids"], 1, tw, th), "offsets")
+
+
+def test_intersect_golden(gs, golden, cuda):
+    for name in ("chain_cfg1", "chain_cfg3"):
+        d = golden(name)
+        W, H, ts = int(d["width"]), int(d["height"]), int(d["tile_size"])
+        tw, th = (W + ts - 1) // ts, (H + ts - 1) // ts
+        inp = {"means2d": T(d["proj_means2d"].reshape(1, -1, 2)),
+               "radii": T(d["proj_radii"].reshape(1, -1, 2)),
+               "depths": T(d["proj_depths"].reshape(1, -1))}
+        g = gs.intersect_tile_forward(inp, 1, ts, tw, th, sort=True)
+        for k in ("tiles_per_gauss", "isect_ids", "flatten_ids"):
+            assert_exact(g[k].reshape(-1), d["isect_" + k].reshape(-1), f"{name} {k}")
+        u = gs.intersect_tile_forward(inp, 1, ts, tw, th, sort=False)
+        assert_exact(u["isect_ids"], d["isect_unsorted_isect_ids"], f"{name} unsorted")
+        o = gs.intersect_offset_forward(g["isect_ids"], 1, tw, th)
+        assert_exact(o, d["tile_offsets"], f"{name} offsets")
+
+
+def test_intersect_known_answers(gs, cuda):
+    """gsplat_core/test/test.cpp:653-1065 through the GPU path."""
+    m2 = T(np.array([[[50, 50], [20, 20], [8, 8]]], np.float32))
+    rad = T(np.array([[[5, 5], [10, 10], [0, 0]]], np.int32))
+    dep = T(np.array([[0.5, 1.0, 2.0]], np.float32))
+    r = gs.intersect_tile_forward({"means2d": m2, "radii": rad, "depths": dep}, 1, 16, 4, 4)
+    assert to_np(r["tiles_per_gauss"]).tolist() == [[4, 4, 0]]
+    assert to_np(r["isect_ids"]).tolist() == [(t << 32) | 0x3F800000 for t in (0, 1, 4, 5)] + \
+        [(t << 32) | 0x3F000000 for t in (10, 11, 14, 15)]
+    assert to_np(r["flatten_ids"]).tolist() == [1, 1, 1, 1, 0, 0, 0, 0]
+    o = gs.intersect_offset_forward(r["isect_ids"], 1, 4, 4)
+    assert to_np(o).ravel().tolist() == [0, 1, 2, 2, 2, 3, 4, 4, 4, 4, 4, 5, 6, 6, 6, 7]
+
+
+def test_intersect_multi_image_and_empty(gs, oracle, cuda):
+    rng = np.random.default_rng(4)
+    I, N = 3, 5000
+    m2 = rng.uniform(-20, 280, size=(I, N, 2)).astype(np.float32)
+    rad = rng.integers(-1, 30, size=(I, N, 2)).astype(np.int32)
+    dep = rng.uniform(0.1, 50, size=(I, N)).astype(np.float32)
+    dep[0, :100] = dep[0, 100]  # ties: stability decides the order
+    g = gs.intersect_tile_forward({"means2d": T(m2), "radii": T(rad), "depths": T(dep)}, I, 8, 32, 32)
+    e = oracle.isect_tile(m2, rad, dep, I, 8, 32, 32)
+    for k in ("tiles_per_gauss", "isect_ids", "flatten_ids"):
+        assert_exact(g[k], e[k], k)
+    assert_exact(gs.intersect_offset_forward(g["isect_ids"], I, 32, 32),
+                 oracle.isect_offset(e["isect_ids"], I, 32, 32), "offsets")
+    z = gs.intersect_tile_forward({"means2d": T(m2), "radii": T(np.zeros_like(rad)),
+                                   "depths": T(dep)}, I, 8, 32, 32)
+    assert z["isect_ids"].numel() == 0 and z["flatten_ids"].numel() == 0
+    oz = gs.intersect_offset_forward(z["isect_ids"], I, 32, 32)
+    assert int(oz.abs().max()) == 0
+
+
+@pytest.mark.parametrize("n", [1, 31, 4095, 4096, 4097, 100_000, 1_000_003])
+@pytest.mark.parametrize("bits", [40, 46, 64])
+def test_sort_stable_exact(gs, oracle, cuda, n, bits):
+    """The radix sort against a stable merge sort: random keys with many
+    duplicates (stability), tile boundaries, and the 64-bit signed order."""
+    rng = np.random.default_rng(n + bits)
+    hi_bits = bits - 32
+    keys = (rng.integers(0, 1 << min(hi_bits, 20), size=n).astype(np.int64) << 32) | \
+        rng.integers(0, 64, size=n).astype(np.int64)
+    if bits == 64:
+        sign = rng.uniform(size=n) < 0.5
+        keys = keys | (rng.integers(0, 1 << 30, size=n).astype(np.int64) << 33)
+        keys[sign] = -keys[sign]
+    vals = np.arange(n, dtype=np.int32)
+    gk, gv = gs.intersect_tile_sort(T(keys), T(vals), bits)
+    ek, ev = oracle.isect_sort(keys, vals)
+    assert_exact(gk, ek, "keys")
+    assert_exact(gv, ev, "values (stability)")
+
+
+# ---------------------------------------------------------------- rasterize
+
+def _raster_case(oracle, name, d, channels=3):
+    W, H, ts = int(d["width"]), int(d["height"]), int(d["tile_size"])
+    colors = d["colors"]
+    if channels != 3:
+        rng = np.random.default_rng(channels)
+        colors = rng.uniform(0, 1, size=colors.shape[:-1] + (channels,)).astype(np.float32)
+    bg = np.linspace(0.1, 0.3, channels, dtype=np.float32)[None]
+    inp = dict(means2d=d["proj_means2d"].reshape(1, -1, 2), conics=d["proj_conics"].reshape(1, -1, 3),
+               colors=colors, opacities=d["opacities"][None], tile_offsets=d["tile_offsets"],
+               flatten_ids=d["isect_flatten_ids"], backgrounds=bg)
+    return W, H, ts, inp
+
+
+@pytest.mark.parametrize("name", ["chain_cfg1", "chain_cfg3"])
+@pytest.mark.parametrize("channels", [3, 1, 4, 5])
+def test_rasterize_fwd_bwd(gs, oracle, golden, cuda, name, channels):
+    d = golden(name)
+    W, H, ts, inp = _raster_case(oracle, name, d, channels)
+    e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
+    g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, W, H, ts)
+    near = e["near_threshold"]
+    assert near.mean() < 0.01, f"{near.sum()} near-threshold pixels"
+    ok = ~near
+    assert_exact(to_np(g["last_ids"])[ok], e["last_ids"][ok], "last_ids")
+    assert_fwd_close(to_np(g["render_alphas"])[..., 0][ok], e["render_alphas"][..., 0][ok], "alphas")
+    assert_fwd_close(to_np(g["render_colors"])[ok], e["render_colors"][ok], "colors")
+    if channels == 3:
+        gold_ok = ~near
+        assert_fwd_close(to_np(g["render_colors"])[gold_ok], d["rf_render_colors"][gold_ok],
+                         "colors vs golden")
+    # Backward from the oracle's forward state, near-threshold pixels muted.
+    vrc = np.random.default_rng(5).normal(size=e["render_colors"].shape).astype(np.float32)
+    vra = np.random.default_rng(6).normal(0, 0.1, size=e["render_alphas"].shape).astype(np.float32)
+    vrc[near] = 0
+    vra[near] = 0
+    fo = {"render_alphas": e["render_alphas"], "last_ids": e["last_ids"]}
+    b = gs.rasterize_to_pixels_3dgs_backward(
+        {k: T(v) for k, v in inp.items()}, {k: T(v) for k, v in fo.items()},
+        {"v_render_colors": T(vrc), "v_render_alphas": T(vra)}, W, H, ts, absgrad=True)
+    eb = oracle.raster_bwd(width=W, height=H, tile_size=ts, render_alphas=e["render_alphas"],
+                           last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra,
+                           absgrad=True, **inp)
+    for k, v in eb.items():
+        assert_grad_close(b[k], v, f"{name} {k}", atol_frac=1e-4)
+
+
+def test_rasterize_known_answers_and_masks(gs, cuda):
+    """gsplat_core/test/test.cpp:1067-1271 through the GPU path."""
+    base = {"means2d": T(np.array([[[1.0, 1.0]]], np.float32)),
+            "conics": T(np.array([[[1.0, 0.0, 1.0]]], np.float32)),
+            "colors": T(np.array([[[1.0, 0.0, 0.0]]], np.float32)),
+            "opacities": T(np.array([[0.5]], np.float32)),
+            "backgrounds": T(np.array([[0.1, 0.2, 0.3]], np.float32)),
+            "flatten_ids": T(np.array([0], np.int32))}
+    a = 0.5 * np.exp(-0.25)
+    Tt = 1 - a
+    r = gs.rasterize_to_pixels_3dgs_forward(dict(base, tile_offsets=T(np.zeros((1, 1, 1), np.int32))), 2, 2, 2)
+    assert np.allclose(to_np(r["render_alphas"]).ravel(), a, atol=1e-5)
+    assert np.allclose(to_np(r["render_colors"]).reshape(4, 3), [a + Tt * .1, Tt * .2, Tt * .3], atol=1e-5)
+    assert to_np(r["last_ids"]).ravel().tolist() == [0] * 4
+    rm = gs.rasterize_to_pixels_3dgs_forward(
+        dict(base, tile_offsets=T(np.array([[[0, 1]]], np.int32)), masks=T(np.array([[[True, False]]]))),
+        4, 2, 2)
+    al = to_np(rm["render_alphas"]).reshape(2, 4)
+    assert np.allclose(al[:, :2], a, atol=1e-5) and np.allclose(al[:, 2:], 0)
+    assert np.allclose(to_np(rm["render_colors"]).reshape(2, 4, 3)[:, 2:], [.1, .2, .3], atol=1e-6)
+
+
+def test_rasterize_masks_backward(gs, oracle, golden, cuda):
+    d = golden("chain_cfg1")
+    W, H, ts, inp = _raster_case(oracle, "chain_cfg1", d)
+    masks = np.random.default_rng(8).uniform(size=d["tile_offsets"].shape) > 0.3
+    inp = dict(inp, masks=masks)
+    e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
+    g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, W, H, ts)
+    ok = ~e["near_threshold"]
+    assert_fwd_close(to_np(g["render_colors"])[ok], e["render_colors"][ok], "masked colors")
+    vrc = np.random.default_rng(5).normal(size=e["render_colors"].shape).astype(np.float32)
+    vra = np.zeros(e["render_alphas"].shape, np.float32)
+    vrc[~ok] = 0
+    b = gs.rasterize_to_pixels_3dgs_backward(
+        {k: T(v) for k, v in inp.items()},
+        {"render_alphas": T(e["render_alphas"]), "last_ids": T(e["last_ids"])},
+        {"v_render_colors": T(vrc), "v_render_alphas": T(vra)}, W, H, ts)
+    eb = oracle.raster_bwd(width=W, height=H, tile_size=ts, render_alphas=e["render_alphas"],
+                           last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra, **inp)
+    for k, v in eb.items():
+        assert_grad_close(b[k], v, "masked " + k, atol_frac=1e-4)
