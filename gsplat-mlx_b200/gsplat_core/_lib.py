@@ -70,7 +70,7 @@ SIGNATURES = {
     "gs_quat_scale_to_covar_fwd": (ct.c_int, [_P(QS2CParams), _vp, _vp, _vp, _vp, _vp]),
     "gs_quat_scale_to_covar_bwd": (ct.c_int, [_P(QS2CParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gs_projection_fwd": (ct.c_int, [_P(ProjectionParams)] + [_vp] * 13),
-    "gs_projection_bwd": (ct.c_int, [_P(ProjectionParams)] + [_vp] * 20),
+    "gs_projection_bwd": (ct.c_int, [_P(ProjectionParams)] + [_vp] * 19),
     "gs_sh_fwd": (ct.c_int, [_P(SHParams), _vp, _vp, _vp, _vp, _vp]),
     "gs_sh_bwd": (ct.c_int, [_P(SHParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gs_sh_glue_fwd": (ct.c_int, [_P(SHGlueParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

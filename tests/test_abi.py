@@ -1,0 +1,89 @@
+"""The C ABI library (CPU-only checks; no kernel is launched): it loads,
+exports every function include/gsplat_b200.h declares, the ctypes
+declarations agree with the header, and host-side helpers behave."""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gsplat_b200.h")
+
+
+def _declarations():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = {}
+    for m in re.finditer(r"\b([A-Za-z_][\w \*]*?)\b(gs_\w+)\s*\(([^;{]*?)\)\s*;", text):
+        name, args = m.group(2), m.group(3).strip()
+        n = 0 if args in ("", "void") else len([a for a in args.split(",") if a.strip()])
+        decls[name] = n
+    return decls
+
+
+def test_header_declares_the_surface():
+    d = _declarations()
+    for name in ("gs_projection_fwd", "gs_projection_bwd", "gs_quat_scale_to_covar_fwd",
+                 "gs_quat_scale_to_covar_bwd", "gs_sh_fwd", "gs_sh_bwd", "gs_isect_tile_count",
+                 "gs_isect_scan", "gs_isect_tile_encode", "gs_isect_sort", "gs_isect_offset",
+                 "gs_rasterize_fwd", "gs_rasterize_bwd"):
+        assert name in d, name
+
+
+def test_library_exports_every_declared_symbol(gs):
+    lib = gs.load()
+    for name in _declarations():
+        assert hasattr(lib, name), f"{name} not exported"
+
+
+def test_ctypes_signatures_match_header(gs):
+    from gsplat_core._lib import SIGNATURES
+    decls = _declarations()
+    assert set(SIGNATURES) == set(decls), set(SIGNATURES) ^ set(decls)
+    for name, (_, args) in SIGNATURES.items():
+        assert len(args) == decls[name], f"{name}: ctypes {len(args)} args, header {decls[name]}"
+
+
+def test_param_struct_layouts(gs):
+    from gsplat_core import _lib as L
+    # Sizes of the POD parameter structs as a C compiler lays them out.
+    assert ct.sizeof(L.QS2CParams) == 24
+    assert ct.sizeof(L.ProjectionParams) == 52
+    assert ct.sizeof(L.SHParams) == 24
+    assert ct.sizeof(L.SHGlueParams) == 20
+    assert ct.sizeof(L.IsectParams) == 20
+    assert ct.sizeof(L.RasterParams) == 56
+
+
+def test_host_helpers(gs):
+    lib = gs.load()
+    assert lib.gs_version() >= 100
+    assert lib.gs_status_string(0) == b"ok"
+    assert lib.gs_status_string(5).startswith(b"workspace")
+    # floor(log2(x)) + 1 of the reference (gsplat_intersect.cpp:60-65)
+    for v, e in [(1, 1), (2, 2), (3, 2), (4, 3), (4346, 13), (8192, 14), (32400, 15)]:
+        assert gs.floor_log2_plus_one(v) == e
+    assert lib.gs_isect_sort_workspace_size(1000) > 12 * 1000
+    assert lib.gs_isect_scan_workspace_size(1 << 20) >= 8 * 256
+
+
+def test_invalid_arguments_rejected_before_launch(gs):
+    """Bad parameters return GS_ERR_INVALID with a message and launch
+    nothing (safe without a GPU)."""
+    from gsplat_core import _lib as L
+    lib = gs.load()
+    p = L.IsectParams(0, 10, 16, 4, 4)
+    assert lib.gs_isect_tile_count(ct.byref(p), None, None, None, None) == L.GS_ERR_INVALID
+    assert b"I * N" in lib.gs_last_error()
+    sp = L.SHParams(10, 4, 5, 0)
+    assert lib.gs_sh_fwd(ct.byref(sp), None, None, None, None, None) == L.GS_ERR_INVALID
+    assert b"degree 0..4" in lib.gs_last_error()
+    assert lib.gs_isect_sort(10, 70, None, None, None, None, None, 0, None) == L.GS_ERR_INVALID
+    rp = L.RasterParams(1, 1, 3, 16, 16, 64, 1, 1, 0, 0, 0, 0)
+    assert lib.gs_rasterize_fwd(ct.byref(rp), *([None] * 12)) == L.GS_ERR_INVALID
+    pp = L.ProjectionParams(1, 1, 1, 8, 8, 0.3, 0.01, 1e10, 0.0, 0, 1, 0, 0)
+    assert lib.gs_projection_bwd(ct.byref(pp), *([None] * 19)) == L.GS_ERR_INVALID
+    assert b"pinhole only" in lib.gs_last_error()

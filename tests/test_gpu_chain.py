@@ -96,7 +96,7 @@ def test_full_size_config3_properties(gs, oracle, cuda):
     torch.cuda.synchronize()
     p = oracle.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
                         quats=sc.quats[None], scales=sc.scales[None])
-    assert_exact(step.radii, p["radii"][0, 0], "radii")
+    assert_exact(step.radii[0], p["radii"][0, 0], "radii")
     tpg = np.zeros(sc.n, np.int32)
     oracle.lib.orc_isect_count(1, sc.n, p["means2d"].ctypes.data, p["radii"].ctypes.data,
                                16, sc.tile_width, sc.tile_height, tpg.ctypes.data)
