@@ -488,3 +488,64 @@ extern "C" int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32
                                                                              I, T, tb, tile_offsets);
   return launch_status("intersect_offset");
 }
+
+// ------------------------------------------------------------ no-alloc sort
+// Some callers may not allocate device memory at all while they run -- a host
+// engine that plans every device buffer up front and hands plugins only their
+// inputs and outputs, or a latency-bound loop where an allocation could fail
+// or stall.  For them the sort below takes its scratch from one fixed
+// file-scope device array instead of a caller workspace.  The array is part of
+// this library's module: every GPU that loads the library holds it until the
+// process exits, so it is kept modest and caps the problem size.
+
+#include <mutex>
+
+namespace {
+constexpr int64_t kNoAllocMaxIsects = int64_t(1) << 20;  // 1,048,576 intersections
+constexpr size_t kNoAllocScratchBytes = size_t(13) << 20;  // 13 MiB
+static __device__ __align__(256) unsigned char g_noalloc_sort_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[64] = {};  // device address of the array, per device
+}  // namespace
+
+extern "C" int gs_isect_sort_noalloc(int64_t n_isects, int32_t key_bits,
+                                     const int64_t* isect_ids, const int32_t* flatten_ids,
+                                     int64_t* sorted_isect_ids, int32_t* sorted_flatten_ids,
+                                     gs_stream_t stream) {
+  if (n_isects > kNoAllocMaxIsects) {
+    set_error("intersect_tile_sort_noalloc: %lld intersections exceed its fixed scratch "
+              "(at most %lld)", (long long)n_isects, (long long)kNoAllocMaxIsects);
+    return GS_ERR_INVALID;
+  }
+  if (n_isects < 0) return invalid("intersect_tile_sort_noalloc: negative size");
+  if (sort_layout(n_isects).total > kNoAllocScratchBytes)
+    return invalid("intersect_tile_sort_noalloc: scratch layout exceeds the fixed array");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return invalid("intersect_tile_sort_noalloc: no usable current device");
+  }
+  void* scratch = nullptr;
+  {
+    // Host code cannot use the array's name as a device address; look the
+    // address up once per device, with that device current.
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_sort_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        set_error("intersect_tile_sort_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(e));
+        return GS_ERR_CUDA;
+      }
+      g_noalloc_scratch_ptr[dev] = p;
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  // Every scratch byte the sort reads is written earlier in the same call
+  // (per-tile digit counts, scan block sums, ping-pong key/value buffers), so
+  // nothing needs clearing between calls.
+  return gs_isect_sort(n_isects, key_bits, isect_ids, flatten_ids, sorted_isect_ids,
+                       sorted_flatten_ids, scratch, kNoAllocScratchBytes, stream);
+}

@@ -82,6 +82,7 @@ SIGNATURES = {
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "gs_isect_sort_noalloc": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gs_rasterize_fwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 12),
     "gs_rasterize_bwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 19),
 }

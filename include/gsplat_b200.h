@@ -196,6 +196,23 @@ int gs_isect_sort(int64_t n_isects, int32_t key_bits, const int64_t* isect_ids,
                   int32_t* sorted_flatten_ids, void* workspace,
                   size_t workspace_bytes, gs_stream_t stream);
 
+/* The same stable sort for callers that may not allocate device memory while
+ * they run (for example a host engine that owns every device buffer and gives
+ * plugins only their inputs and outputs).  It has no counterpart in the
+ * reference.  Its scratch is a fixed 13 MiB array inside this library, held
+ * on every GPU that loads the library until the process exits; it sorts at
+ * most 1,048,576 intersections and returns GS_ERR_INVALID for more, before
+ * launching anything.  It calls no allocator.  The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress) with that device
+ * current -- make that first call before any stream capture.  All calls share
+ * the one array, which keeps the last call's contents: calls that may overlap
+ * on the GPU (several streams, several host threads) race and must be
+ * serialised by the caller. */
+int gs_isect_sort_noalloc(int64_t n_isects, int32_t key_bits,
+                          const int64_t* isect_ids, const int32_t* flatten_ids,
+                          int64_t* sorted_isect_ids, int32_t* sorted_flatten_ids,
+                          gs_stream_t stream);
+
 /* tile_offsets [I, tile_height, tile_width] int32 from sorted isect_ids:
  * lower bound of (image << tile_bits | tile) in isect_ids >> 32. */
 int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,
