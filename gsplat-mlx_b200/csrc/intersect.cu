@@ -49,34 +49,79 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
   }
 }
 
-__global__ void __launch_bounds__(256) encode_kernel(int64_t n, int n_per_image,
-                                                     const float* __restrict__ means2d,
-                                                     const int32_t* __restrict__ radii,
-                                                     const float* __restrict__ depths,
-                                                     const int32_t* __restrict__ offsets, int ts,
-                                                     int tw, int th, int tile_bits,
-                                                     int64_t n_isects,
-                                                     int64_t* __restrict__ isect_ids,
-                                                     int32_t* __restrict__ flatten_ids) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
-    if (rad.x <= 0 || rad.y <= 0) continue;
-    const float2 m = __ldg(reinterpret_cast<const float2*>(means2d) + i);
-    const Rect r = tile_rect(m.x, m.y, rad.x, rad.y, ts, tw, th);
-    const int64_t image_id = i / n_per_image;
-    const uint32_t depth_bits = __float_as_uint(__ldg(depths + i));
-    const int64_t hi = image_id << (32 + tile_bits);
-    int64_t out = __ldg(offsets + i);
-    for (int y = r.y0; y < r.y1; ++y)
-      for (int x = r.x0; x < r.x1; ++x) {
-        // Same bound the reference CPU path checks (gsplat_intersect.cpp:473).
-        if (out >= 0 && out < n_isects) {
-          isect_ids[out] = hi | ((int64_t)(y * tw + x) << 32) | (int64_t)depth_bits;
-          flatten_ids[out] = (int32_t)i;
+// One warp encodes 32 consecutive Gaussians at a time.  A warp scan of their
+// tile counts flattens the 32 runs into one index space j; lane l emits
+// entries j = l, l+32, ...: the owner Gaussian of j comes from a search over
+// the 32 prefix sums, its k-th tile in row-major order of its rect.  Runs
+// start at offsets[i] as in the reference (consecutive runs are adjacent
+// when offsets is the scan of the counts, so stores are coalesced); every
+// write is bounds-checked like the CPU path (gsplat_intersect.cpp:473).
+constexpr int kEncodeThreads = 256;
+constexpr int kEncodeWarps = kEncodeThreads / 32;
+
+__global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
+    int64_t n, int n_per_image, const float* __restrict__ means2d,
+    const int32_t* __restrict__ radii, const float* __restrict__ depths,
+    const int32_t* __restrict__ offsets, int ts, int tw, int th, int tile_bits, int64_t n_isects,
+    int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids) {
+  __shared__ int s_pref[kEncodeWarps][33];
+  __shared__ int s_x0[kEncodeWarps][32], s_y0[kEncodeWarps][32], s_w[kEncodeWarps][32];
+  __shared__ int64_t s_off[kEncodeWarps][32], s_base[kEncodeWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t chunks = (n + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kEncodeWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kEncodeWarps) {
+    const int64_t i = ch * 32 + lane;
+    int cnt = 0;
+    if (i < n) {
+      const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
+      if (rad.x > 0 && rad.y > 0) {
+        const float2 m = __ldg(reinterpret_cast<const float2*>(means2d) + i);
+        const Rect r = tile_rect(m.x, m.y, rad.x, rad.y, ts, tw, th);
+        const int w = r.x1 - r.x0;
+        cnt = (r.y1 - r.y0) * w;
+        if (cnt > 0) {
+          s_x0[warp][lane] = r.x0;
+          s_y0[warp][lane] = r.y0;
+          s_w[warp][lane] = w;
+          s_off[warp][lane] = __ldg(offsets + i);
+          const int64_t image_id = i / n_per_image;
+          s_base[warp][lane] = (image_id << (32 + tile_bits)) |
+                               (int64_t)__float_as_uint(__ldg(depths + i));
         }
-        ++out;
       }
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    s_pref[warp][lane + 1] = incl;
+    if (lane == 0) s_pref[warp][0] = 0;
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();
+    for (int j = lane; j < total; j += 32) {
+      // owner: the largest o with s_pref[o] <= j (counts of 0 never own)
+      int lo = 0, hi = 31;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pref[warp][mid] <= j) lo = mid;
+        else hi = mid - 1;
+      }
+      const int o = lo;
+      const int k = j - s_pref[warp][o];
+      const int w = s_w[warp][o];
+      const int dy = k / w;
+      const int y = s_y0[warp][o] + dy;
+      const int x = s_x0[warp][o] + (k - dy * w);
+      const int64_t pos = s_off[warp][o] + k;
+      if (pos >= 0 && pos < n_isects) {
+        isect_ids[pos] = s_base[warp][o] | ((int64_t)(y * tw + x) << 32);
+        flatten_ids[pos] = (int32_t)(ch * 32 + o);
+      }
+    }
+    __syncwarp();
   }
 }
 
@@ -214,19 +259,25 @@ __device__ __forceinline__ uint32_t digit_of(uint64_t k, int shift, uint64_t fli
 }
 
 // Per-CTA digit histogram of one pass; counts laid out digit-major
-// ([digit][cta]) so that one exclusive scan yields scatter offsets.
+// ([digit][cta]) so that each digit's row can be scanned independently.
 __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(
     int64_t n, const uint64_t* __restrict__ keys, int shift, uint64_t flip, int num_tiles,
     int32_t* __restrict__ counts) {
   __shared__ uint32_t s_hist[kSortWarps][kRadix];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&s_hist[0][0])[i] = 0;
-  __syncthreads();
   const int64_t base = (int64_t)blockIdx.x * kSortTile + (int64_t)warp * kWarpSpan;
-#pragma unroll 4
+  uint64_t k[kSortItems];
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {  // all loads in flight before any use
+    const int64_t i = base + r * 32 + lane;
+    k[r] = i < n ? __ldg(keys + i) : 0ull;
+  }
+  __syncthreads();
+#pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
     const int64_t i = base + r * 32 + lane;
-    if (i < n) atomicAdd(&s_hist[warp][digit_of(__ldg(keys + i), shift, flip)], 1u);
+    if (i < n) atomicAdd(&s_hist[warp][digit_of(k[r], shift, flip)], 1u);
   }
   __syncthreads();
   for (int d = threadIdx.x; d < kRadix; d += kSortThreads) {
@@ -235,6 +286,36 @@ __global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(
     for (int w = 0; w < kSortWarps; ++w) c += s_hist[w][d];
     counts[(int64_t)d * num_tiles + blockIdx.x] = (int32_t)c;
   }
+}
+
+// One CTA per digit: exclusive scan of that digit's per-tile counts in
+// place (offsets of the digit's keys within the digit) and the digit total.
+constexpr int kRowScanThreads = 256;
+__global__ void __launch_bounds__(kRowScanThreads) radix_rowscan_kernel(
+    int num_tiles, int32_t* __restrict__ counts, int32_t* __restrict__ totals) {
+  __shared__ int64_t s_warp[32];
+  int32_t* row = counts + (int64_t)blockIdx.x * num_tiles;
+  int64_t carry = 0;
+  for (int b0 = 0; b0 < num_tiles; b0 += kRowScanThreads * 4) {
+    int32_t v[4];
+    int64_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = b0 + threadIdx.x * 4 + k;
+      v[k] = i < num_tiles ? row[i] : 0;
+      acc += v[k];
+    }
+    int64_t chunk_total;
+    int64_t run = block_exclusive_scan<kRowScanThreads>(acc, s_warp, &chunk_total) + carry;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = b0 + threadIdx.x * 4 + k;
+      if (i < num_tiles) row[i] = (int32_t)run;
+      run += v[k];
+    }
+    carry += chunk_total;
+  }
+  if (threadIdx.x == 0) totals[blockIdx.x] = (int32_t)carry;
 }
 
 struct DownSmem {
@@ -248,31 +329,37 @@ struct DownSmem {
 
 // Stable rank-and-scatter of one pass.  Keys of a warp are processed in
 // index order (round r covers keys r*32..r*32+31 of the warp's span), lanes
-// in lane order, so ranks respect input order and the sort is stable.
-__global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
+// in lane order, so ranks respect input order and the sort is stable.  The
+// global base of each digit is the exclusive scan of the 256 digit totals
+// (done here, redundantly per CTA) plus this CTA's row offset.
+__global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
     int64_t n, const uint64_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
     uint64_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int shift, uint64_t flip,
-    int num_tiles, const int32_t* __restrict__ offsets) {
+    int num_tiles, const int32_t* __restrict__ offsets, const int32_t* __restrict__ totals) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   DownSmem& sm = *reinterpret_cast<DownSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
-  for (int d = threadIdx.x; d < kRadix; d += kSortThreads)
-    sm.goff[d] = (uint32_t)__ldg(offsets + (int64_t)d * num_tiles + blockIdx.x);
-  __syncthreads();
-
   const int64_t tile_base = (int64_t)blockIdx.x * kSortTile;
   const int64_t base = tile_base + (int64_t)warp * kWarpSpan;
   uint64_t k[kSortItems];
-  int32_t v[kSortItems];
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {  // all loads in flight before ranking
+    const int64_t i = base + r * 32 + lane;
+    k[r] = i < n ? __ldg(keys_in + i) : 0ull;
+  }
+  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
+  int64_t unused;
+  const int64_t dbase =
+      block_exclusive_scan<kSortThreads>(__ldg(totals + threadIdx.x), sm.warp_tot, &unused);
+  sm.goff[threadIdx.x] =
+      (uint32_t)(dbase + __ldg(offsets + (int64_t)threadIdx.x * num_tiles + blockIdx.x));
+  __syncthreads();
+
   uint32_t rank[kSortItems];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
-    const int64_t i = base + r * 32 + lane;
-    const bool valid = i < n;
-    k[r] = valid ? __ldg(keys_in + i) : 0ull;
-    v[r] = valid ? __ldg(vals_in + i) : 0;
+    const bool valid = base + r * 32 + lane < n;
     // Invalid lanes form their own group (digit 256) and count nowhere.
     const uint32_t d = valid ? digit_of(k[r], shift, flip) : (uint32_t)kRadix;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
@@ -289,7 +376,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
   // Per digit: exclusive offsets over warps, CTA count, then a CTA-wide
   // exclusive scan over digits for the staging layout.
   uint32_t cta_count = 0;
-  if (threadIdx.x < kRadix) {
+  {
     const int d = threadIdx.x;
 #pragma unroll
     for (int w = 0; w < kSortWarps; ++w) {
@@ -300,7 +387,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
   }
   int64_t total;
   const int64_t start = block_exclusive_scan<kSortThreads>(cta_count, sm.warp_tot, &total);
-  if (threadIdx.x < kRadix) sm.digit_start[threadIdx.x] = (uint32_t)start;
+  sm.digit_start[threadIdx.x] = (uint32_t)start;
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
@@ -309,7 +396,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
       const uint32_t d = digit_of(k[r], shift, flip);
       const uint32_t p = sm.digit_start[d] + sm.hist[warp][d] + rank[r];
       sm.keys[p] = k[r];
-      sm.vals[p] = v[r];
+      sm.vals[p] = __ldg(vals_in + i);
     }
   }
   __syncthreads();
@@ -326,7 +413,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_downsweep_kernel(
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
 struct SortLayout {
-  size_t keys_alt, vals_alt, counts, scan, total;
+  size_t keys_alt, vals_alt, counts, totals, total;
 };
 
 SortLayout sort_layout(int64_t n) {
@@ -336,8 +423,8 @@ SortLayout sort_layout(int64_t n) {
   L.keys_alt = 0;
   L.vals_alt = L.keys_alt + align256(sizeof(uint64_t) * (size_t)(n < 1 ? 1 : n));
   L.counts = L.vals_alt + align256(sizeof(int32_t) * (size_t)(n < 1 ? 1 : n));
-  L.scan = L.counts + align256(sizeof(int32_t) * (size_t)ncounts);
-  L.total = L.scan + scan_ws_bytes(ncounts);
+  L.totals = L.counts + align256(sizeof(int32_t) * (size_t)ncounts);
+  L.total = L.totals + align256(sizeof(int32_t) * kRadix);
   return L;
 }
 
@@ -418,7 +505,7 @@ extern "C" int gs_isect_tile_encode(const gs_isect_params* p, const float* means
   if (n == 0 || n_isects == 0) return GS_OK;
   if (!means2d || !radii || !depths || !offsets || !isect_ids || !flatten_ids)
     return invalid("intersect_tile_encode: missing buffer");
-  encode_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+  encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, as_stream(stream)>>>(
       n, p->N, means2d, radii, depths, offsets, p->tile_size, p->tile_width, p->tile_height,
       tile_bits, n_isects, isect_ids, flatten_ids);
   return launch_status("intersect_tile_encode");
@@ -447,9 +534,8 @@ extern "C" int gs_isect_sort(int64_t n, int32_t key_bits, const int64_t* isect_i
   uint64_t* alt_k = reinterpret_cast<uint64_t*>(ws + L.keys_alt);
   int32_t* alt_v = reinterpret_cast<int32_t*>(ws + L.vals_alt);
   int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-  void* scan_ws = ws + L.scan;
+  int32_t* totals = reinterpret_cast<int32_t*>(ws + L.totals);
   const int tiles = (int)ceil_div(n, kSortTile);
-  const int64_t ncounts = (int64_t)tiles * kRadix;
   const int passes = (key_bits + 7) / 8;
   // Signed order: with all 64 bits in play the sign bit is flipped so that
   // an unsigned digit sort orders like the signed int64 comparison.
@@ -465,10 +551,9 @@ extern "C" int gs_isect_sort(int64_t n, int32_t key_bits, const int64_t* isect_i
     int32_t* dst_v = to_out ? sorted_flatten_ids : alt_v;
     const int shift = pass * 8;
     radix_upsweep_kernel<<<tiles, kSortThreads, 0, s>>>(n, src_k, shift, flip, tiles, counts);
-    int rc = scan_i32(ncounts, counts, counts, nullptr, scan_ws, L.total - L.scan, s);
-    if (rc) return rc;
+    radix_rowscan_kernel<<<kRadix, kRowScanThreads, 0, s>>>(tiles, counts, totals);
     radix_downsweep_kernel<<<tiles, kSortThreads, smem, s>>>(n, src_k, src_v, dst_k, dst_v, shift,
-                                                             flip, tiles, counts);
+                                                             flip, tiles, counts, totals);
     src_k = dst_k;
     src_v = dst_v;
   }

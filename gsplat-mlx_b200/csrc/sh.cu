@@ -62,9 +62,9 @@ __device__ __forceinline__ void basis(float x, float y, float z, float* b) {
 // colour = sum_b basis_b * coeff_b, accumulated per degree band like the
 // reference (gsplat_spherical_harmonics.cpp:189-286).
 template <int D>
-__device__ __forceinline__ void sh_color(const float* d, const float* __restrict__ co, float out[3]) {
+__device__ __forceinline__ void sh_color(const float* d, const float* co, float out[3]) {
 #pragma unroll
-  for (int ch = 0; ch < 3; ++ch) out[ch] = kC0 * __ldg(co + ch);
+  for (int ch = 0; ch < 3; ++ch) out[ch] = kC0 * co[ch];
   if (D < 1) return;
   const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
   if (norm == 0.0f) return;
@@ -78,7 +78,7 @@ __device__ __forceinline__ void sh_color(const float* d, const float* __restrict
     for (int ch = 0; ch < 3; ++ch) {
       float acc = 0.0f;
 #pragma unroll
-      for (int k = bands[l - 1]; k < bands[l]; ++k) acc += b[k] * __ldg(co + k * 3 + ch);
+      for (int k = bands[l - 1]; k < bands[l]; ++k) acc += b[k] * co[k * 3 + ch];
       out[ch] += acc;
     }
   }
@@ -86,7 +86,7 @@ __device__ __forceinline__ void sh_color(const float* d, const float* __restrict
 
 // gsplat_spherical_harmonics.cpp:288-425: d colour / d dir (un-normalised).
 template <int D>
-__device__ __forceinline__ void sh_dir_vjp(const float* d, const float* __restrict__ co,
+__device__ __forceinline__ void sh_dir_vjp(const float* d, const float* co,
                                            const float vc[3], float vd[3]) {
   vd[0] = vd[1] = vd[2] = 0.0f;
   if (D < 1) return;
@@ -183,8 +183,7 @@ __device__ __forceinline__ void sh_dir_vjp(const float* d, const float* __restri
   float vn0 = 0.0f, vn1 = 0.0f, vn2 = 0.0f;
 #pragma unroll
   for (int k = 1; k < A; ++k) {
-    const float vb = __ldg(co + k * 3) * vc[0] + __ldg(co + k * 3 + 1) * vc[1] +
-                     __ldg(co + k * 3 + 2) * vc[2];
+    const float vb = co[k * 3] * vc[0] + co[k * 3 + 1] * vc[1] + co[k * 3 + 2] * vc[2];
     vn0 += dx[k] * vb;
     vn1 += dy[k] * vb;
     vn2 += dz[k] * vb;
@@ -383,6 +382,288 @@ __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
   }
 }
 
+// ------------------------------------------------------------ warp-staged
+// Each warp owns 32 consecutive elements.  Their coefficient rows (R = 3K
+// floats each, contiguous in memory) are copied into shared memory with
+// whole-warp coalesced accesses -- or row by row when only a few rows are
+// needed (culled Gaussians are skipped) -- at an odd row stride S, so that
+// every lane can then walk its own row with conflict-free shared loads.
+// Gradient rows are assembled the same way and written back with
+// coalesced stores.  Used when R <= kWsMaxR (K <= 25, i.e. up to SH4).
+
+constexpr int kWsThreads = 128;
+constexpr int kWsWarps = kWsThreads / 32;
+constexpr int kWsMaxR = 75;
+
+__device__ __forceinline__ void ws_load_block(const float* __restrict__ g, int64_t e0, int cnt,
+                                              int R, int S, float* sm, int lane) {
+  const float* src = g + e0 * R;
+  const int total = cnt * R;
+  int row = 0, col = lane;
+  while (col >= R) { col -= R; ++row; }
+  for (int f = lane; f < total; f += 32) {
+    sm[row * S + col] = __ldg(src + f);
+    col += 32;
+    while (col >= R) { col -= R; ++row; }
+  }
+}
+
+__device__ __forceinline__ void ws_load_rows(const float* __restrict__ g, int64_t e0, int cnt,
+                                             uint32_t need, int R, int S, float* sm, int lane) {
+  if (__popc(need) * 4 >= cnt * 3) {  // most rows needed: one contiguous sweep
+    ws_load_block(g, e0, cnt, R, S, sm, lane);
+    return;
+  }
+  while (need) {
+    const int r = __ffs(need) - 1;
+    need &= need - 1;
+    const float* src = g + (e0 + r) * R;
+    for (int c = lane; c < R; c += 32) sm[r * S + c] = __ldg(src + c);
+  }
+}
+
+__device__ __forceinline__ void ws_store_block(float* __restrict__ g, int64_t e0, int cnt, int R,
+                                               int S, const float* sm, int lane) {
+  float* dst = g + e0 * R;
+  const int total = cnt * R;
+  int row = 0, col = lane;
+  while (col >= R) { col -= R; ++row; }
+  for (int f = lane; f < total; f += 32) {
+    dst[f] = sm[row * S + col];
+    col += 32;
+    while (col >= R) { col -= R; ++row; }
+  }
+}
+
+// v_coeffs row (active bases; the caller zeroed the rest) += basis * vc.
+template <int D>
+__device__ __forceinline__ void add_vcoeffs(const float* d, const float vc[3], float* row) {
+  constexpr int A = (D + 1) * (D + 1);
+  float b[25];
+  b[0] = kC0;
+#pragma unroll
+  for (int k = 1; k < A; ++k) b[k] = 0.0f;
+  if (D >= 1) {
+    const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+    if (norm != 0.0f) basis<D>(d[0] / norm, d[1] / norm, d[2] / norm, b);
+  }
+#pragma unroll
+  for (int k = 0; k < A; ++k)
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) row[k * 3 + ch] += b[k] * vc[ch];
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWsThreads) glue_fwd_ws_kernel(
+    int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
+    const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
+    const int32_t* __restrict__ radii, float* __restrict__ colors) {
+  extern __shared__ float smem[];
+  const int R = K * 3, S = R | 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sm = smem + warp * 32 * S;
+  const int64_t chunks = (N + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kWsWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kWsWarps) {
+    const int64_t e0 = ch * 32;
+    const int cnt = (int)(N - e0 < 32 ? N - e0 : 32);
+    const int64_t n = e0 + lane;
+    const bool live = lane < cnt;
+    bool any = false;
+    for (int c = 0; c < C && live; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    const uint32_t need = __ballot_sync(0xffffffffu, any);
+    ws_load_rows(coeffs, e0, cnt, need, R, S, sm, lane);
+    __syncwarp();
+    float m[3] = {0.f, 0.f, 0.f};
+    if (live) {
+      m[0] = __ldg(means + n * 3);
+      m[1] = __ldg(means + n * 3 + 1);
+      m[2] = __ldg(means + n * 3 + 2);
+    }
+    for (int c = 0; c < C; ++c) {
+      if (!live) break;
+      const int64_t e = (int64_t)c * N + n;
+      float out[3] = {0.0f, 0.0f, 0.0f};
+      if (visible(masks, radii, e)) {
+        float cp[3];
+        campos_of(viewmats + (int64_t)c * 16, cp);
+        const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+        const float s = fmaxf(sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]), 1.0e-8f);
+        const float d[3] = {u[0] / s, u[1] / s, u[2] / s};
+        sh_color<D>(d, sm + lane * S, out);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) out[k] = fminf(fmaxf(out[k] + 0.5f, 0.0f), 1.0f);
+      }
+      colors[e * 3] = out[0];
+      colors[e * 3 + 1] = out[1];
+      colors[e * 3 + 2] = out[2];
+    }
+    __syncwarp();
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
+    int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
+    const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
+    const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
+    float* __restrict__ v_means, float* __restrict__ v_coeffs) {
+  extern __shared__ float smem[];
+  const int R = K * 3, S = R | 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sm = smem + warp * 64 * S;   // coefficient rows
+  float* sv = sm + 32 * S;            // gradient rows
+  const int64_t chunks = (N + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kWsWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kWsWarps) {
+    const int64_t e0 = ch * 32;
+    const int cnt = (int)(N - e0 < 32 ? N - e0 : 32);
+    const int64_t n = e0 + lane;
+    const bool live = lane < cnt;
+    bool any = false;
+    for (int c = 0; c < C && live; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    const uint32_t need = __ballot_sync(0xffffffffu, any);
+    ws_load_rows(coeffs, e0, cnt, need, R, S, sm, lane);
+    float* myv = sv + lane * S;
+    for (int j = 0; j < R; ++j) myv[j] = 0.0f;
+    __syncwarp();
+    float vm[3] = {0.0f, 0.0f, 0.0f};
+    if (any) {
+      const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1), __ldg(means + n * 3 + 2)};
+      const float* co = sm + lane * S;
+      for (int c = 0; c < C; ++c) {
+        const int64_t e = (int64_t)c * N + n;
+        if (!visible(masks, radii, e)) continue;
+        float cp[3];
+        campos_of(viewmats + (int64_t)c * 16, cp);
+        const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+        const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
+        const float mm = fmaxf(s, 1.0e-8f);
+        const float d[3] = {u[0] / mm, u[1] / mm, u[2] / mm};
+        float x[3];
+        sh_color<D>(d, co, x);
+        float vc[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const float v = x[k] + 0.5f;
+          vc[k] = (v > 0.0f && v < 1.0f) ? __ldg(v_colors + e * 3 + k) : 0.0f;
+        }
+        add_vcoeffs<D>(d, vc, myv);
+        float vd[3];
+        sh_dir_vjp<D>(d, co, vc, vd);
+        const float dot = vd[0] * u[0] + vd[1] * u[1] + vd[2] * u[2];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          float vu = vd[i] / mm;
+          if (s > 1.0e-8f) vu -= (u[i] / s) * dot / (mm * mm);
+          vm[i] += vu;
+        }
+      }
+    }
+    __syncwarp();
+    ws_store_block(v_coeffs, e0, cnt, R, S, sv, lane);
+    if (live) {
+      v_means[n * 3] += vm[0];
+      v_means[n * 3 + 1] += vm[1];
+      v_means[n * 3 + 2] += vm[2];
+    }
+    __syncwarp();
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWsThreads) sh_fwd_ws_kernel(int64_t n, int K,
+                                                               const float* __restrict__ dirs,
+                                                               const float* __restrict__ coeffs,
+                                                               const uint8_t* __restrict__ masks,
+                                                               float* __restrict__ colors) {
+  extern __shared__ float smem[];
+  const int R = K * 3, S = R | 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sm = smem + warp * 32 * S;
+  const int64_t chunks = (n + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kWsWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kWsWarps) {
+    const int64_t e0 = ch * 32;
+    const int cnt = (int)(n - e0 < 32 ? n - e0 : 32);
+    const int64_t e = e0 + lane;
+    const bool on = lane < cnt && (!masks || masks[e]);
+    ws_load_rows(coeffs, e0, cnt, __ballot_sync(0xffffffffu, on), R, S, sm, lane);
+    __syncwarp();
+    if (lane < cnt) {
+      float c[3] = {0.0f, 0.0f, 0.0f};
+      if (on) {
+        const float d[3] = {__ldg(dirs + e * 3), __ldg(dirs + e * 3 + 1), __ldg(dirs + e * 3 + 2)};
+        sh_color<D>(d, sm + lane * S, c);
+      }
+      colors[e * 3] = c[0];
+      colors[e * 3 + 1] = c[1];
+      colors[e * 3 + 2] = c[2];
+    }
+    __syncwarp();
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kWsThreads) sh_bwd_ws_kernel(
+    int64_t n, int K, const float* __restrict__ dirs, const float* __restrict__ coeffs,
+    const uint8_t* __restrict__ masks, const float* __restrict__ v_colors,
+    float* __restrict__ v_dirs, float* __restrict__ v_coeffs) {
+  extern __shared__ float smem[];
+  const int R = K * 3, S = R | 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sm = smem + warp * 64 * S;
+  float* sv = sm + 32 * S;
+  const int64_t chunks = (n + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kWsWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kWsWarps) {
+    const int64_t e0 = ch * 32;
+    const int cnt = (int)(n - e0 < 32 ? n - e0 : 32);
+    const int64_t e = e0 + lane;
+    const bool on = lane < cnt && (!masks || masks[e]);
+    // coefficient rows are only read for v_dirs
+    ws_load_rows(coeffs, e0, cnt, v_dirs ? __ballot_sync(0xffffffffu, on) : 0u, R, S, sm, lane);
+    float* myv = sv + lane * S;
+    for (int j = 0; j < R; ++j) myv[j] = 0.0f;
+    __syncwarp();
+    if (on) {
+      const float d[3] = {__ldg(dirs + e * 3), __ldg(dirs + e * 3 + 1), __ldg(dirs + e * 3 + 2)};
+      const float vc[3] = {__ldg(v_colors + e * 3), __ldg(v_colors + e * 3 + 1),
+                           __ldg(v_colors + e * 3 + 2)};
+      add_vcoeffs<D>(d, vc, myv);
+      if (v_dirs) {
+        float vd[3];
+        sh_dir_vjp<D>(d, sm + lane * S, vc, vd);
+        v_dirs[e * 3] = vd[0];
+        v_dirs[e * 3 + 1] = vd[1];
+        v_dirs[e * 3 + 2] = vd[2];
+      }
+    } else if (lane < cnt && v_dirs) {
+      v_dirs[e * 3] = v_dirs[e * 3 + 1] = v_dirs[e * 3 + 2] = 0.0f;
+    }
+    __syncwarp();
+    ws_store_block(v_coeffs, e0, cnt, R, S, sv, lane);
+    __syncwarp();
+  }
+}
+
+// Launch helper of the staged kernels: `rows` row buffers of 32 x S floats
+// per warp.
+template <typename Kern>
+int ws_launch(Kern kernel, int64_t elems, int K, int rows, cudaStream_t s, const char* what,
+              void** args) {
+  const int S = (K * 3) | 1;
+  const size_t smem = sizeof(float) * (size_t)kWsWarps * rows * 32 * S;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int64_t chunks = (elems + 31) / 32;
+  const unsigned grid = grid_for(chunks, kWsWarps, 8);
+  if (cudaLaunchKernel((const void*)kernel, dim3(grid), dim3(kWsThreads), args, smem, s) !=
+      cudaSuccess)
+    return launch_status(what);
+  return launch_status(what);
+}
+
 template <template <int> class Launch, typename... Args>
 int by_degree(int degree, Args... args) {
   switch (degree) {
@@ -399,6 +680,13 @@ template <int D>
 struct FwdL {
   static int run(const gs_sh_params* p, const float* dirs, const float* coeffs,
                  const uint8_t* masks, float* colors, cudaStream_t s) {
+    if (p->K * 3 <= kWsMaxR) {
+      int64_t n = p->n;
+      int K = p->K;
+      const uint8_t* mk = p->use_masks ? masks : nullptr;
+      void* args[] = {&n, &K, &dirs, &coeffs, &mk, &colors};
+      return ws_launch(sh_fwd_ws_kernel<D>, n, K, 1, s, "sh_fwd", args);
+    }
     sh_fwd_kernel<D><<<grid_for(p->n, 256), 256, 0, s>>>(p->n, p->K, dirs, coeffs,
                                                          p->use_masks ? masks : nullptr, colors);
     return launch_status("sh_fwd");
@@ -410,6 +698,13 @@ struct BwdL {
   static int run(const gs_sh_params* p, const float* dirs, const float* coeffs,
                  const uint8_t* masks, const float* v_colors, float* v_dirs, float* v_coeffs,
                  cudaStream_t s) {
+    if (p->K * 3 <= kWsMaxR) {
+      int64_t n = p->n;
+      int K = p->K;
+      const uint8_t* mk = p->use_masks ? masks : nullptr;
+      void* args[] = {&n, &K, &dirs, &coeffs, &mk, &v_colors, &v_dirs, &v_coeffs};
+      return ws_launch(sh_bwd_ws_kernel<D>, n, K, 2, s, "sh_bwd", args);
+    }
     sh_bwd_kernel<D><<<grid_for(p->n, 256), 256, 0, s>>>(
         p->n, p->K, dirs, coeffs, p->use_masks ? masks : nullptr, v_colors, v_dirs, v_coeffs);
     return launch_status("sh_bwd");
@@ -421,6 +716,12 @@ struct GlueFwdL {
   static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
                  const float* coeffs, const uint8_t* masks, const int32_t* radii, float* colors,
                  cudaStream_t s) {
+    if (p->K * 3 <= kWsMaxR) {
+      int C = p->C, N = p->N, K = p->K;
+      const uint8_t* mk = p->use_masks ? masks : nullptr;
+      void* args[] = {&C, &N, &K, &means, &viewmats, &coeffs, &mk, &radii, &colors};
+      return ws_launch(glue_fwd_ws_kernel<D>, N, K, 1, s, "sh_glue_fwd", args);
+    }
     glue_fwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(
         p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii, colors);
     return launch_status("sh_glue_fwd");
@@ -432,6 +733,13 @@ struct GlueBwdL {
   static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
                  const float* coeffs, const uint8_t* masks, const int32_t* radii,
                  const float* v_colors, float* v_means, float* v_coeffs, cudaStream_t s) {
+    if (p->K * 3 <= kWsMaxR) {
+      int C = p->C, N = p->N, K = p->K;
+      const uint8_t* mk = p->use_masks ? masks : nullptr;
+      void* args[] = {&C, &N, &K, &means, &viewmats, &coeffs, &mk, &radii, &v_colors, &v_means,
+                      &v_coeffs};
+      return ws_launch(glue_bwd_ws_kernel<D>, N, K, 2, s, "sh_glue_bwd", args);
+    }
     glue_bwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(p->C, p->N, p->K, means, viewmats,
                                                            coeffs, p->use_masks ? masks : nullptr,
                                                            radii, v_colors, v_means, v_coeffs);
