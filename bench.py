@@ -37,6 +37,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd ms/step and Mpix/s at 1M Gaussians SH3; intersections sorted/s"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# measured peer copy per direction per GPU on this pool (NVLink 5; 900 nominal)
+LINK_GBS = 770.0
 
 
 def load_peaks():
@@ -140,9 +142,9 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
 
 def our_kernel_launches(sort_passes):
     # projection fwd 1, glue fwd 1, count 1, scan 3, encode 1,
-    # sort passes x (upsweep + 3 scan + downsweep), offset 1,
+    # sort passes x (upsweep + rowscan + downsweep), offset 1,
     # rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
-    return 1 + 1 + 1 + 3 + 1 + sort_passes * 5 + 1 + 1 + 1 + 1 + 1
+    return 1 + 1 + 1 + 3 + 1 + sort_passes * 3 + 1 + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -233,7 +235,8 @@ def run_reference_arm(args):
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from gsplat_core import pipeline, synthetic as S
+    from gsplat_core import synthetic as S
+    from gsplat_core.sharded import ShardedTrainingStep, exchange_bytes
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -246,20 +249,25 @@ def run_ours(args):
 
     sc = scene_for(rank, world, args.seed)
     vrc_np, vra_np = S.cotangents(args.seed + rank, 1, sc.height, sc.width)
+    # every rank holds the poses of all ranks' cameras (the SH exchange
+    # recomputes the colour basis of remote cameras)
+    views_all = np.concatenate([scene_for(r, world, args.seed).viewmats for r in range(world)])
+    Ks_all = np.repeat(sc.Ks[:1], world, 0)
     host = {"means": sc.means, "quats": sc.quats, "scales": sc.scales,
-            "opacities": sc.opacities, "coeffs": sc.coeffs, "viewmats": sc.viewmats,
-            "Ks": sc.Ks, "v_render_colors": vrc_np, "v_render_alphas": vra_np}
+            "opacities": sc.opacities, "coeffs": sc.coeffs, "viewmats": views_all,
+            "Ks": Ks_all, "v_render_colors": vrc_np, "v_render_alphas": vra_np}
     order = list(host)
     d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in host.items()}
     pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in host.items()}
-    step = pipeline.TrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], 1, sc.width, sc.height,
-                                 device=dev)
+    sharded = ShardedTrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], world, sc.width,
+                                  sc.height, exchange=args.exchange, device=dev)
+    step = sharded.step
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def one(inp):
-        flat, m = step.run(*[inp[k] for k in order])
+        flat, m = sharded.run(*[inp[k] for k in order])
         if world > 1:
-            dist.all_reduce(flat)
+            step._mark("exchange")
         return m
 
     for _ in range(args.warmup):
@@ -336,11 +344,19 @@ def run_ours(args):
         K = sc.coeffs.shape[1]
         passes = (step.key_bits + 7) // 8
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
-        top = max(avg, key=avg.get)
+        top = max((k for k in avg if k != "exchange"), key=avg.get)
         bytes_top = algorithmic_bytes(top, sc.n, visible, m, sc.width * sc.height, K, passes)
         achieved = bytes_top / (avg[top] / 1e3) / 1e9
         stages = {}
         for k, v in avg.items():
+            if k == "exchange":
+                # NCCL exchange (+ the SH glue backward over all cameras in
+                # gather mode): bytes each rank sends, against the link
+                b = exchange_bytes(sharded.exchange, sc.n, K, 1, world)
+                stages[k] = {"ms": round(v, 4), "mode": sharded.exchange,
+                             "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
+                             "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
+                continue
             b = algorithmic_bytes(k, sc.n, visible, m, sc.width * sc.height, K, passes)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
@@ -362,6 +378,7 @@ def run_ours(args):
             "config": {"workload": "cfg3: N=1M SH3 Gaussians, 1 camera 1297x840 per GPU, tile 16",
                        "gaussians": sc.n, "visible": visible, "isects": m,
                        "parallelism": f"camera-sharded dp{world}" if world > 1 else "single",
+                       "exchange": sharded.exchange if world > 1 else None,
                        "l2": "flushed (256 MB write) between timed steps"},
             "intersections_sorted_per_s": round(m * world / (ms_step / 1e3), 1),
             "stages_ms": stages,
@@ -391,6 +408,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-stride", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["auto", "allreduce", "gather"], default="auto",
+                    help="gradient exchange of the camera-sharded step (N > 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -367,12 +367,374 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
   }
 }
 
+// ------------------------------------------------------------------ 16x16 tiles
+// The common 16x16 tile runs on 128 threads: thread t owns pixels
+// (t % 16, t / 16) and (t % 16, t / 16 + 8).  Per staged Gaussian the shared
+// loads, the loop control and -- in the backward -- the warp reduction are
+// shared by 64 pixels per warp instead of 32.  Gaussians are staged packed:
+// a = (mean x, mean y, conic0, conic1), b = (conic2, opacity, col0, col1),
+// c = (col2, col3).  Per-pixel arithmetic is unchanged.
+constexpr int kT16Threads = 128;
+
+// Can the Gaussian reach alpha >= 1/255 at any pixel centre of the tile?
+// sigma(d) = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy is convex for a positive
+// definite conic, so its minimum over the box of pixel-centre offsets
+// [mx - x0 - 15, mx - x0] x [my - y0 - 15, my - y0] is 0 when the mean lies
+// inside, else on an edge, where it is a 1-D quadratic minimised in closed
+// form and clamped.  A Gaussian is dropped only when even that minimum
+// leaves o exp(-sigma) below the threshold by a margin that covers the fp32
+// rounding of the per-pixel sigma and of __expf; such a Gaussian would be
+// skipped by every pixel of the tile (alpha < 1/255), so dropping it
+// changes no output bit.  Conics that are not positive definite are kept.
+__device__ __forceinline__ bool tile_may_hit(float mx, float my, float c0, float c1, float c2,
+                                             float o, float x0, float y0) {
+  if (!(c0 > 0.0f && c2 > 0.0f && c0 * c2 - c1 * c1 > 0.0f)) return true;
+  const float dxl = mx - (x0 + 15.0f), dxh = mx - x0;
+  const float dyl = my - (y0 + 15.0f), dyh = my - y0;
+  float best = 0.0f;
+  if (!(dxl <= 0.0f && dxh >= 0.0f && dyl <= 0.0f && dyh >= 0.0f)) {
+    const float ry = -c1 / c2, rx = -c1 / c0;
+    best = INFINITY;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float X = e ? dxh : dxl;
+      const float Y = fminf(fmaxf(ry * X, dyl), dyh);
+      best = fminf(best, 0.5f * (c0 * X * X + c2 * Y * Y) + c1 * X * Y);
+      const float Y2 = e ? dyh : dyl;
+      const float X2 = fminf(fmaxf(rx * Y2, dxl), dxh);
+      best = fminf(best, 0.5f * (c0 * X2 * X2 + c2 * Y2 * Y2) + c1 * X2 * Y2);
+    }
+  }
+  const float xm = fmaxf(fabsf(dxl), fabsf(dxh)), ym = fmaxf(fabsf(dyl), fabsf(dyh));
+  const float mag = 0.5f * (c0 * xm * xm + c2 * ym * ym) + fabsf(c1) * xm * ym;
+  const float margin = 1.0e-5f * mag + 1.0e-5f;
+  return o * __expf(-(best - margin)) >= kAlphaThreshold * 0.998f;
+}
+
+// Stage the batch [b0, b0 + 128) of the tile's intersection list: thread t
+// loads entry b0 + t, tests it against the tile, and the kept entries are
+// compacted in list order into the packed shared arrays.  Returns the
+// number kept.  Entries: a = (mean x, mean y, conic0, conic1),
+// b = (conic2, opacity, col0, col1), c = (col2, col3), the intersection
+// index and the Gaussian id.
+template <int CH>
+__device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0, float y0,
+                                       float4* sa, float4* sb, float2* sc, int* sidx, int* sgid,
+                                       int* swcnt) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int idx = b0 + tid;
+  bool keep = false;
+  int g = 0;
+  if (idx < end) {
+    g = __ldg(a.flatten_ids + idx);
+    const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+    const float* con = a.conics + (int64_t)g * 3;
+    keep = tile_may_hit(m.x, m.y, __ldg(con), __ldg(con + 1), __ldg(con + 2),
+                        __ldg(a.opacities + g), x0, y0);
+  }
+  const unsigned bal = __ballot_sync(0xffffffffu, keep);
+  if (lane == 0) swcnt[warp] = __popc(bal);
+  __syncthreads();
+  int base = 0, cnt = 0;
+#pragma unroll
+  for (int w = 0; w < kT16Threads / 32; ++w) {
+    const int c = swcnt[w];
+    base += w < warp ? c : 0;
+    cnt += c;
+  }
+  if (keep) {
+    // the record is re-read (L1 hits) rather than held across the barrier
+    const int slot = base + __popc(bal & ((1u << lane) - 1u));
+    const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+    const float* con = a.conics + (int64_t)g * 3;
+    const float* col = a.colors + (int64_t)g * CH;
+    float cc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < CH; ++c) cc[c] = __ldg(col + c);
+    sa[slot] = make_float4(m.x, m.y, __ldg(con), __ldg(con + 1));
+    sb[slot] = make_float4(__ldg(con + 2), __ldg(a.opacities + g), cc[0], cc[1]);
+    sc[slot] = make_float2(cc[2], cc[3]);
+    sidx[slot] = idx;
+    if (sgid) sgid[slot] = g;
+  }
+  __syncthreads();
+  return cnt;
+}
+
+template <int CH>
+__device__ __forceinline__ void composite16(float dx, float dy, const float4& A, const float4& B,
+                                            const float* col, float& Tr, float* acc, int& cur,
+                                            bool& done, int idx) {
+  const float sigma = 0.5f * (A.z * dx * dx + B.x * dy * dy) + A.w * dx * dy;
+  const float alpha = fminf(kMaxAlpha, B.y * __expf(-sigma));
+  if (sigma < 0.0f || alpha < kAlphaThreshold) return;
+  const float next_T = Tr * (1.0f - alpha);
+  if (next_T <= kTransmittanceThreshold) {
+    done = true;
+    return;
+  }
+  const float vis = alpha * Tr;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc[c] += col[c] * vis;
+  cur = idx;
+  Tr = next_T;
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kT16Threads, 10) raster_fwd16_kernel(
+    RArgs a, float* __restrict__ render_colors, float* __restrict__ render_alphas,
+    int32_t* __restrict__ last_ids) {
+  __shared__ float4 s_a[kT16Threads];
+  __shared__ float4 s_b[kT16Threads];
+  __shared__ float2 s_c[kT16Threads];
+  __shared__ int s_idx[kT16Threads];
+  __shared__ int s_wcnt[kT16Threads / 32];
+  const int64_t tile = blockIdx.x;
+  const int T = a.tw * a.th;
+  const int image = (int)(tile / T);
+  const int t = (int)(tile - (int64_t)image * T);
+  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const int tid = threadIdx.x;
+  const int x = tile_x * 16 + (tid & 15);
+  const int y0 = tile_y * 16 + (tid >> 4), y1 = y0 + 8;
+  const bool in0 = x < a.W && y0 < a.H, in1 = x < a.W && y1 < a.H;
+  const int64_t pix0 = ((int64_t)image * a.H + y0) * a.W + x;
+  const int64_t pix1 = pix0 + 8 * (int64_t)a.W;
+
+  if (a.masks && !a.masks[tile]) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (!(q ? in1 : in0)) continue;
+      const int64_t pix = q ? pix1 : pix0;
+#pragma unroll
+      for (int c = 0; c < CH; ++c)
+        render_colors[pix * CH + c] = a.backgrounds ? __ldg(a.backgrounds + image * CH + c) : 0.0f;
+      render_alphas[pix] = 0.0f;
+      last_ids[pix] = 0;
+    }
+    return;
+  }
+  int start, end;
+  tile_range(a, tile, start, end);
+  const float px = (float)x + 0.5f, py0 = (float)y0 + 0.5f, py1 = (float)y1 + 0.5f;
+  float T0 = 1.0f, T1 = 1.0f;
+  int cur0 = 0, cur1 = 0;
+  bool d0 = !in0, d1 = !in1;
+  float acc0[CH], acc1[CH];
+#pragma unroll
+  for (int c = 0; c < CH; ++c) acc0[c] = acc1[c] = 0.0f;
+
+  for (int b0 = start; b0 < end; b0 += kT16Threads) {
+    if (__syncthreads_count(!(d0 && d1)) == 0) break;
+    const int cnt = stage16<CH>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
+                                s_c, s_idx, nullptr, s_wcnt);
+    for (int j = 0; j < cnt; ++j) {
+      if (d0 && d1) break;
+      const float4 A = s_a[j];
+      const float4 B = s_b[j];
+      float col[4] = {B.z, B.w, 0.0f, 0.0f};
+      if (CH > 2) {
+        const float2 C = s_c[j];
+        col[2] = C.x;
+        col[3] = C.y;
+      }
+      const float dx = A.x - px;
+      const int idx = s_idx[j];
+      if (!d0) composite16<CH>(dx, A.y - py0, A, B, col, T0, acc0, cur0, d0, idx);
+      if (!d1) composite16<CH>(dx, A.y - py1, A, B, col, T1, acc1, cur1, d1, idx);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    if (!(q ? in1 : in0)) continue;
+    const int64_t pix = q ? pix1 : pix0;
+    const float Tr = q ? T1 : T0;
+    render_alphas[pix] = 1.0f - Tr;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const float bg = a.backgrounds ? __ldg(a.backgrounds + image * CH + c) : 0.0f;
+      render_colors[pix * CH + c] = (q ? acc1[c] : acc0[c]) + Tr * bg;
+    }
+    last_ids[pix] = q ? cur1 : cur0;
+  }
+}
+
+// Reverse step of one pixel for one Gaussian (gsplat_rasterize.cpp:503-562);
+// adds the pixel's contributions to the Gaussian's gradient terms g[].
+template <int CH>
+__device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, const float4& A,
+                                           const float4& B, const float* col, float T_final,
+                                           float& Tr, float* buf, const float* v_rc, float v_ra,
+                                           float bg_dot, bool has_bg, float* g) {
+  if (!in_range) return false;
+  const float sigma = 0.5f * (A.z * dx * dx + B.x * dy * dy) + A.w * dx * dy;
+  const float vis = __expf(-sigma);
+  const float alpha = fminf(kMaxAlpha, B.y * vis);
+  if (sigma < 0.0f || alpha < kAlphaThreshold) return false;
+  const float ra = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
+  Tr *= ra;
+  const float fac = alpha * Tr;
+  float v_alpha = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    g[8 + c] += fac * v_rc[c];
+    v_alpha += (col[c] * Tr - buf[c] * ra) * v_rc[c];
+    buf[c] += col[c] * fac;
+  }
+  v_alpha += T_final * ra * v_ra;
+  if (has_bg) v_alpha += -T_final * ra * bg_dot;
+  if (B.y * vis <= kMaxAlpha) {
+    const float v_sigma = -B.y * vis * v_alpha;
+    const float vx = v_sigma * (A.z * dx + A.w * dy);
+    const float vy = v_sigma * (A.w * dx + B.x * dy);
+    g[0] += vx;
+    g[1] += vy;
+    g[2] += 0.5f * v_sigma * dx * dx;
+    g[3] += v_sigma * dx * dy;
+    g[4] += 0.5f * v_sigma * dy * dy;
+    g[5] += vis * v_alpha;
+    g[6] += fabsf(vx);
+    g[7] += fabsf(vy);
+  }
+  return true;
+}
+
+template <int CH>
+__global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
+    RArgs a, const float* __restrict__ render_alphas, const int32_t* __restrict__ last_ids,
+    const float* __restrict__ v_render_colors, const float* __restrict__ v_render_alphas,
+    int absgrad, float* __restrict__ v_means2d_abs, float* __restrict__ v_means2d,
+    float* __restrict__ v_conics, float* __restrict__ v_colors, float* __restrict__ v_opacities,
+    float* __restrict__ v_backgrounds) {
+  constexpr int NT = 8 + CH;
+  __shared__ float4 s_a[kT16Threads];
+  __shared__ float4 s_b[kT16Threads];
+  __shared__ float2 s_c[kT16Threads];
+  __shared__ int s_idx[kT16Threads];
+  __shared__ int s_gid[kT16Threads];
+  __shared__ int s_wcnt[kT16Threads / 32];
+  __shared__ float s_acc[kT16Threads * NT];
+  __shared__ int s_last;
+  __shared__ float s_bg[4];
+  const int64_t tile = blockIdx.x;
+  const int T = a.tw * a.th;
+  const int image = (int)(tile / T);
+  const int t = (int)(tile - (int64_t)image * T);
+  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int x = tile_x * 16 + (tid & 15);
+  const int y0 = tile_y * 16 + (tid >> 4), y1 = y0 + 8;
+  const bool in0 = x < a.W && y0 < a.H, in1 = x < a.W && y1 < a.H;
+  const int64_t pix0 = ((int64_t)image * a.H + y0) * a.W + x;
+  const int64_t pix1 = pix0 + 8 * (int64_t)a.W;
+  if (a.masks && !a.masks[tile]) return;
+  int start, end;
+  tile_range(a, tile, start, end);
+  const float px = (float)x + 0.5f, py0 = (float)y0 + 0.5f, py1 = (float)y1 + 0.5f;
+  const float Tf0 = in0 ? 1.0f - __ldg(render_alphas + pix0) : 1.0f;
+  const float Tf1 = in1 ? 1.0f - __ldg(render_alphas + pix1) : 1.0f;
+  float T0 = Tf0, T1 = Tf1;
+  const int last0 = in0 ? min(end - 1, __ldg(last_ids + pix0)) : -1;
+  const int last1 = in1 ? min(end - 1, __ldg(last_ids + pix1)) : -1;
+  const float vra0 = in0 ? __ldg(v_render_alphas + pix0) : 0.0f;
+  const float vra1 = in1 ? __ldg(v_render_alphas + pix1) : 0.0f;
+  float vrc0[CH], vrc1[CH], buf0[CH], buf1[CH];
+  float bgd0 = 0.0f, bgd1 = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    vrc0[c] = in0 ? __ldg(v_render_colors + pix0 * CH + c) : 0.0f;
+    vrc1[c] = in1 ? __ldg(v_render_colors + pix1 * CH + c) : 0.0f;
+    buf0[c] = buf1[c] = 0.0f;
+    if (a.backgrounds) {
+      const float bg = __ldg(a.backgrounds + image * CH + c);
+      bgd0 += bg * vrc0[c];
+      bgd1 += bg * vrc1[c];
+    }
+  }
+  const bool has_bg = a.backgrounds != nullptr;
+  if (tid < 4) s_bg[tid] = 0.0f;
+  if (tid == 0) s_last = -1;
+  __syncthreads();
+  if (v_backgrounds) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const float v = warp_sum((in0 ? Tf0 * vrc0[c] : 0.0f) + (in1 ? Tf1 * vrc1[c] : 0.0f));
+      if (lane == 0) atomicAdd(&s_bg[c], v);
+    }
+  }
+  if (in0 || in1) atomicMax(&s_last, max(last0, last1));
+  __syncthreads();
+  if (v_backgrounds && tid < CH && s_bg[tid] != 0.0f)
+    atomicAdd(v_backgrounds + image * CH + tid, s_bg[tid]);
+  const int cta_last = s_last;
+
+  for (int b_end = cta_last + 1; b_end > start; b_end -= kT16Threads) {
+    const int b0 = max(start, b_end - kT16Threads);
+    __syncthreads();
+    const int cnt = stage16<CH>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
+                                s_c, s_idx, s_gid, s_wcnt);
+    for (int i = tid; i < cnt * NT; i += kT16Threads) s_acc[i] = 0.0f;
+    __syncthreads();
+    for (int j = cnt - 1; j >= 0; --j) {
+      const int idx = s_idx[j];
+      const float4 A = s_a[j];
+      const float4 B = s_b[j];
+      float col[4] = {B.z, B.w, 0.0f, 0.0f};
+      if (CH > 2) {
+        const float2 C = s_c[j];
+        col[2] = C.x;
+        col[3] = C.y;
+      }
+      float g[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) g[i] = 0.0f;
+      const float dx = A.x - px;
+      const bool v0 = backward16<CH>(idx <= last0, dx, A.y - py0, A, B, col, Tf0, T0, buf0, vrc0,
+                                     vra0, bgd0, has_bg, g);
+      const bool v1 = backward16<CH>(idx <= last1, dx, A.y - py1, A, B, col, Tf1, T1, buf1, vrc1,
+                                     vra1, bgd1, has_bg, g);
+      const unsigned active = __ballot_sync(0xffffffffu, v0 || v1);
+      if (!active) continue;
+      if (__popc(active) <= 2) {
+        // Sparse warp: its one or two contributing lanes add directly.
+        if (v0 || v1) {
+#pragma unroll
+          for (int k = 0; k < NT; ++k)
+            if (g[k] != 0.0f) atomicAdd(&s_acc[j * NT + k], g[k]);
+        }
+      } else {
+        const float r = butterfly_reduce<16>(g, lane);
+        const int ri = red_index(lane);
+        if ((lane & 1) == 0 && ri < NT && r != 0.0f) atomicAdd(&s_acc[j * NT + ri], r);
+      }
+    }
+    __syncthreads();
+    for (int i = tid; i < cnt * NT; i += kT16Threads) {
+      const float v = s_acc[i];
+      if (v == 0.0f) continue;
+      const int j = i / NT, k = i - j * NT;
+      const int64_t gg = s_gid[j];
+      if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
+      else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
+      else if (k == 5) atomicAdd(v_opacities + gg, v);
+      else if (k < 8) {
+        if (absgrad) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);
+      } else atomicAdd(v_colors + gg * CH + (k - 8), v);
+    }
+  }
+}
+
 int smem_bytes(int block, int ch, bool bwd) {
   return (int)sizeof(float) * (block * (6 + ch) + (bwd ? block * (8 + ch) : 0));
 }
 
 template <int CH>
 int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cudaStream_t s) {
+  if (CH > 0 && a.ts == 16) {
+    raster_fwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.tw * a.th), kT16Threads, 0, s>>>(
+        a, rc, ra, li);
+    return launch_status("rasterize_fwd");
+  }
   const int smem = smem_bytes(block, a.CH, false);
   cudaFuncSetAttribute(raster_fwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int64_t tiles = (int64_t)a.I * a.tw * a.th;
@@ -384,6 +746,11 @@ template <int CH>
 int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, const float* vrc,
                const float* vra, int absgrad, float* vabs, float* vm, float* vc, float* vcol,
                float* vop, float* vbg, cudaStream_t s) {
+  if (CH > 0 && a.ts == 16) {
+    raster_bwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.tw * a.th), kT16Threads, 0, s>>>(
+        a, ra, li, vrc, vra, absgrad, vabs, vm, vc, vcol, vop, vbg);
+    return launch_status("rasterize_bwd");
+  }
   const int smem = smem_bytes(block, a.CH, true);
   cudaFuncSetAttribute(raster_bwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int64_t tiles = (int64_t)a.I * a.tw * a.th;

@@ -401,10 +401,21 @@ __device__ __forceinline__ void ws_load_block(const float* __restrict__ g, int64
   const int total = cnt * R;
   int row = 0, col = lane;
   while (col >= R) { col -= R; ++row; }
-  for (int f = lane; f < total; f += 32) {
-    sm[row * S + col] = __ldg(src + f);
-    col += 32;
-    while (col >= R) { col -= R; ++row; }
+  // eight loads in flight per lane before their stores
+  for (int f0 = 0; f0 < total; f0 += 32 * 8) {
+    float v[8];
+    int pos[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int f = f0 + lane + 32 * q;
+      pos[q] = row * S + col;
+      v[q] = f < total ? __ldg(src + f) : 0.0f;
+      col += 32;
+      while (col >= R) { col -= R; ++row; }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (f0 + lane + 32 * q < total) sm[pos[q]] = v[q];
   }
 }
 
@@ -414,11 +425,34 @@ __device__ __forceinline__ void ws_load_rows(const float* __restrict__ g, int64_
     ws_load_block(g, e0, cnt, R, S, sm, lane);
     return;
   }
+  // Eight rows per round, every load of the round issued before any store,
+  // so that a warp keeps up to 24 row loads in flight instead of one.
+  constexpr int kRows = 8;
   while (need) {
-    const int r = __ffs(need) - 1;
-    need &= need - 1;
-    const float* src = g + (e0 + r) * R;
-    for (int c = lane; c < R; c += 32) sm[r * S + c] = __ldg(src + c);
+    int rr[kRows];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      rr[q] = need ? __ffs(need) - 1 : -1;
+      need &= need - 1;
+    }
+    float v[kRows][3];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+      const float* src = g + (e0 + (rr[q] < 0 ? 0 : rr[q])) * R;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int c = lane + 32 * k;
+        v[q][k] = (rr[q] >= 0 && c < R) ? __ldg(src + c) : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int c = lane + 32 * k;
+        if (rr[q] >= 0 && c < R) sm[rr[q] * S + c] = v[q][k];
+      }
+    }
   }
 }
 

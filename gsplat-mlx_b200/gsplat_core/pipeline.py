@@ -138,9 +138,14 @@ class TrainingStep:
             self.events.append((name, ev))
 
     def run(self, means, quats, scales, opacities, coeffs, viewmats, Ks, v_render_colors,
-            v_render_alphas):
+            v_render_alphas, sh_backward=True):
         """Forward and backward; returns the flat gradient buffer (a view of
-        self.grad_flat) and the intersection count of this step."""
+        self.grad_flat) and the intersection count of this step.
+
+        With ``sh_backward=False`` the SH colour glue backward is left to the
+        caller: v_coeffs is not written and v_means holds the projection part
+        only, while ``self.v_colors`` holds the colour cotangents (the camera-
+        sharded step exchanges those instead of the SH gradients)."""
         L, s = self.lib, _s()
         C, N = self.C, self.N
         self._mark("start")
@@ -207,6 +212,8 @@ class TrainingStep:
                                   _p(self.v_means), None, _p(self.v_quats), _p(self.v_scales),
                                   None, s), "projection_bwd")
         self._mark("projection_bwd")
+        if not sh_backward:
+            return self.grad_flat, m
         check(L.gs_sh_glue_bwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
                                _p(self.radii), _p(self.v_colors), _p(self.v_means),
                                _p(self.v_coeffs), s), "sh_glue_bwd")

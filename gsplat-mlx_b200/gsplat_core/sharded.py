@@ -1,0 +1,149 @@
+"""Camera-sharded multi-view training step, one process per GPU.
+
+Every (camera, Gaussian) pair, tile and pixel of the hot path is
+independent; the only coupling between cameras is the per-Gaussian gradient
+sum that the reference's projection backward forms by looping over the
+cameras (metal/gsplat_projection.metal:488-545) and that MLX autograd forms
+over the trainers' camera loop.  So each rank holds the full Gaussian set,
+renders its own contiguous slice of the cameras with ``TrainingStep``, and
+the ranks exchange gradients once per step.  Two exchanges give the same
+sums (up to fp32 summation order):
+
+* ``"allreduce"`` -- every rank runs the whole backward for its cameras and
+  one all-reduce(sum) runs over the flat gradient buffer
+  ``[v_means | v_quats | v_scales | v_opacities | v_coeffs]`` (4 (11 + 3K)
+  bytes per Gaussian: 236 B at SH degree 3).
+* ``"gather"`` -- the SH gradient is a sum over cameras of the colour
+  cotangent times a basis that any rank can recompute from the replicated
+  means, coefficients and camera poses.  Ranks all-gather the colour
+  cotangents ``v_colors`` of their cameras (12 B per Gaussian per camera)
+  and all-reduce only the projection part ``[v_means | v_quats | v_scales |
+  v_opacities]`` (44 B per Gaussian); each rank then runs the SH glue
+  backward over all cameras, which writes the full v_coeffs and adds the
+  SH part of v_means.
+
+``"auto"`` picks the exchange that moves fewer bytes per rank (ring
+estimates in ``exchange_bytes``): at SH degree 3 gather wins up to 3
+cameras per rank on 8 ranks and up to 16 on 2.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def camera_shard(cameras, world, rank):
+    """Contiguous, balanced camera slice [start, stop) of ``rank``; the
+    first ``cameras % world`` ranks take one camera more."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    base, extra = divmod(int(cameras), int(world))
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def exchange_bytes(mode, n, K, cameras_per_rank, world):
+    """Bytes each rank sends per step for an exchange (ring algorithms:
+    all-reduce 2 (w-1)/w S, all-gather (w-1) S_rank)."""
+    if world <= 1:
+        return 0.0
+    ring = 2.0 * (world - 1) / world
+    if mode == "allreduce":
+        return ring * 4.0 * (11 + 3 * K) * n
+    if mode == "gather":
+        return ring * 44.0 * n + (world - 1) * 12.0 * n * cameras_per_rank
+    raise ValueError(f"unknown exchange {mode!r}")
+
+
+def choose_exchange(n, K, cameras_per_rank, world):
+    if world <= 1:
+        return "allreduce"
+    ar = exchange_bytes("allreduce", n, K, cameras_per_rank, world)
+    ga = exchange_bytes("gather", n, K, cameras_per_rank, world)
+    return "gather" if ga < ar else "allreduce"
+
+
+def _all_gather(out, inp, group):
+    """all-gather of equal-size contiguous shards into ``out`` (rank-major)."""
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, inp, group=group)
+    else:  # gloo has no all_gather_into_tensor
+        dist.all_gather(list(out.chunk(dist.get_world_size(group))), inp, group=group)
+
+
+def exchange_gradients(mode, grad_flat, n, v_colors_local, v_colors_all, sh_backward, group=None):
+    """Sum the per-Gaussian gradients of all ranks into ``grad_flat``.
+
+    mode "allreduce": ``grad_flat`` already holds this rank's complete
+    gradients; one all-reduce.  mode "gather": ``grad_flat`` holds the
+    projection part (v_means without its SH part, v_quats, v_scales,
+    v_opacities) and ``v_colors_local`` [C_local, N, 3] the colour
+    cotangents; after the gather ``sh_backward(v_colors_all)`` must write
+    v_coeffs and add the SH part of v_means for all cameras."""
+    if mode == "allreduce":
+        dist.all_reduce(grad_flat, group=group)
+        return
+    if mode != "gather":
+        raise ValueError(f"unknown exchange {mode!r}")
+    _all_gather(v_colors_all.view(-1), v_colors_local.reshape(-1), group)
+    dist.all_reduce(grad_flat[:11 * n], group=group)
+    sh_backward(v_colors_all)
+
+
+class ShardedTrainingStep:
+    """One camera-sharded fwd+bwd step of C_total cameras over the process
+    group: this rank renders ``cameras[start:stop]`` and, after the
+    exchange, holds the gradient summed over every camera.  All ranks must
+    have the same number of cameras (C_total divisible by the world size)."""
+
+    def __init__(self, n, sh_degree, K, cameras_total, width, height, group=None, exchange="auto",
+                 **step_kw):
+        from .pipeline import TrainingStep
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if cameras_total % self.world:
+            raise ValueError(f"{cameras_total} cameras do not split evenly over "
+                             f"{self.world} ranks")
+        self.C_total = int(cameras_total)
+        self.start, self.stop = camera_shard(cameras_total, self.world, self.rank)
+        self.C = self.stop - self.start
+        self.N, self.K, self.deg = int(n), int(K), int(sh_degree)
+        self.step = TrainingStep(n, sh_degree, K, self.C, width, height, **step_kw)
+        self.exchange = (choose_exchange(self.N, self.K, self.C, self.world)
+                         if exchange == "auto" else exchange)
+        if self.exchange not in ("allreduce", "gather"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.v_colors_all = None
+        if self.exchange == "gather" and self.world > 1:
+            self.v_colors_all = torch.empty((self.C_total, self.N, 3), dtype=torch.float32,
+                                            device=self.step.dev)
+
+    def local(self, t):
+        """This rank's slice of a per-camera tensor [C_total, ...]."""
+        return t[self.start:self.stop]
+
+    def run(self, means, quats, scales, opacities, coeffs, viewmats_all, Ks_all,
+            v_render_colors, v_render_alphas):
+        """``viewmats_all`` / ``Ks_all``: every camera [C_total, 4|3, 4|3];
+        ``v_render_*``: this rank's cotangents [C_local, H, W, 3|1].
+        Returns (grad_flat summed over all cameras, local intersections)."""
+        from .pipeline import sh_colors_backward
+        st = self.step
+        gather = self.exchange == "gather" and self.world > 1
+        flat, m = st.run(means, quats, scales, opacities, coeffs, self.local(viewmats_all),
+                         self.local(Ks_all), v_render_colors, v_render_alphas,
+                         sh_backward=not gather)
+        if self.world == 1:
+            return flat, m
+
+        def sh_bwd(v_all):
+            sh_colors_backward(self.deg, means, viewmats_all, coeffs, None, v_all, st.v_means,
+                               radii=None, v_coeffs=st.v_coeffs)
+
+        exchange_gradients("gather" if gather else "allreduce", flat, self.N, st.v_colors,
+                           self.v_colors_all, sh_bwd, self.group)
+        return flat, m
+
+    def gradients(self):
+        return self.step.gradients()

@@ -63,7 +63,9 @@ def test_autograd_chain_matches_training_step(gs, cuda):
     torch.cuda.synchronize()
     g = step.gradients()
     for name, t in zip(("v_means", "v_quats", "v_scales", "v_opacities", "v_coeffs"), p):
-        assert_grad_close(t.grad, g[name], "autograd " + name, atol_frac=1e-4)
+        # two GPU runs differ only by atomic order; heavy cancellation in a
+        # few entries needs the wider absolute floor
+        assert_grad_close(t.grad, g[name], "autograd " + name, atol_frac=5e-4)
     # viewspace_points receives the means2d cotangent unchanged (cpp:1200-1201)
     assert_grad_close(vsp.grad.view(-1, 2), step.v_means2d.view(-1, 2), "viewspace proxy",
                       atol_frac=1e-6)

@@ -448,3 +448,65 @@ def test_rasterize_masks_backward(gs, oracle, golden, cuda):
                            last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra, **inp)
     for k, v in eb.items():
         assert_grad_close(b[k], v, "masked " + k, atol_frac=1e-4)
+
+
+def test_rasterize_tile_cull_boundary(gs, oracle, cuda):
+    """The 16x16 rasterizer drops a Gaussian from a tile only when no pixel
+    centre of the tile can reach alpha >= 1/255.  Gaussians tuned to peak
+    just above / below the threshold inside the tile (thin, rotated, far
+    outside and inside it), one per 16x16 image, must render exactly as the
+    oracle renders them."""
+    rng = np.random.default_rng(21)
+    thr = 1.0 / 255.0
+    px = np.arange(16) + 0.5
+    means, conics, opac, above = [], [], [], []
+    while len(means) < 3000:
+        th = rng.uniform(0, np.pi)
+        s1 = np.exp(rng.uniform(np.log(0.3), np.log(25.0)))
+        s2 = s1 / np.exp(rng.uniform(0, np.log(60.0)))
+        R = np.array([[np.cos(th), -np.sin(th)], [np.sin(th), np.cos(th)]])
+        cov = R @ np.diag([s1 * s1, s2 * s2]) @ R.T
+        inv = np.linalg.inv(cov)
+        a, b, c = inv[0, 0], inv[0, 1], inv[1, 1]
+        m = rng.uniform(-40, 56, size=2)
+        dx = m[0] - px[None, :]
+        dy = m[1] - px[:, None]
+        smin = (0.5 * (a * dx * dx + c * dy * dy) + b * dx * dy).min()
+        d = rng.uniform(2e-3, 0.1) * (1 if rng.uniform() < 0.5 else -1)
+        if smin > 5.4:
+            continue
+        o = thr * (1 + d) * np.exp(smin)
+        if o > 0.9:
+            continue
+        means.append(m)
+        conics.append([a, b, c])
+        opac.append(o)
+        above.append(d > 0)
+    I = len(means)
+    inp = dict(means2d=np.array(means, np.float32).reshape(I, 1, 2),
+               conics=np.array(conics, np.float32).reshape(I, 1, 3),
+               colors=rng.uniform(0, 1, size=(I, 1, 3)).astype(np.float32),
+               opacities=np.array(opac, np.float32).reshape(I, 1),
+               tile_offsets=np.arange(I, dtype=np.int32).reshape(I, 1, 1),
+               flatten_ids=np.arange(I, dtype=np.int32))
+    e = oracle.raster_fwd(width=16, height=16, tile_size=16, **inp)
+    g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, 16, 16, 16)
+    near = e["near_threshold"]
+    ok = ~near
+    assert_exact(to_np(g["last_ids"])[ok], e["last_ids"][ok], "last_ids")
+    ga = to_np(g["render_alphas"])[..., 0]
+    assert_fwd_close(ga[ok], e["render_alphas"][..., 0][ok], "alphas")
+    hit = ga.reshape(I, -1).max(1) > 0
+    assert np.array_equal(hit, np.array(above)), "a Gaussian reaching the threshold was dropped"
+    vrc = rng.normal(size=e["render_colors"].shape).astype(np.float32)
+    vra = rng.normal(0, 0.1, size=e["render_alphas"].shape).astype(np.float32)
+    vrc[near] = 0
+    vra[near] = 0
+    b = gs.rasterize_to_pixels_3dgs_backward(
+        {k: T(v) for k, v in inp.items()},
+        {"render_alphas": T(e["render_alphas"]), "last_ids": T(e["last_ids"])},
+        {"v_render_colors": T(vrc), "v_render_alphas": T(vra)}, 16, 16, 16)
+    eb = oracle.raster_bwd(width=16, height=16, tile_size=16, render_alphas=e["render_alphas"],
+                           last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra, **inp)
+    for k, v in eb.items():
+        assert_grad_close(b[k], v, f"cull {k}", atol_frac=1e-4)

@@ -1,0 +1,89 @@
+"""Camera-sharded step on two GPUs (NCCL): both gradient exchanges give the
+gradients of one single-GPU TrainingStep over all cameras.  Skipped where
+fewer than two GPUs are visible."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _scene():
+    from gsplat_core import synthetic as S
+    sc = S.config3(seed=4, n=200_000)
+    C = 4
+    sc.viewmats = S.orbit(C, 4.0)
+    sc.Ks = np.repeat(sc.Ks[:1], C, 0).copy()
+    sc.Ks[:, :2, :] /= 2
+    sc.width, sc.height = sc.width // 2, sc.height // 2
+    vrc, vra = S.cotangents(6, C, sc.height, sc.width)
+    return sc, vrc, vra
+
+
+def _args(sc, dev, torch):
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)  # noqa: E731
+    return [T(sc.means), T(sc.quats), T(sc.scales), T(sc.opacities), T(sc.coeffs),
+            T(sc.viewmats), T(sc.Ks)]
+
+
+def _worker(rank, world, port, mode, out_dir):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from gsplat_core.sharded import ShardedTrainingStep
+        sc, vrc, vra = _scene()
+        st = ShardedTrainingStep(sc.n, 3, 16, sc.cameras, sc.width, sc.height, exchange=mode,
+                                 device=dev)
+        args = _args(sc, dev, torch)
+        T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)  # noqa: E731
+        flat, _ = st.run(*args, T(st.local(vrc)), T(st.local(vra)))
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"{mode}_{rank}.npy"), flat.cpu().numpy())
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["allreduce", "gather"])
+def test_two_gpu_exchange_matches_single_gpu(gs, cuda, tmp_path, mode):
+    import torch
+    import torch.multiprocessing as mp
+    from _util import assert_grad_close
+    from gsplat_core import pipeline
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    sc, vrc, vra = _scene()
+    step = pipeline.TrainingStep(sc.n, 3, 16, sc.cameras, sc.width, sc.height)
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    flat, _ = step.run(*_args(sc, torch.device("cuda", 0), torch), T(vrc), T(vra))
+    expect = flat.cpu().numpy()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank did not finish")
+        assert p.exitcode == 0
+    outs = [np.load(tmp_path / f"{mode}_{r}.npy") for r in range(2)]
+    np.testing.assert_array_equal(outs[0], outs[1])
+    n = sc.n
+    for name, a, b in (("v_means", 0, 3 * n), ("v_quats", 3 * n, 7 * n),
+                       ("v_scales", 7 * n, 10 * n), ("v_opacities", 10 * n, 11 * n),
+                       ("v_coeffs", 11 * n, expect.size)):
+        assert_grad_close(outs[0][a:b], expect[a:b], f"{mode} {name}", atol_frac=1e-4)
