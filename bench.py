@@ -39,6 +39,11 @@ METRIC = "fwd+bwd ms/step and Mpix/s at 1M Gaussians SH3; intersections sorted/s
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # measured peer copy per direction per GPU on this pool (NVLink 5; 900 nominal)
 LINK_GBS = 770.0
+# DRAM bytes (read + write) per launch of each stage's dominant kernel from
+# one ncu capture of this benchmark (profiles/*_config3.md); None = not
+# captured.  Valid for the config-3 workload only.
+PROFILED_TRAFFIC = {"rasterize_bwd": 44.4e6 + 0.2e6, "rasterize_fwd": 18.2e6 + 0.02e6,
+                    "sh_bwd": 118.2e6 + 147.7e6}
 
 
 def load_peaks():
@@ -122,15 +127,19 @@ class ClockSampler:
 # ------------------------------------------------------------------ helpers
 
 def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
-    """Bytes each stage must move at minimum (the roofline convention)."""
+    """Bytes each stage must move at minimum (the roofline convention).
+    ``sort_passes``: radix passes over the tile and image bits of the keys
+    (the depth word is ordered per element, 4 passes over the N elements)."""
     return {
         # means/quats/scales in (40 B), 2D outputs out (36 B) per Gaussian
         "projection_fwd": n * (40 + 36),
         # means + campos in, colours out for all; coefficient rows of visible
         "sh_fwd": n * (12 + 8 + 12) + visible * K * 12,
         "isect_count_scan": n * (16 + 4) + n * 8,
-        "isect_encode": n * 24 + m * 12,
-        "isect_sort": m * 24 * sort_passes,
+        # depth keys (4 B in, 12 out), 4 element passes at 24 B, permuted scan
+        # (12 B), encode (24 B per element, 12 B per intersection out), then
+        # 24 B per intersection per tile/image pass
+        "isect_encode_sort": n * (16 + 4 * 24 + 12 + 24) + m * 12 + m * 24 * sort_passes,
         "isect_offset": m * 8,
         # per intersection: flatten id + Gaussian record; per pixel: outputs
         "rasterize_fwd": m * 40 + pixels * 20,
@@ -141,10 +150,11 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
 
 
 def our_kernel_launches(sort_passes):
-    # projection fwd 1, glue fwd 1, count 1, scan 3, encode 1,
-    # sort passes x (upsweep + rowscan + downsweep), offset 1,
-    # rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
-    return 1 + 1 + 1 + 3 + 1 + sort_passes * 3 + 1 + 1 + 1 + 1 + 1
+    # projection fwd 1, glue fwd 1, count 1, scan 3, depth keys 1, element
+    # sort 4 x (upsweep + rowscan + downsweep), permuted scan 3, encode 1,
+    # tile/image passes x 3, offset 1, rasterize fwd 1, rasterize bwd 1,
+    # projection bwd 1, glue bwd 1
+    return 1 + 1 + 1 + 3 + 1 + 4 * 3 + 3 + 1 + sort_passes * 3 + 1 + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -153,7 +163,8 @@ def cpu_step(checker, sc, vrc, vra, stride):
     """One reference-CPU step on a bounded sample: projection, SH colours
     and the intersection pipeline over all Gaussians; rasterize fwd+bwd on
     every `stride`-th tile (tile masks), with the raster time scaled by
-    `stride`.  Returns (seconds, extrapolated seconds, intersections)."""
+    `stride`.  Returns (seconds, extrapolated seconds, intersections,
+    seconds of the intersect encode + sort)."""
     t0 = time.perf_counter()
     p = checker.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
                          quats=sc.quats[None], scales=sc.scales[None])
@@ -162,8 +173,10 @@ def cpu_step(checker, sc, vrc, vra, stride):
     dirs /= np.maximum(np.linalg.norm(dirs, axis=-1, keepdims=True), 1e-8)
     colors = np.clip(checker.sh_fwd(sc.sh_degree, dirs, sc.coeffs) + 0.5, 0, 1)[None]
     m2 = p["means2d"].reshape(1, -1, 2)
+    ti = time.perf_counter()
     it = checker.isect_tile(m2, p["radii"].reshape(1, -1, 2), p["depths"].reshape(1, -1), 1,
                             sc.tile_size, sc.tile_width, sc.tile_height)
+    t_isect = time.perf_counter() - ti
     offs = checker.isect_offset(it["isect_ids"], 1, sc.tile_width, sc.tile_height)
     t1 = time.perf_counter()
     masks = np.zeros((1, sc.tile_height, sc.tile_width), bool)
@@ -182,7 +195,7 @@ def cpu_step(checker, sc, vrc, vra, stride):
                      quats=sc.quats[None], scales=sc.scales[None])
     t3 = time.perf_counter()
     full = (t1 - t0) + (t2 - t1) * stride + (t3 - t2)
-    return t3 - t0, full, int(it["isect_ids"].size)
+    return t3 - t0, full, int(it["isect_ids"].size), t_isect
 
 
 def make_checker():
@@ -205,10 +218,12 @@ def run_reference_arm(args):
     for _ in range(args.warmup):
         cpu_step(checker, sc, vrc, vra, stride)
     fulls = []
+    isects = []
     m = 0
     for _ in range(args.steps):
-        _, full, m = cpu_step(checker, sc, vrc, vra, stride)
+        _, full, m, t_isect = cpu_step(checker, sc, vrc, vra, stride)
         fulls.append(full)
+        isects.append(t_isect)
     ms = 1e3 * float(np.mean(fulls))
     pixels = sc.width * sc.height
     value = pixels / (ms / 1e3) / 1e6
@@ -221,7 +236,7 @@ def run_reference_arm(args):
            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 3 shapes)",
            "config": {"workload": "cfg3: N=1M SH3, 1 camera 1297x840, tile 16",
                       "gaussians": sc.n, "isects": m},
-           "intersections_sorted_per_s": round(m / (ms / 1e3), 1),
+           "intersections_sorted_per_s": round(m / float(np.mean(isects)), 1),
            "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": 1,
                             "kind": kind, "sample": sample},
            "e2e": {"value": round(value, 4), "unit": "Mpix/s", "h2d_bytes_per_step": 0,
@@ -312,27 +327,63 @@ def run_ours(args):
     pixels = sc.width * sc.height * world
     value = pixels * args.steps / (total_ms / 1e3) / 1e6
 
-    # ---- e2e: host (pinned) inputs copied in, gradients copied out, each step
-    grad_host = torch.empty(step.grad_flat.shape, dtype=torch.float32).pin_memory()
+    # ---- e2e: the same step driven from pinned host buffers.  Every step
+    # uploads all of its inputs (Gaussian parameters, cameras, image
+    # cotangents) and downloads its whole flat gradient.  Uploads and
+    # downloads run on their own streams, double-buffered, so that step k+1's
+    # upload and step k's download overlap step k's kernels (PCIe is full
+    # duplex).  Timed on the device from the first upload to the last
+    # download; the inputs (253 MB) exceed L2, so no flush is added.
+    h2d_s = torch.cuda.Stream(device=dev)
+    d2h_s = torch.cuda.Stream(device=dev)
+    comp = torch.cuda.current_stream(dev)
+    bufs = [{k: torch.empty_like(d[k]) for k in order} for _ in range(2)]
+    stage = [torch.empty_like(step.grad_flat) for _ in range(2)]
+    grad_host = [torch.empty(step.grad_flat.shape, dtype=torch.float32).pin_memory()
+                 for _ in range(2)]
+    h2d_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    d2h_done = [torch.cuda.Event() for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in pinned.values())
-    d2h = grad_host.numel() * 4
-    e2e_ms = []
-    for i in range(args.warmup + args.steps):
-        flush.fill_(1.0)
+    d2h = grad_host[0].numel() * 4
+
+    def upload(k):
+        b = k % 2
+        if k >= 2:
+            h2d_s.wait_event(comp_done[b])      # step k-2 has consumed buffer b
+        with torch.cuda.stream(h2d_s):
+            for name in order:
+                bufs[b][name].copy_(pinned[name], non_blocking=True)
+        h2d_done[b].record(h2d_s)
+
+    def run_e2e(n_steps):
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        s_ev = torch.cuda.Event(enable_timing=True)
-        e_ev = torch.cuda.Event(enable_timing=True)
-        s_ev.record()
-        dev_in = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
-        one(dev_in)
-        grad_host.copy_(step.grad_flat, non_blocking=True)
-        e_ev.record()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(h2d_s)
+        upload(0)
+        for k in range(n_steps):
+            b = k % 2
+            if k + 1 < n_steps:
+                upload(k + 1)
+            comp.wait_event(h2d_done[b])
+            if k >= 2:
+                comp.wait_event(d2h_done[b])    # staging buffer b downloaded
+            one(bufs[b])
+            stage[b].copy_(step.grad_flat)
+            comp_done[b].record(comp)
+            d2h_s.wait_event(comp_done[b])
+            with torch.cuda.stream(d2h_s):
+                grad_host[b].copy_(stage[b], non_blocking=True)
+            d2h_done[b].record(d2h_s)
+        t1.record(d2h_s)
         torch.cuda.synchronize()
-        if i >= args.warmup:
-            e2e_ms.append(s_ev.elapsed_time(e_ev))
-    t = torch.tensor([float(np.sum(e2e_ms))], dtype=torch.float64, device=dev)
+        return t0.elapsed_time(t1)
+
+    run_e2e(args.warmup)
+    t = torch.tensor([run_e2e(args.steps)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = pixels * args.steps / (float(t.item()) / 1e3) / 1e6
@@ -342,7 +393,7 @@ def run_ours(args):
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
         visible = int(((step.radii[..., 0] > 0) & (step.radii[..., 1] > 0)).sum().item())
         K = sc.coeffs.shape[1]
-        passes = (step.key_bits + 7) // 8
+        passes = (step.key_bits - 32 + 7) // 8
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
         top = max((k for k in avg if k != "exchange"), key=avg.get)
         bytes_top = algorithmic_bytes(top, sc.n, visible, m, sc.width * sc.height, K, passes)
@@ -364,7 +415,7 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             checker, kind = make_checker()
             sc0 = scene_for(0, 1, args.seed)
-            _, full, _ = cpu_step(checker, sc0, vrc_np, vra_np, args.cpu_stride)
+            _, full, _, _ = cpu_step(checker, sc0, vrc_np, vra_np, args.cpu_stride)
             cpu = {"value": round(sc0.width * sc0.height / full / 1e6, 4), "unit": "Mpix/s",
                    "cores": 1, "kind": kind,
                    "sample": (f"one config-3 step; rasterize fwd+bwd on every "
@@ -380,15 +431,19 @@ def run_ours(args):
                        "parallelism": f"camera-sharded dp{world}" if world > 1 else "single",
                        "exchange": sharded.exchange if world > 1 else None,
                        "l2": "flushed (256 MB write) between timed steps"},
-            "intersections_sorted_per_s": round(m * world / (ms_step / 1e3), 1),
+            # M / (encode + sort) time of this rank's step
+            "intersections_sorted_per_s": round(m / (avg["isect_encode_sort"] / 1e3), 1),
             "stages_ms": stages,
             "roofline": {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "peak_source": peak_kind, "traffic": None,
+                         "peak_source": peak_kind, "traffic": PROFILED_TRAFFIC.get(top),
                          "algorithmic_bytes": int(bytes_top)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h)},
+                    "d2h_bytes_per_step": int(d2h),
+                    "how": "all inputs uploaded and the flat gradient downloaded every step "
+                           "from pinned host memory; copies double-buffered on their own "
+                           "streams, overlapping the neighbouring steps' kernels"},
             "gpu_launches": our_kernel_launches(passes) * args.steps,
             "clocks": clk,
         }

@@ -51,11 +51,15 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
 
 // One warp encodes 32 consecutive Gaussians at a time.  A warp scan of their
 // tile counts flattens the 32 runs into one index space j; lane l emits
-// entries j = l, l+32, ...: the owner Gaussian of j comes from a search over
-// the 32 prefix sums, its k-th tile in row-major order of its rect.  Runs
-// start at offsets[i] as in the reference (consecutive runs are adjacent
-// when offsets is the scan of the counts, so stores are coalesced); every
-// write is bounds-checked like the CPU path (gsplat_intersect.cpp:473).
+// entries j = l, l+32, ...: the owner Gaussian of j is the last one whose
+// run starts at or before j (found per 32-entry window from a bit mask of
+// the run starts), its k-th tile in row-major order of its rect.  Run i
+// starts at offsets[i] -- the reference's scan order (adjacent runs, so
+// stores are coalesced) or any other order of the runs; every write is
+// bounds-checked like the CPU path (gsplat_intersect.cpp:473).  With
+// `hist`, the kernel also counts the digits of the key bits above the depth
+// word for the radix passes that follow (hist[p][d], 8-bit digits from
+// bit 32).
 constexpr int kEncodeThreads = 256;
 constexpr int kEncodeWarps = kEncodeThreads / 32;
 
@@ -63,11 +67,18 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
     int64_t n, int n_per_image, const float* __restrict__ means2d,
     const int32_t* __restrict__ radii, const float* __restrict__ depths,
     const int32_t* __restrict__ offsets, int ts, int tw, int th, int tile_bits, int64_t n_isects,
-    int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids) {
-  __shared__ int s_pref[kEncodeWarps][33];
+    int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids,
+    uint32_t* __restrict__ hist, int hist_passes) {
+  __shared__ int s_pref[kEncodeWarps][32];
   __shared__ int s_x0[kEncodeWarps][32], s_y0[kEncodeWarps][32], s_w[kEncodeWarps][32];
+  __shared__ float s_invw[kEncodeWarps][32];
+  __shared__ int s_e[kEncodeWarps][32], s_start[kEncodeWarps][32];
   __shared__ int64_t s_off[kEncodeWarps][32], s_base[kEncodeWarps][32];
+  __shared__ uint32_t s_hist[4][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (hist)
+    for (int i = threadIdx.x; i < 4 * 256; i += kEncodeThreads) (&s_hist[0][0])[i] = 0;
+  __syncthreads();
   const int64_t chunks = (n + 31) / 32;
   for (int64_t ch = (int64_t)blockIdx.x * kEncodeWarps + warp; ch < chunks;
        ch += (int64_t)gridDim.x * kEncodeWarps) {
@@ -84,6 +95,8 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
           s_x0[warp][lane] = r.x0;
           s_y0[warp][lane] = r.y0;
           s_w[warp][lane] = w;
+          s_invw[warp][lane] = 1.0f / (float)w;
+          s_e[warp][lane] = (int)i;
           s_off[warp][lane] = __ldg(offsets + i);
           const int64_t image_id = i / n_per_image;
           s_base[warp][lane] = (image_id << (32 + tile_bits)) |
@@ -97,31 +110,48 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
       const int t = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += t;
     }
-    s_pref[warp][lane + 1] = incl;
-    if (lane == 0) s_pref[warp][0] = 0;
+    const int excl = incl - cnt;
+    s_pref[warp][lane] = excl;
     const int total = __shfl_sync(0xffffffffu, incl, 31);
-    __syncwarp();
-    for (int j = lane; j < total; j += 32) {
-      // owner: the largest o with s_pref[o] <= j (counts of 0 never own)
-      int lo = 0, hi = 31;
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_pref[warp][mid] <= j) lo = mid;
-        else hi = mid - 1;
+    int carry = 0;  // owner of the last entry of the previous window
+    for (int j0 = 0; j0 < total; j0 += 32) {
+      // runs starting inside this window: bit (start - j0), owner in s_start
+      const bool st = cnt > 0 && excl >= j0 && excl < j0 + 32;
+      if (st) s_start[warp][excl - j0] = lane;
+      const uint32_t starts = __reduce_or_sync(0xffffffffu, st ? 1u << (excl - j0) : 0u);
+      __syncwarp();
+      const uint32_t upto = starts & (0xFFFFFFFFu >> (31 - lane));
+      const int o = upto ? s_start[warp][31 - __clz(upto)] : carry;
+      carry = __shfl_sync(0xffffffffu, o, 31);
+      const int j = j0 + lane;
+      if (j < total) {
+        const int k = j - s_pref[warp][o];
+        const int w = s_w[warp][o];
+        int dy = (int)(((float)k + 0.5f) * s_invw[warp][o]);  // k / w, then made exact
+        if (dy * w > k) --dy;
+        if ((dy + 1) * w <= k) ++dy;
+        const int y = s_y0[warp][o] + dy;
+        const int x = s_x0[warp][o] + (k - dy * w);
+        const int64_t pos = s_off[warp][o] + k;
+        const int64_t key = s_base[warp][o] | ((int64_t)(y * tw + x) << 32);
+        if (pos >= 0 && pos < n_isects) {
+          isect_ids[pos] = key;
+          flatten_ids[pos] = s_e[warp][o];
+          if (hist) {
+            const uint32_t hi = (uint32_t)((uint64_t)key >> 32);
+            for (int p = 0; p < hist_passes; ++p) atomicAdd(&s_hist[p][(hi >> (8 * p)) & 0xFFu], 1u);
+          }
+        }
       }
-      const int o = lo;
-      const int k = j - s_pref[warp][o];
-      const int w = s_w[warp][o];
-      const int dy = k / w;
-      const int y = s_y0[warp][o] + dy;
-      const int x = s_x0[warp][o] + (k - dy * w);
-      const int64_t pos = s_off[warp][o] + k;
-      if (pos >= 0 && pos < n_isects) {
-        isect_ids[pos] = s_base[warp][o] | ((int64_t)(y * tw + x) << 32);
-        flatten_ids[pos] = (int32_t)(ch * 32 + o);
-      }
+      __syncwarp();
     }
-    __syncwarp();
+  }
+  if (hist) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < hist_passes * 256; i += kEncodeThreads) {
+      const uint32_t c = (&s_hist[0][0])[i];
+      if (c) atomicAdd(hist + i, c);
+    }
   }
 }
 
@@ -162,8 +192,10 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t* s_wa
   return excl;
 }
 
+// With `perm`, element i of the scanned sequence is in[perm[i]].
 __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(int64_t n,
                                                                     const int32_t* __restrict__ in,
+                                                                    const int32_t* __restrict__ perm,
                                                                     int64_t* __restrict__ sums) {
   __shared__ int64_t s_warp[32];
   const int64_t base = (int64_t)blockIdx.x * kScanChunk;
@@ -171,7 +203,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(int64_t n,
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    if (i < n) acc += __ldg(in + i);
+    if (i < n) acc += __ldg(in + (perm ? (int64_t)__ldg(perm + i) : i));
   }
   int64_t total;
   block_exclusive_scan<kScanThreads>(acc, s_warp, &total);
@@ -198,8 +230,11 @@ __global__ void __launch_bounds__(1024) scan_sums_kernel(int64_t nb, int64_t* __
   if (threadIdx.x == 0 && total_out) *total_out = total;
 }
 
-// May run in place (in == out): every element is read before it is written.
+// Without `perm` it may run in place (in == out): every element is read
+// before it is written.  With `perm` the scanned sequence is in[perm[i]] and its prefix of
+// position i is stored at out[perm[i]] (scattered back to element order).
 __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, const int32_t* in,
+                                                                  const int32_t* __restrict__ perm,
                                                                   const int64_t* __restrict__ sums,
                                                                   int32_t* out) {
   __shared__ int64_t s_warp[32];
@@ -209,7 +244,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, cons
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    v[k] = i < n ? in[i] : 0;
+    v[k] = i < n ? in[perm ? (int64_t)__ldg(perm + i) : i] : 0;
     acc += v[k];
   }
   int64_t total;
@@ -217,7 +252,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, cons
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    if (i < n) out[i] = (int32_t)run;
+    if (i < n) out[perm ? (int64_t)__ldg(perm + i) : i] = (int32_t)run;
     run += v[k];
   }
 }
@@ -228,7 +263,7 @@ size_t scan_ws_bytes(int64_t n) {
 }
 
 int scan_i32(int64_t n, const int32_t* in, int32_t* out, int64_t* total, void* ws, size_t ws_bytes,
-             cudaStream_t s) {
+             cudaStream_t s, const int32_t* perm = nullptr) {
   if (n <= 0) {
     if (total) cudaMemsetAsync(total, 0, sizeof(int64_t), s);
     return launch_status("scan");
@@ -239,13 +274,27 @@ int scan_i32(int64_t n, const int32_t* in, int32_t* out, int64_t* total, void* w
   }
   const int64_t nb = ceil_div(n, kScanChunk);
   int64_t* sums = static_cast<int64_t*>(ws);
-  scan_reduce_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, sums);
+  scan_reduce_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, sums);
   scan_sums_kernel<<<1, 1024, 0, s>>>(nb, sums, total);
-  scan_down_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, sums, out);
+  scan_down_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, sums, out);
   return launch_status("scan");
 }
 
 // ------------------------------------------------------------ radix sort
+// LSD radix sort, 8-bit digits, one kernel per digit ("onesweep": Adinets &
+// Merrill, 2022).  A histogram kernel counts the digits of every pass in
+// one read of the keys.  Each pass kernel then takes tiles of 4096 keys in
+// the order its CTAs start (an atomic tile counter), ranks them stably in
+// shared memory, publishes its per-digit tile counts, and finds the counts
+// of all earlier tiles by decoupled look-back: walking back over the
+// published tile states until one carries an inclusive prefix.  Keys are
+// read once and written once per pass.
+//
+// Every look-back wait is bounded: a tile waits only for tiles whose CTAs
+// already started, which publish their counts without waiting themselves,
+// so the wait ends; should it not within the bound (a bug, not a workload),
+// the kernel raises the error word in the workspace, takes the count as 0
+// and finishes -- the output is then wrong but no GPU is held.
 
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
@@ -253,93 +302,74 @@ constexpr int kSortItems = 16;                          // keys per thread
 constexpr int kSortTile = kSortThreads * kSortItems;    // 4096 keys per CTA
 constexpr int kWarpSpan = 32 * kSortItems;              // 512 keys per warp
 constexpr int kRadix = 256;
+constexpr int kMaxPasses = 8;
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 __device__ __forceinline__ uint32_t digit_of(uint64_t k, int shift, uint64_t flip) {
   return (uint32_t)(((k ^ flip) >> shift) & 0xFFu);
 }
 
-// Per-CTA digit histogram of one pass; counts laid out digit-major
-// ([digit][cta]) so that each digit's row can be scanned independently.
-__global__ void __launch_bounds__(kSortThreads) radix_upsweep_kernel(
-    int64_t n, const uint64_t* __restrict__ keys, int shift, uint64_t flip, int num_tiles,
-    int32_t* __restrict__ counts) {
-  __shared__ uint32_t s_hist[kSortWarps][kRadix];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&s_hist[0][0])[i] = 0;
-  const int64_t base = (int64_t)blockIdx.x * kSortTile + (int64_t)warp * kWarpSpan;
-  uint64_t k[kSortItems];
+// hist[p][d] += number of keys whose digit of pass p is d, for passes
+// 0..passes-1 starting at bit begin_bit.
+__global__ void __launch_bounds__(256) radix_hist_kernel(int64_t n,
+                                                         const uint64_t* __restrict__ keys,
+                                                         int begin_bit, int passes, uint64_t flip,
+                                                         uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[kMaxPasses][kRadix];
+  for (int i = threadIdx.x; i < kMaxPasses * kRadix; i += blockDim.x) (&s_hist[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
+  for (int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i0 < n; i0 += stride) {
+    uint64_t k[4];
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {  // all loads in flight before any use
-    const int64_t i = base + r * 32 + lane;
-    k[r] = i < n ? __ldg(keys + i) : 0ull;
+    for (int r = 0; r < 4; ++r) k[r] = i0 + r < n ? __ldg(keys + i0 + r) : 0ull;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      if (i0 + r >= n) break;
+      for (int p = 0; p < passes; ++p)
+        atomicAdd(&s_hist[p][digit_of(k[r], begin_bit + 8 * p, flip)], 1u);
+    }
   }
   __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const int64_t i = base + r * 32 + lane;
-    if (i < n) atomicAdd(&s_hist[warp][digit_of(k[r], shift, flip)], 1u);
-  }
-  __syncthreads();
-  for (int d = threadIdx.x; d < kRadix; d += kSortThreads) {
-    uint32_t c = 0;
-#pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) c += s_hist[w][d];
-    counts[(int64_t)d * num_tiles + blockIdx.x] = (int32_t)c;
+  for (int i = threadIdx.x; i < passes * kRadix; i += blockDim.x) {
+    const uint32_t c = (&s_hist[0][0])[i];
+    if (c) atomicAdd(hist + i, c);
   }
 }
 
-// One CTA per digit: exclusive scan of that digit's per-tile counts in
-// place (offsets of the digit's keys within the digit) and the digit total.
-constexpr int kRowScanThreads = 256;
-__global__ void __launch_bounds__(kRowScanThreads) radix_rowscan_kernel(
-    int num_tiles, int32_t* __restrict__ counts, int32_t* __restrict__ totals) {
-  __shared__ int64_t s_warp[32];
-  int32_t* row = counts + (int64_t)blockIdx.x * num_tiles;
-  int64_t carry = 0;
-  for (int b0 = 0; b0 < num_tiles; b0 += kRowScanThreads * 4) {
-    int32_t v[4];
-    int64_t acc = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = b0 + threadIdx.x * 4 + k;
-      v[k] = i < num_tiles ? row[i] : 0;
-      acc += v[k];
-    }
-    int64_t chunk_total;
-    int64_t run = block_exclusive_scan<kRowScanThreads>(acc, s_warp, &chunk_total) + carry;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = b0 + threadIdx.x * 4 + k;
-      if (i < num_tiles) row[i] = (int32_t)run;
-      run += v[k];
-    }
-    carry += chunk_total;
-  }
-  if (threadIdx.x == 0) totals[blockIdx.x] = (int32_t)carry;
-}
-
-struct DownSmem {
+struct PassSmem {
   uint64_t keys[kSortTile];
   int32_t vals[kSortTile];
   uint32_t hist[kSortWarps][kRadix];  // warp counts -> warp exclusive offsets
   uint32_t digit_start[kRadix];       // CTA-local exclusive prefix over digits
-  uint32_t goff[kRadix];              // global offset of each digit for this CTA
+  uint64_t goff[kRadix];              // global offset of each digit for this tile
   int64_t warp_tot[32];
+  int tile;
 };
 
-// Stable rank-and-scatter of one pass.  Keys of a warp are processed in
-// index order (round r covers keys r*32..r*32+31 of the warp's span), lanes
-// in lane order, so ranks respect input order and the sort is stable.  The
-// global base of each digit is the exclusive scan of the 256 digit totals
-// (done here, redundantly per CTA) plus this CTA's row offset.
-__global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
+__device__ __forceinline__ uint64_t load_state(const uint64_t* p) {
+  return *reinterpret_cast<const volatile uint64_t*>(p);
+}
+__device__ __forceinline__ void store_state(uint64_t* p, uint64_t v) {
+  *reinterpret_cast<volatile uint64_t*>(p) = v;
+}
+
+// One digit pass.  state[tile][digit] = (tag << 32) | value with tag
+// 2*pass+1 (value = this tile's count) or 2*pass+2 (value = inclusive
+// prefix over tiles 0..tile); words of other passes or zero mean "not yet".
+__global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
     int64_t n, const uint64_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
     uint64_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int shift, uint64_t flip,
-    int num_tiles, const int32_t* __restrict__ offsets, const int32_t* __restrict__ totals) {
+    int pass, const uint32_t* __restrict__ pass_hist, uint32_t* __restrict__ tile_counter,
+    uint64_t* __restrict__ state, uint32_t* __restrict__ error_word) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  DownSmem& sm = *reinterpret_cast<DownSmem*>(smem_raw);
+  PassSmem& sm = *reinterpret_cast<PassSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tile_base = (int64_t)blockIdx.x * kSortTile;
+  if (threadIdx.x == 0) sm.tile = (int)atomicAdd(tile_counter, 1u);
+  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
+  __syncthreads();
+  const int tile = sm.tile;
+  const int64_t tile_base = (int64_t)tile * kSortTile;
   const int64_t base = tile_base + (int64_t)warp * kWarpSpan;
   uint64_t k[kSortItems];
 #pragma unroll
@@ -347,20 +377,13 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
     const int64_t i = base + r * 32 + lane;
     k[r] = i < n ? __ldg(keys_in + i) : 0ull;
   }
-  for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
-  int64_t unused;
-  const int64_t dbase =
-      block_exclusive_scan<kSortThreads>(__ldg(totals + threadIdx.x), sm.warp_tot, &unused);
-  sm.goff[threadIdx.x] =
-      (uint32_t)(dbase + __ldg(offsets + (int64_t)threadIdx.x * num_tiles + blockIdx.x));
-  __syncthreads();
-
+  // Stable ranks: a warp's keys in index order (round r covers keys
+  // r*32..r*32+31 of its span), lanes in lane order.
   uint32_t rank[kSortItems];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
     const bool valid = base + r * 32 + lane < n;
-    // Invalid lanes form their own group (digit 256) and count nowhere.
     const uint32_t d = valid ? digit_of(k[r], shift, flip) : (uint32_t)kRadix;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     const uint32_t before = __popc(peers & lt_mask);
@@ -373,28 +396,68 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
     rank[r] = cur + before;
   }
   __syncthreads();
-  // Per digit: exclusive offsets over warps, CTA count, then a CTA-wide
-  // exclusive scan over digits for the staging layout.
+  const int d = threadIdx.x;  // one thread per digit
   uint32_t cta_count = 0;
-  {
-    const int d = threadIdx.x;
 #pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) {
-      const uint32_t c = sm.hist[w][d];
-      sm.hist[w][d] = cta_count;
-      cta_count += c;
-    }
+  for (int w = 0; w < kSortWarps; ++w) {
+    const uint32_t c = sm.hist[w][d];
+    sm.hist[w][d] = cta_count;
+    cta_count += c;
   }
+  // Publish, then look back for the exclusive prefix over earlier tiles.
+  const uint64_t tag_agg = (uint64_t)(2 * pass + 1) << 32;
+  const uint64_t tag_inc = (uint64_t)(2 * pass + 2) << 32;
+  uint64_t* my = state + (int64_t)tile * kRadix + d;
+  uint64_t excl = 0;
+  if (tile == 0) {
+    store_state(my, tag_inc | cta_count);
+  } else {
+    store_state(my, tag_agg | cta_count);
+    // Walk back kLookback tiles per round with all their states loaded at
+    // once, so that a long run of not-yet-inclusive predecessors costs one
+    // memory round trip per kLookback tiles instead of one per tile.
+    constexpr int kLookback = 8;
+    bool found = false;
+    for (int t0 = tile - 1; t0 >= 0 && !found; t0 -= kLookback) {
+      uint64_t w[kLookback];
+#pragma unroll
+      for (int i = 0; i < kLookback; ++i)
+        w[i] = t0 - i >= 0 ? load_state(state + (int64_t)(t0 - i) * kRadix + d) : tag_inc;
+#pragma unroll
+      for (int i = 0; i < kLookback; ++i) {
+        if (found) break;
+        const uint64_t* q = state + (int64_t)(t0 - i) * kRadix + d;
+        uint64_t v = w[i];
+        uint32_t spins = 0;
+        while ((v & ~0xFFFFFFFFull) != tag_agg && (v & ~0xFFFFFFFFull) != tag_inc) {
+          if (++spins > kSpinLimit) {
+            atomicOr(error_word, 1u);
+            v = tag_inc;  // give up: count 0, stop walking
+            break;
+          }
+          __nanosleep(32);
+          v = load_state(q);
+        }
+        excl += (uint32_t)v;
+        found = (v & ~0xFFFFFFFFull) == tag_inc;
+      }
+    }
+    store_state(my, tag_inc | (uint32_t)(excl + cta_count));
+  }
+  // Global digit bases: exclusive scan of this pass's digit totals.
+  int64_t unused;
+  const int64_t dbase = block_exclusive_scan<kSortThreads>(__ldg(pass_hist + d), sm.warp_tot, &unused);
+  sm.goff[d] = (uint64_t)dbase + excl;
   int64_t total;
   const int64_t start = block_exclusive_scan<kSortThreads>(cta_count, sm.warp_tot, &total);
-  sm.digit_start[threadIdx.x] = (uint32_t)start;
+  sm.digit_start[d] = (uint32_t)start;
   __syncthreads();
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
     const int64_t i = base + r * 32 + lane;
     if (i < n) {
-      const uint32_t d = digit_of(k[r], shift, flip);
-      const uint32_t p = sm.digit_start[d] + sm.hist[warp][d] + rank[r];
+      const uint32_t dg = digit_of(k[r], shift, flip);
+      const uint32_t p = sm.digit_start[dg] + sm.hist[warp][dg] + rank[r];
       sm.keys[p] = k[r];
       sm.vals[p] = __ldg(vals_in + i);
     }
@@ -403,8 +466,8 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
   const int64_t tile_n = (n - tile_base) < kSortTile ? (n - tile_base) : kSortTile;
   for (int i = threadIdx.x; i < tile_n; i += kSortThreads) {
     const uint64_t key = sm.keys[i];
-    const uint32_t d = digit_of(key, shift, flip);
-    const int64_t dst = (int64_t)sm.goff[d] + (i - (int64_t)sm.digit_start[d]);
+    const uint32_t dg = digit_of(key, shift, flip);
+    const int64_t dst = (int64_t)sm.goff[dg] + (i - (int64_t)sm.digit_start[dg]);
     keys_out[dst] = key;
     vals_out[dst] = sm.vals[i];
   }
@@ -412,19 +475,103 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_downsweep_kernel(
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
+// Workspace of a sort of n keys: the ping-pong buffers, then one region
+// cleared per call (digit histograms of every pass, tile counters, the
+// error word, one tile-state slice shared by the passes).
 struct SortLayout {
-  size_t keys_alt, vals_alt, counts, totals, total;
+  size_t keys_alt, vals_alt, hist, ctrl, state, total;
 };
 
 SortLayout sort_layout(int64_t n) {
   SortLayout L;
-  const int64_t tiles = ceil_div(n < 1 ? 1 : n, kSortTile);
-  const int64_t ncounts = tiles * kRadix;
+  const int64_t n1 = n < 1 ? 1 : n;
+  const int64_t tiles = ceil_div(n1, kSortTile);
   L.keys_alt = 0;
-  L.vals_alt = L.keys_alt + align256(sizeof(uint64_t) * (size_t)(n < 1 ? 1 : n));
-  L.counts = L.vals_alt + align256(sizeof(int32_t) * (size_t)(n < 1 ? 1 : n));
-  L.totals = L.counts + align256(sizeof(int32_t) * (size_t)ncounts);
-  L.total = L.totals + align256(sizeof(int32_t) * kRadix);
+  L.vals_alt = L.keys_alt + align256(sizeof(uint64_t) * (size_t)n1);
+  L.hist = L.vals_alt + align256(sizeof(int32_t) * (size_t)n1);
+  L.ctrl = L.hist + align256(sizeof(uint32_t) * kMaxPasses * kRadix);
+  L.state = L.ctrl + 256;
+  L.total = L.state + align256(sizeof(uint64_t) * (size_t)tiles * kRadix);
+  return L;
+}
+
+// LSD passes over key bits [begin_bit, end_bit) with the scratch of
+// sort_layout(n) at `ws`; the last pass lands in (out_k, out_v) and the
+// input is only read.  With end_bit == 64 the sign bit is flipped so that
+// the unsigned digit order is the signed int64 order.
+// Clears the per-call region of sort_layout(n) at `ws` and returns its
+// digit histograms, for a producer that counts the digits itself.
+uint32_t* radix_reset(int64_t n, char* ws, cudaStream_t s) {
+  const SortLayout L = sort_layout(n);
+  cudaMemsetAsync(ws + L.hist, 0, L.total - L.hist, s);
+  return reinterpret_cast<uint32_t*>(ws + L.hist);
+}
+
+void radix_passes(int64_t n, int begin_bit, int end_bit, const uint64_t* in_k, const int32_t* in_v,
+                  uint64_t* out_k, int32_t* out_v, char* ws, cudaStream_t s,
+                  bool hist_ready = false) {
+  const SortLayout L = sort_layout(n);
+  uint64_t* alt_k = reinterpret_cast<uint64_t*>(ws + L.keys_alt);
+  int32_t* alt_v = reinterpret_cast<int32_t*>(ws + L.vals_alt);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(ws + L.hist);
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ws + L.ctrl);  // [0..7] counters, [8] error
+  uint64_t* state = reinterpret_cast<uint64_t*>(ws + L.state);
+  const int tiles = (int)ceil_div(n, kSortTile);
+  const int passes = (end_bit - begin_bit + 7) / 8;
+  const uint64_t flip = end_bit == 64 ? (1ull << 63) : 0ull;
+  if (!hist_ready) {  // else radix_reset ran and the producer counted the digits
+    cudaMemsetAsync(ws + L.hist, 0, L.total - L.hist, s);
+    radix_hist_kernel<<<grid_for(ceil_div(n, 4), 256, 2), 256, 0, s>>>(n, in_k, begin_bit, passes,
+                                                                         flip, hist);
+  }
+  const int smem = (int)sizeof(PassSmem);
+  cudaFuncSetAttribute(radix_onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const uint64_t* src_k = in_k;
+  const int32_t* src_v = in_v;
+  for (int pass = 0; pass < passes; ++pass) {
+    const bool to_out = ((passes - 1 - pass) % 2) == 0;
+    uint64_t* dst_k = to_out ? out_k : alt_k;
+    int32_t* dst_v = to_out ? out_v : alt_v;
+    radix_onesweep_kernel<<<tiles, kSortThreads, smem, s>>>(
+        n, src_k, src_v, dst_k, dst_v, begin_bit + pass * 8, flip, pass, hist + pass * kRadix,
+        ctrl + pass, state, ctrl + kMaxPasses);
+    src_k = dst_k;
+    src_v = dst_v;
+  }
+}
+
+// keys[e] = bits of depths[e] (the low word of every intersection key of
+// element e), vals[e] = e.
+__global__ void __launch_bounds__(256) depth_keys_kernel(int64_t n, const float* __restrict__ depths,
+                                                         uint64_t* __restrict__ keys,
+                                                         int32_t* __restrict__ vals) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    keys[e] = (uint64_t)__float_as_uint(__ldg(depths + e));
+    vals[e] = (int32_t)e;
+  }
+}
+
+// Workspace of the depth-first sorted encode (n elements, m intersections).
+struct SortedEncodeLayout {
+  size_t sort, ek, ev, pk, pv, offs, scan, dk, dv, total;
+};
+
+SortedEncodeLayout sorted_encode_layout(int64_t n, int64_t m) {
+  SortedEncodeLayout L;
+  const int64_t big = (n > m ? n : m) < 1 ? 1 : (n > m ? n : m);
+  const int64_t n1 = n < 1 ? 1 : n, m1 = m < 1 ? 1 : m;
+  size_t o = 0;
+  L.sort = o; o += sort_layout(big).total;
+  L.ek = o; o += align256(8 * (size_t)n1);
+  L.ev = o; o += align256(4 * (size_t)n1);
+  L.pk = o; o += align256(8 * (size_t)n1);
+  L.pv = o; o += align256(4 * (size_t)n1);
+  L.offs = o; o += align256(4 * (size_t)n1);
+  L.scan = o; o += scan_ws_bytes(n1);
+  L.dk = o; o += align256(8 * (size_t)m1);
+  L.dv = o; o += align256(4 * (size_t)m1);
+  L.total = o;
   return L;
 }
 
@@ -506,9 +653,73 @@ extern "C" int gs_isect_tile_encode(const gs_isect_params* p, const float* means
   if (!means2d || !radii || !depths || !offsets || !isect_ids || !flatten_ids)
     return invalid("intersect_tile_encode: missing buffer");
   encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, as_stream(stream)>>>(
-      n, p->N, means2d, radii, depths, offsets, p->tile_size, p->tile_width, p->tile_height,
-      tile_bits, n_isects, isect_ids, flatten_ids);
+      n, p->N, means2d, radii, depths, offsets, p->tile_size, p->tile_width,
+      p->tile_height, tile_bits, n_isects, isect_ids, flatten_ids, nullptr, 0);
   return launch_status("intersect_tile_encode");
+}
+
+extern "C" size_t gs_isect_tile_encode_sorted_workspace_size(int64_t n_elements,
+                                                            int64_t n_isects) {
+  return sorted_encode_layout(n_elements, n_isects).total;
+}
+
+// Depth-first sorted encode: the elements (i, n) are first put in stable
+// order of their depth bits (4 radix passes over I*N elements), the
+// intersections are then encoded in that order, and a stable sort over the
+// key bits above the depth word (tile and image: 2 passes at 1297x840)
+// finishes the job.  Within one (image, tile) the order is by depth bits,
+// then by element index -- exactly the stable order of the full 64-bit key
+// over the reference's encode order, because an element meets each tile at
+// most once.
+extern "C" int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
+                                           const int32_t* radii, const float* depths,
+                                           const int32_t* tiles_per_gauss, int64_t n_isects,
+                                           int64_t* isect_ids, int32_t* flatten_ids,
+                                           void* workspace, size_t workspace_bytes,
+                                           gs_stream_t stream) {
+  if (int rc = check_isect(p)) return rc;
+  if (n_isects < 0) return invalid("intersect_tile_encode expects non-negative total_isects.");
+  if (n_isects > INT32_MAX) {
+    set_error("intersect_tile_encode: %lld intersections exceed the int32 offsets", (long long)n_isects);
+    return GS_ERR_OVERFLOW;
+  }
+  const int n_tiles = p->tile_width * p->tile_height;
+  const int tile_bits = gs_floor_log2_plus_one(n_tiles);
+  const int image_bits = gs_floor_log2_plus_one(p->I);
+  if (image_bits + tile_bits > 32)
+    return invalid("intersect_tile_encode image id and tile id require more than 32 bits.");
+  const int64_t n = (int64_t)p->I * p->N;
+  if (n == 0 || n_isects == 0) return GS_OK;
+  if (!means2d || !radii || !depths || !tiles_per_gauss || !isect_ids || !flatten_ids)
+    return invalid("intersect_tile_encode_sorted: missing buffer");
+  const SortedEncodeLayout L = sorted_encode_layout(n, n_isects);
+  if (!workspace || workspace_bytes < L.total) {
+    set_error("intersect_tile_encode_sorted: workspace of %zu bytes needed", L.total);
+    return GS_ERR_WORKSPACE;
+  }
+  cudaStream_t s = as_stream(stream);
+  char* ws = static_cast<char*>(workspace);
+  auto K = [&](size_t off) { return reinterpret_cast<uint64_t*>(ws + off); };
+  auto V = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
+  depth_keys_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, depths, K(L.ek), V(L.ev));
+  radix_passes(n, 0, 32, K(L.ek), V(L.ev), K(L.pk), V(L.pv), ws + L.sort, s);
+  const int32_t* perm = V(L.pv);
+  if (int rc = scan_i32(n, tiles_per_gauss, V(L.offs), nullptr, ws + L.scan, scan_ws_bytes(n), s,
+                        perm))
+    return rc;
+  // V(L.offs)[e] is now element e's offset in depth order; encoding in
+  // element order keeps the warps' work as balanced as the plain encode
+  // (depth order would cluster the large near-camera footprints).
+  // The encode also counts the digits of the tile/image passes.
+  const int hb = tile_bits + image_bits;
+  uint32_t* hist = radix_reset(n_isects, ws + L.sort, s);
+  encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, s>>>(
+      n, p->N, means2d, radii, depths, V(L.offs), p->tile_size, p->tile_width,
+      p->tile_height, tile_bits, n_isects, reinterpret_cast<int64_t*>(K(L.dk)), V(L.dv), hist,
+      (hb + 7) / 8);
+  radix_passes(n_isects, 32, 32 + hb, K(L.dk), V(L.dv), reinterpret_cast<uint64_t*>(isect_ids),
+               flatten_ids, ws + L.sort, s, /*hist_ready=*/true);
+  return launch_status("intersect_tile_encode_sorted");
 }
 
 extern "C" size_t gs_isect_sort_workspace_size(int64_t n_isects) {
@@ -531,32 +742,9 @@ extern "C" int gs_isect_sort(int64_t n, int32_t key_bits, const int64_t* isect_i
   }
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
-  uint64_t* alt_k = reinterpret_cast<uint64_t*>(ws + L.keys_alt);
-  int32_t* alt_v = reinterpret_cast<int32_t*>(ws + L.vals_alt);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.counts);
-  int32_t* totals = reinterpret_cast<int32_t*>(ws + L.totals);
-  const int tiles = (int)ceil_div(n, kSortTile);
-  const int passes = (key_bits + 7) / 8;
-  // Signed order: with all 64 bits in play the sign bit is flipped so that
-  // an unsigned digit sort orders like the signed int64 comparison.
-  const uint64_t flip = key_bits == 64 ? (1ull << 63) : 0ull;
-  const int smem = (int)sizeof(DownSmem);
-  cudaFuncSetAttribute(radix_downsweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const uint64_t* src_k = reinterpret_cast<const uint64_t*>(isect_ids);
-  const int32_t* src_v = flatten_ids;
-  for (int pass = 0; pass < passes; ++pass) {
-    // Choose destinations so that the last pass lands in the output.
-    const bool to_out = ((passes - 1 - pass) % 2) == 0;
-    uint64_t* dst_k = to_out ? reinterpret_cast<uint64_t*>(sorted_isect_ids) : alt_k;
-    int32_t* dst_v = to_out ? sorted_flatten_ids : alt_v;
-    const int shift = pass * 8;
-    radix_upsweep_kernel<<<tiles, kSortThreads, 0, s>>>(n, src_k, shift, flip, tiles, counts);
-    radix_rowscan_kernel<<<kRadix, kRowScanThreads, 0, s>>>(tiles, counts, totals);
-    radix_downsweep_kernel<<<tiles, kSortThreads, smem, s>>>(n, src_k, src_v, dst_k, dst_v, shift,
-                                                             flip, tiles, counts, totals);
-    src_k = dst_k;
-    src_v = dst_v;
-  }
+  radix_passes(n, 0, key_bits, reinterpret_cast<const uint64_t*>(isect_ids), flatten_ids,
+               reinterpret_cast<uint64_t*>(sorted_isect_ids), sorted_flatten_ids,
+               ws, s);
   return launch_status("intersect_tile_sort");
 }
 

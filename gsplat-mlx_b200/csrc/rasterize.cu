@@ -28,6 +28,23 @@ constexpr float kTransmittanceThreshold = 1.0e-4f;
 constexpr float kMinOneMinusAlpha = 1.0e-6f;
 constexpr int kMaxChannels = 64;
 
+// sigma = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy with one fixed rounding
+// sequence (explicit intrinsics, which the compiler does not re-contract):
+// every forward and backward kernel then makes the same alpha decision for
+// the same pixel and Gaussian.  c0 dx and c2 dy are returned for reuse.
+struct Sigma {
+  float cdx, cdy, s;
+};
+
+__device__ __forceinline__ Sigma gauss_sigma(float dx, float dy, float c0, float c1, float c2) {
+  Sigma r;
+  r.cdx = __fmul_rn(c0, dx);
+  r.cdy = __fmul_rn(c2, dy);
+  const float q = __fmaf_rn(r.cdx, dx, __fmul_rn(r.cdy, dy));
+  r.s = __fmaf_rn(__fmul_rn(c1, dx), dy, __fmul_rn(0.5f, q));
+  return r;
+}
+
 struct RArgs {
   int I, N, CH, W, H, ts, tw, th;
   int64_t n_isects;
@@ -109,8 +126,8 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
       const float dx = m.x - px, dy = m.y - py;
-      const float sigma = 0.5f * (co.x * dx * dx + co.z * dy * dy) + co.y * dx * dy;
-      const float alpha = fminf(kMaxAlpha, co.w * __expf(-sigma));
+      const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
+      const float alpha = fminf(kMaxAlpha, __fmul_rn(co.w, __expf(-sigma)));
       if (sigma < 0.0f || alpha < kAlphaThreshold) continue;
       const float next_T = Tr * (1.0f - alpha);
       if (next_T <= kTransmittanceThreshold) {
@@ -186,6 +203,39 @@ __device__ __forceinline__ float butterfly_reduce(float (&v)[16], int lane) {
 
 __device__ __forceinline__ int red_index(int lane) {
   return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
+// The same for the first 8 values (9 shuffles); afterwards lane l with
+// (l & 3) == 0 holds the warp total of value red_index8(l).  v[8..15] are
+// left untouched.
+__device__ __forceinline__ float butterfly_reduce8(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 16;
+    const float send = hi ? v[i] : v[i + 4];
+    const float keep = hi ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 8;
+    const float send = hi ? v[i] : v[i + 2];
+    const float keep = hi ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const bool hi = lane & 4;
+    const float send = hi ? v[0] : v[1];
+    const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return v[0];
+}
+
+__device__ __forceinline__ int red_index8(int lane) {
+  return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 }
 
 // Gradient terms per Gaussian: [0,1] v_xy, [2,3,4] v_conic, [5] v_opacity,
@@ -292,9 +342,9 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
       if (valid) {
         dx = m.x - px;
         dy = m.y - py;
-        const float sigma = 0.5f * (co.x * dx * dx + co.z * dy * dy) + co.y * dx * dy;
+        const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
         vis = __expf(-sigma);
-        alpha = fminf(kMaxAlpha, co.w * vis);
+        alpha = fminf(kMaxAlpha, __fmul_rn(co.w, vis));
         valid = !(sigma < 0.0f || alpha < kAlphaThreshold);
       }
       if (!__any_sync(0xffffffffu, valid)) continue;
@@ -325,7 +375,7 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
         }
         v_alpha += T_final * ra * v_ra;
         if (a.backgrounds) v_alpha += -T_final * ra * bg_dot;
-        if (co.w * vis <= kMaxAlpha) {
+        if (__fmul_rn(co.w, vis) <= kMaxAlpha) {
           const float v_sigma = -co.w * vis * v_alpha;
           const float vx = v_sigma * (co.x * dx + co.y * dy);
           const float vy = v_sigma * (co.y * dx + co.z * dy);
@@ -465,8 +515,8 @@ template <int CH>
 __device__ __forceinline__ void composite16(float dx, float dy, const float4& A, const float4& B,
                                             const float* col, float& Tr, float* acc, int& cur,
                                             bool& done, int idx) {
-  const float sigma = 0.5f * (A.z * dx * dx + B.x * dy * dy) + A.w * dx * dy;
-  const float alpha = fminf(kMaxAlpha, B.y * __expf(-sigma));
+  const float sigma = gauss_sigma(dx, dy, A.z, A.w, B.x).s;
+  const float alpha = fminf(kMaxAlpha, __fmul_rn(B.y, __expf(-sigma)));
   if (sigma < 0.0f || alpha < kAlphaThreshold) return;
   const float next_T = Tr * (1.0f - alpha);
   if (next_T <= kTransmittanceThreshold) {
@@ -560,53 +610,65 @@ __global__ void __launch_bounds__(kT16Threads, 10) raster_fwd16_kernel(
 }
 
 // Reverse step of one pixel for one Gaussian (gsplat_rasterize.cpp:503-562);
-// adds the pixel's contributions to the Gaussian's gradient terms g[].
-template <int CH>
+// adds the pixel's contributions to the Gaussian's gradient terms g[]:
+// [0,1] v_xy, [2,3,4] v_conic, [5] v_opacity, then with ABS [6,7] |v_xy|
+// and [8..8+CH) v_colors, without ABS [6..6+CH) v_colors.
+//
+// The reference's per-channel terms are folded into scalars per pixel:
+//   v_alpha = sum_c (col_c T - buf_c ra) vrc_c + ra T_final (v_ra - bg.vrc)
+//           = T (col.vrc) + ra (K - bufdot),
+// with K = T_final (v_ra - bg.vrc) fixed per pixel and bufdot = buf.vrc
+// advanced by fac (col.vrc) -- the same sums in fewer operations.
+// 1 / (1 - alpha) uses the fast reciprocal (2 ulp; alpha <= 0.99 keeps its
+// argument in [0.01, 1]).
+template <int CH, bool ABS>
 __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, const float4& A,
-                                           const float4& B, const float* col, float T_final,
-                                           float& Tr, float* buf, const float* v_rc, float v_ra,
-                                           float bg_dot, bool has_bg, float* g) {
+                                           const float4& B, const float* col, float& Tr,
+                                           float& bufdot, float K, const float* v_rc, float* g) {
   if (!in_range) return false;
-  const float sigma = 0.5f * (A.z * dx * dx + B.x * dy * dy) + A.w * dx * dy;
-  const float vis = __expf(-sigma);
-  const float alpha = fminf(kMaxAlpha, B.y * vis);
-  if (sigma < 0.0f || alpha < kAlphaThreshold) return false;
-  const float ra = 1.0f / fmaxf(kMinOneMinusAlpha, 1.0f - alpha);
+  const Sigma sg = gauss_sigma(dx, dy, A.z, A.w, B.x);
+  const float vis = __expf(-sg.s);
+  const float ov = __fmul_rn(B.y, vis);
+  const float alpha = fminf(kMaxAlpha, ov);
+  if (sg.s < 0.0f || alpha < kAlphaThreshold) return false;
+  const float ra = __fdividef(1.0f, fmaxf(kMinOneMinusAlpha, 1.0f - alpha));
   Tr *= ra;
   const float fac = alpha * Tr;
-  float v_alpha = 0.0f;
+  float cdot = col[0] * v_rc[0];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    g[8 + c] += fac * v_rc[c];
-    v_alpha += (col[c] * Tr - buf[c] * ra) * v_rc[c];
-    buf[c] += col[c] * fac;
-  }
-  v_alpha += T_final * ra * v_ra;
-  if (has_bg) v_alpha += -T_final * ra * bg_dot;
-  if (B.y * vis <= kMaxAlpha) {
-    const float v_sigma = -B.y * vis * v_alpha;
-    const float vx = v_sigma * (A.z * dx + A.w * dy);
-    const float vy = v_sigma * (A.w * dx + B.x * dy);
+  for (int c = 1; c < CH; ++c) cdot = fmaf(col[c], v_rc[c], cdot);
+#pragma unroll
+  for (int c = 0; c < CH; ++c) g[(ABS ? 8 : 6) + c] = fmaf(fac, v_rc[c], g[(ABS ? 8 : 6) + c]);
+  const float v_alpha = fmaf(Tr, cdot, ra * (K - bufdot));
+  bufdot = fmaf(fac, cdot, bufdot);
+  if (ov <= kMaxAlpha) {
+    const float v_sigma = -ov * v_alpha;
+    const float vsdx = v_sigma * dx, vsdy = v_sigma * dy;
+    const float vx = fmaf(A.w, vsdy, v_sigma * sg.cdx);   // v_sigma (c0 dx + c1 dy)
+    const float vy = fmaf(A.w, vsdx, v_sigma * sg.cdy);   // v_sigma (c1 dx + c2 dy)
     g[0] += vx;
     g[1] += vy;
-    g[2] += 0.5f * v_sigma * dx * dx;
-    g[3] += v_sigma * dx * dy;
-    g[4] += 0.5f * v_sigma * dy * dy;
-    g[5] += vis * v_alpha;
-    g[6] += fabsf(vx);
-    g[7] += fabsf(vy);
+    g[2] = fmaf(0.5f * vsdx, dx, g[2]);
+    g[3] = fmaf(vsdx, dy, g[3]);
+    g[4] = fmaf(0.5f * vsdy, dy, g[4]);
+    g[5] = fmaf(vis, v_alpha, g[5]);
+    if (ABS) {
+      g[6] += fabsf(vx);
+      g[7] += fabsf(vy);
+    }
   }
   return true;
 }
 
-template <int CH>
-__global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
+template <int CH, bool ABS>
+__global__ void __launch_bounds__(kT16Threads, 8) raster_bwd16_kernel(
     RArgs a, const float* __restrict__ render_alphas, const int32_t* __restrict__ last_ids,
     const float* __restrict__ v_render_colors, const float* __restrict__ v_render_alphas,
     int absgrad, float* __restrict__ v_means2d_abs, float* __restrict__ v_means2d,
     float* __restrict__ v_conics, float* __restrict__ v_colors, float* __restrict__ v_opacities,
     float* __restrict__ v_backgrounds) {
-  constexpr int NT = 8 + CH;
+  constexpr int CB = ABS ? 8 : 6;  // index of the first colour term
+  constexpr int NT = CB + CH;      // gradient terms per Gaussian
   __shared__ float4 s_a[kT16Threads];
   __shared__ float4 s_b[kT16Threads];
   __shared__ float2 s_c[kT16Threads];
@@ -638,20 +700,20 @@ __global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
   const int last1 = in1 ? min(end - 1, __ldg(last_ids + pix1)) : -1;
   const float vra0 = in0 ? __ldg(v_render_alphas + pix0) : 0.0f;
   const float vra1 = in1 ? __ldg(v_render_alphas + pix1) : 0.0f;
-  float vrc0[CH], vrc1[CH], buf0[CH], buf1[CH];
+  float vrc0[CH], vrc1[CH];
   float bgd0 = 0.0f, bgd1 = 0.0f;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     vrc0[c] = in0 ? __ldg(v_render_colors + pix0 * CH + c) : 0.0f;
     vrc1[c] = in1 ? __ldg(v_render_colors + pix1 * CH + c) : 0.0f;
-    buf0[c] = buf1[c] = 0.0f;
     if (a.backgrounds) {
       const float bg = __ldg(a.backgrounds + image * CH + c);
       bgd0 += bg * vrc0[c];
       bgd1 += bg * vrc1[c];
     }
   }
-  const bool has_bg = a.backgrounds != nullptr;
+  const float K0 = Tf0 * (vra0 - bgd0), K1 = Tf1 * (vra1 - bgd1);
+  float bufdot0 = 0.0f, bufdot1 = 0.0f;
   if (tid < 4) s_bg[tid] = 0.0f;
   if (tid == 0) s_last = -1;
   __syncthreads();
@@ -689,10 +751,10 @@ __global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = 0.0f;
       const float dx = A.x - px;
-      const bool v0 = backward16<CH>(idx <= last0, dx, A.y - py0, A, B, col, Tf0, T0, buf0, vrc0,
-                                     vra0, bgd0, has_bg, g);
-      const bool v1 = backward16<CH>(idx <= last1, dx, A.y - py1, A, B, col, Tf1, T1, buf1, vrc1,
-                                     vra1, bgd1, has_bg, g);
+      const bool v0 = backward16<CH, ABS>(idx <= last0, dx, A.y - py0, A, B, col, T0, bufdot0,
+                                          K0, vrc0, g);
+      const bool v1 = backward16<CH, ABS>(idx <= last1, dx, A.y - py1, A, B, col, T1, bufdot1,
+                                          K1, vrc1, g);
       const unsigned active = __ballot_sync(0xffffffffu, v0 || v1);
       if (!active) continue;
       if (__popc(active) <= 2) {
@@ -701,6 +763,16 @@ __global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
 #pragma unroll
           for (int k = 0; k < NT; ++k)
             if (g[k] != 0.0f) atomicAdd(&s_acc[j * NT + k], g[k]);
+        }
+      } else if (NT <= 10) {
+        // terms 0..7 by the 8-value butterfly, the rest (<= 2) by warp sums
+        const float r = butterfly_reduce8(g, lane);
+        const int ri = red_index8(lane);
+        if ((lane & 3) == 0 && ri < NT && r != 0.0f) atomicAdd(&s_acc[j * NT + ri], r);
+#pragma unroll
+        for (int k = 8; k < NT; ++k) {
+          const float v = warp_sum(g[k]);
+          if (lane == 0 && v != 0.0f) atomicAdd(&s_acc[j * NT + k], v);
         }
       } else {
         const float r = butterfly_reduce<16>(g, lane);
@@ -717,9 +789,8 @@ __global__ void __launch_bounds__(kT16Threads, 7) raster_bwd16_kernel(
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
       else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
       else if (k == 5) atomicAdd(v_opacities + gg, v);
-      else if (k < 8) {
-        if (absgrad) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);
-      } else atomicAdd(v_colors + gg * CH + (k - 8), v);
+      else if (k < CB) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);  // ABS only
+      else atomicAdd(v_colors + gg * CH + (k - CB), v);
     }
   }
 }
@@ -747,8 +818,14 @@ int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, co
                const float* vra, int absgrad, float* vabs, float* vm, float* vc, float* vcol,
                float* vop, float* vbg, cudaStream_t s) {
   if (CH > 0 && a.ts == 16) {
-    raster_bwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.tw * a.th), kT16Threads, 0, s>>>(
-        a, ra, li, vrc, vra, absgrad, vabs, vm, vc, vcol, vop, vbg);
+    constexpr int C1 = CH > 0 ? CH : 1;
+    const unsigned grid = (unsigned)((int64_t)a.I * a.tw * a.th);
+    if (absgrad)
+      raster_bwd16_kernel<C1, true><<<grid, kT16Threads, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+                                                                 vabs, vm, vc, vcol, vop, vbg);
+    else
+      raster_bwd16_kernel<C1, false><<<grid, kT16Threads, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+                                                                  vabs, vm, vc, vcol, vop, vbg);
     return launch_status("rasterize_bwd");
   }
   const int smem = smem_bytes(block, a.CH, true);

@@ -487,6 +487,160 @@ __device__ __forceinline__ void add_vcoeffs(const float* d, const float vc[3], f
     for (int ch = 0; ch < 3; ++ch) row[k * 3 + ch] += b[k] * vc[ch];
 }
 
+// ------------------------------------------------------------ vectorised
+// One thread per Gaussian with its coefficient row held in registers:
+// the active (D+1)^2 x 3 floats are read with back-to-back 16-byte loads
+// (12 for SH3), all in flight at once, and v_coeffs rows are written with
+// 16-byte stores.  Needs rows on a 16-byte boundary (K % 4 == 0 and
+// aligned base pointers) and D <= 3 (the row must fit in registers); the
+// other cases use the warp-staged kernels below.  The row is read once
+// per Gaussian and reused for every camera.
+
+template <int D>
+__global__ void __launch_bounds__(256) glue_fwd_vec_kernel(
+    int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
+    const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
+    const int32_t* __restrict__ radii, float* __restrict__ colors) {
+  constexpr int A = (D + 1) * (D + 1);
+  constexpr int NV = (A * 3 + 3) / 4;
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    bool any = false;
+    for (int c = 0; c < C; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    float co[NV * 4];
+    float m[3] = {0.0f, 0.0f, 0.0f};
+    if (any) {
+      const float4* row = reinterpret_cast<const float4*>(coeffs + n * (int64_t)K * 3);
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const float4 q = __ldg(row + v);
+        co[4 * v] = q.x;
+        co[4 * v + 1] = q.y;
+        co[4 * v + 2] = q.z;
+        co[4 * v + 3] = q.w;
+      }
+      m[0] = __ldg(means + n * 3);
+      m[1] = __ldg(means + n * 3 + 1);
+      m[2] = __ldg(means + n * 3 + 2);
+    }
+    for (int c = 0; c < C; ++c) {
+      const int64_t e = (int64_t)c * N + n;
+      float out[3] = {0.0f, 0.0f, 0.0f};
+      if (any && visible(masks, radii, e)) {
+        float cp[3];
+        campos_of(viewmats + (int64_t)c * 16, cp);
+        const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+        const float s = fmaxf(sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]), 1.0e-8f);
+        const float d[3] = {u[0] / s, u[1] / s, u[2] / s};
+        sh_color<D>(d, co, out);
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) out[ch] = fminf(fmaxf(out[ch] + 0.5f, 0.0f), 1.0f);
+      }
+      colors[e * 3] = out[0];
+      colors[e * 3 + 1] = out[1];
+      colors[e * 3 + 2] = out[2];
+    }
+  }
+}
+
+// The v_coeffs row is written camera by camera (16-byte stores; cameras
+// after the first add to it) instead of being accumulated in registers,
+// which keeps the register count low enough for latency hiding.
+template <int D>
+__global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
+    int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
+    const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
+    const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
+    float* __restrict__ v_means, float* __restrict__ v_coeffs) {
+  constexpr int A = (D + 1) * (D + 1);
+  constexpr int NV = (A * 3 + 3) / 4;
+  for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
+       n += (int64_t)gridDim.x * blockDim.x) {
+    bool any = false;
+    for (int c = 0; c < C; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    float4* out = reinterpret_cast<float4*>(v_coeffs + n * (int64_t)K * 3);
+    int first_zero = 0;  // first float4 of the row that still needs zeros
+    if (any) {
+      float co[NV * 4];
+      const float4* row = reinterpret_cast<const float4*>(coeffs + n * (int64_t)K * 3);
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const float4 q = __ldg(row + v);
+        co[4 * v] = q.x;
+        co[4 * v + 1] = q.y;
+        co[4 * v + 2] = q.z;
+        co[4 * v + 3] = q.w;
+      }
+      const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1),
+                          __ldg(means + n * 3 + 2)};
+      float vm[3] = {0.0f, 0.0f, 0.0f};
+      bool first = true;
+      for (int c = 0; c < C; ++c) {
+        const int64_t e = (int64_t)c * N + n;
+        if (!visible(masks, radii, e)) continue;
+        float cp[3];
+        campos_of(viewmats + (int64_t)c * 16, cp);
+        const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
+        const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
+        const float mm = fmaxf(s, 1.0e-8f);
+        const float d[3] = {u[0] / mm, u[1] / mm, u[2] / mm};
+        float x[3];
+        sh_color<D>(d, co, x);
+        float vc[3];
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+          const float v = x[ch] + 0.5f;
+          vc[ch] = (v > 0.0f && v < 1.0f) ? __ldg(v_colors + e * 3 + ch) : 0.0f;
+        }
+        // basis (the reference's zero-norm guard keeps only the DC term)
+        float b[NV * 4 / 3 + 1];
+#pragma unroll
+        for (int k = 0; k < NV * 4 / 3 + 1; ++k) b[k] = 0.0f;
+        b[0] = kC0;
+        if (D >= 1) {
+          const float norm = sqrtf(d[0] * d[0] + d[1] * d[1] + d[2] * d[2]);
+          if (norm != 0.0f) basis<D>(d[0] / norm, d[1] / norm, d[2] / norm, b);
+        }
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+          float q[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int idx = 4 * v + t;  // (basis idx / 3, channel idx % 3)
+            q[t] = idx < A * 3 ? b[idx / 3] * vc[idx % 3] : 0.0f;
+          }
+          float4 val = make_float4(q[0], q[1], q[2], q[3]);
+          if (!first) {
+            const float4 o = out[v];
+            val.x += o.x;
+            val.y += o.y;
+            val.z += o.z;
+            val.w += o.w;
+          }
+          out[v] = val;
+        }
+        first = false;
+        float vd[3];
+        sh_dir_vjp<D>(d, co, vc, vd);
+        const float dot = vd[0] * u[0] + vd[1] * u[1] + vd[2] * u[2];
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          float vu = vd[i] / mm;
+          if (s > 1.0e-8f) vu -= (u[i] / s) * dot / (mm * mm);
+          vm[i] += vu;
+        }
+      }
+      if (!first) {
+        first_zero = NV;
+        v_means[n * 3] += vm[0];
+        v_means[n * 3 + 1] += vm[1];
+        v_means[n * 3 + 2] += vm[2];
+      }
+    }
+    for (int v = first_zero; v < K * 3 / 4; ++v) out[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(kWsThreads) glue_fwd_ws_kernel(
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
@@ -745,11 +899,24 @@ struct BwdL {
   }
 };
 
+// The vectorised glue kernels apply: SH degree <= 3 and 16-byte rows.
+template <int D>
+bool vec_ok(int K, const float* a, const float* b) {
+  return D <= 3 && K % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(b) & 15) == 0;
+}
+
 template <int D>
 struct GlueFwdL {
   static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
                  const float* coeffs, const uint8_t* masks, const int32_t* radii, float* colors,
                  cudaStream_t s) {
+    if (vec_ok<D>(p->K, coeffs, nullptr)) {
+      glue_fwd_vec_kernel<(D < 3 ? D : 3)><<<grid_for(p->N, 256), 256, 0, s>>>(
+          p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii,
+          colors);
+      return launch_status("sh_glue_fwd");
+    }
     if (p->K * 3 <= kWsMaxR) {
       int C = p->C, N = p->N, K = p->K;
       const uint8_t* mk = p->use_masks ? masks : nullptr;
@@ -767,6 +934,12 @@ struct GlueBwdL {
   static int run(const gs_sh_glue_params* p, const float* means, const float* viewmats,
                  const float* coeffs, const uint8_t* masks, const int32_t* radii,
                  const float* v_colors, float* v_means, float* v_coeffs, cudaStream_t s) {
+    if (vec_ok<D>(p->K, coeffs, v_coeffs)) {
+      glue_bwd_vec_kernel<(D < 3 ? D : 3)><<<grid_for(p->N, 128), 128, 0, s>>>(
+          p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii,
+          v_colors, v_means, v_coeffs);
+      return launch_status("sh_glue_bwd");
+    }
     if (p->K * 3 <= kWsMaxR) {
       int C = p->C, N = p->N, K = p->K;
       const uint8_t* mk = p->use_masks ? masks : nullptr;

@@ -336,6 +336,31 @@ def intersect_tile_encode(means2d, radii, depths, tile_offsets, I, tile_size, ti
     return isect_ids, flatten_ids
 
 
+def intersect_tile_encode_sorted(means2d, radii, depths, tiles_per_gauss, I, tile_size,
+                                 tile_width, tile_height, total_isects):
+    """Encode + stable sort in one native call (the sort=True branch of
+    gsplat_intersect.cpp:288-307); bit-identical to encode then sort."""
+    N = means2d.shape[-2]
+    if total_isects < 0:
+        raise RuntimeError("intersect_tile_encode expects non-negative total_isects.")
+    if total_isects >= 2 ** 31:
+        raise RuntimeError(
+            f"intersect_tile_encode: {total_isects} intersections exceed the int32 index range")
+    isect_ids = _empty((total_isects,), torch.int64)
+    flatten_ids = _empty((total_isects,), torch.int32)
+    if total_isects == 0:
+        return isect_ids, flatten_ids
+    lib = _lib.load()
+    ws = _empty((lib.gs_isect_tile_encode_sorted_workspace_size(int(I) * int(N), total_isects),),
+                torch.uint8)
+    p = IsectParams(int(I), int(N), int(tile_size), int(tile_width), int(tile_height))
+    check(lib.gs_isect_tile_encode_sorted(ct.byref(p), _ptr(means2d), _ptr(radii), _ptr(depths),
+                                          _ptr(tiles_per_gauss), int(total_isects),
+                                          _ptr(isect_ids), _ptr(flatten_ids), _ptr(ws), ws.numel(),
+                                          _stream()), "intersect_tile_encode_sorted")
+    return isect_ids, flatten_ids
+
+
 def intersect_tile_sort(isect_ids, flatten_ids, key_bits=64):
     """Stable sort by key (gsplat_intersect.cpp:266-286: argsort + take)."""
     if isect_ids.dtype != torch.int64:
@@ -377,11 +402,12 @@ def intersect_tile_forward(inputs, I, tile_size, tile_width, tile_height, sort=T
     image_bits = floor_log2_plus_one(I)
     if image_bits + tile_bits > 32:
         raise RuntimeError("intersect_tile_encode image id and tile id require more than 32 bits.")
-    isect_ids, flatten_ids = intersect_tile_encode(means2d, radii, depths, offsets, I, tile_size,
-                                                   tile_width, tile_height, m)
     if sort:
-        isect_ids, flatten_ids = intersect_tile_sort(isect_ids, flatten_ids,
-                                                     32 + tile_bits + image_bits)
+        isect_ids, flatten_ids = intersect_tile_encode_sorted(
+            means2d, radii, depths, tiles_per_gauss, I, tile_size, tile_width, tile_height, m)
+    else:
+        isect_ids, flatten_ids = intersect_tile_encode(means2d, radii, depths, offsets, I,
+                                                       tile_size, tile_width, tile_height, m)
     return {"tiles_per_gauss": tiles_per_gauss, "isect_ids": isect_ids,
             "flatten_ids": flatten_ids}
 

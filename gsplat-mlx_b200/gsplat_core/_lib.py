@@ -79,6 +79,9 @@ SIGNATURES = {
     "gs_isect_scan_workspace_size": (_sz, [_i64]),
     "gs_isect_scan": (ct.c_int, [_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_tile_encode": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "gs_isect_tile_encode_sorted_workspace_size": (_sz, [_i64, _i64]),
+    "gs_isect_tile_encode_sorted": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp,
+                                               _vp, _sz, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),

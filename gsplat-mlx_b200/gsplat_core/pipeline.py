@@ -6,8 +6,9 @@ autograd of sh_loss_fn, scripts/test/scanner_points_training_utils.py:
 1050-1122 and 2076-2119):
 
   projection fwd -> SH colour glue fwd -> count -> scan -> (host read of the
-  intersection count) -> encode -> radix sort -> tile offsets ->
-  rasterize fwd -> rasterize bwd -> projection bwd -> SH glue bwd
+  intersection count) -> depth-ordered encode + tile/image radix passes
+  (= encode -> stable key sort) -> tile offsets -> rasterize fwd ->
+  rasterize bwd -> projection bwd -> SH glue bwd
 
 with the cotangents of the rendered colours / alphas given.  Every stage is
 a native kernel of libgsplat_b200.so called through its C ABI on one CUDA
@@ -124,11 +125,10 @@ class TrainingStep:
             return
         cap = max(int(m * 1.25) + 1024, 1 << 16)
         e = lambda shape, dt: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
-        self.isect_ids = e((cap,), torch.int64)
-        self.flatten_ids = e((cap,), torch.int32)
         self.sorted_ids = e((cap,), torch.int64)
         self.sorted_flatten = e((cap,), torch.int32)
-        self.sort_ws = e((self.lib.gs_isect_sort_workspace_size(cap),), torch.uint8)
+        self.sort_ws = e((self.lib.gs_isect_tile_encode_sorted_workspace_size(self.C * self.N, cap),),
+                         torch.uint8)
         self.capacity = cap
 
     def _mark(self, name):
@@ -173,14 +173,12 @@ class TrainingStep:
             raise RuntimeError(f"{m} intersections exceed the int32 index range")
         self._ensure_capacity(m)
         self.m = m
-        check(L.gs_isect_tile_encode(ct.byref(ip), _p(self.means2d), _p(self.radii),
-                                     _p(self.depths), _p(self.g_offsets), m, _p(self.isect_ids),
-                                     _p(self.flatten_ids), s), "isect_encode")
-        self._mark("isect_encode")
-        check(L.gs_isect_sort(m, self.key_bits, _p(self.isect_ids), _p(self.flatten_ids),
-                              _p(self.sorted_ids), _p(self.sorted_flatten), _p(self.sort_ws),
-                              self.sort_ws.numel(), s), "isect_sort")
-        self._mark("isect_sort")
+        check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                            _p(self.depths), _p(self.tiles_per_gauss), m,
+                                            _p(self.sorted_ids), _p(self.sorted_flatten),
+                                            _p(self.sort_ws), self.sort_ws.numel(), s),
+              "isect_encode_sort")
+        self._mark("isect_encode_sort")
         check(L.gs_isect_offset(m, _p(self.sorted_ids), C, self.tw, self.th,
                                 _p(self.tile_offsets), s), "isect_offset")
         self._mark("isect_offset")

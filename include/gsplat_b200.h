@@ -186,6 +186,23 @@ int gs_isect_tile_encode(const gs_isect_params* p, const float* means2d,
                          int64_t* isect_ids, int32_t* flatten_ids,
                          gs_stream_t stream);
 
+/* Encode and sort in one call: the output equals gs_isect_tile_encode
+ * followed by gs_isect_sort over all key bits (the reference's encode +
+ * mx::argsort + 2x mx::take, gsplat_intersect.cpp:266-286 and :488-539,
+ * i.e. isect_tiles with sort=True), bit for bit.  Inside, the I*N elements
+ * are first ordered by their depth bits, the intersections are encoded in
+ * that order, and only the tile and image bits are sorted afterwards.
+ * tiles_per_gauss [I*N] comes from gs_isect_tile_count; n_isects is its
+ * total.  The workspace is sized by
+ * gs_isect_tile_encode_sorted_workspace_size(I*N, n_isects). */
+size_t gs_isect_tile_encode_sorted_workspace_size(int64_t n_elements, int64_t n_isects);
+int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
+                                const int32_t* radii, const float* depths,
+                                const int32_t* tiles_per_gauss, int64_t n_isects,
+                                int64_t* isect_ids, int32_t* flatten_ids,
+                                void* workspace, size_t workspace_bytes,
+                                gs_stream_t stream);
+
 /* Stable ascending sort of (isect_ids, flatten_ids) by the signed 64-bit
  * key, equal keys kept in input order -- the result of MLX's argsort+take.
  * key_bits = 32 + tile_bits + image_bits is the number of low key bits

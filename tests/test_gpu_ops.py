@@ -239,26 +239,44 @@ def test_sh_large(gs, oracle, cuda, deg, K):
     assert_grad_close(b["v_coeffs"], eb["v_coeffs"], "sh v_coeffs")
 
 
-def test_sh_glue(gs, oracle, cuda):
+@pytest.mark.parametrize("deg,K,misalign", [(3, 16, False), (3, 16, True), (2, 16, False),
+                                             (1, 4, False), (0, 4, False), (0, 1, False),
+                                             (2, 9, False), (4, 25, False)])
+def test_sh_glue(gs, oracle, cuda, deg, K, misalign):
     """Fused colour glue (scanner_points_training_utils.py:1005-1034) against
-    the composition restated in the oracle, with and without masks."""
+    the composition restated in the oracle, with and without masks, on both
+    kernel families (vectorised rows: K % 4 == 0, 16-byte aligned, degree
+    <= 3; warp-staged otherwise)."""
     from gsplat_core import pipeline
     sc, idx = _scene_subset("config3", 50_000)
-    means, coeffs = sc.means[idx], sc.coeffs[idx]
+    means = sc.means[idx]
+    rng = np.random.default_rng(2 + deg)
+    if K == 16:
+        coeffs = sc.coeffs[idx]
+    else:
+        coeffs = rng.normal(0, 0.3, size=(means.shape[0], K, 3)).astype(np.float32)
+        coeffs[:, 0] += 0.5
     views = np.concatenate([sc.viewmats, sc.viewmats @ np.diag([1, 1, 1, 1]).astype(np.float32)])
     views[1, :3, 3] += np.array([0.3, -0.2, 0.5], np.float32)
-    rng = np.random.default_rng(2)
     masks = rng.uniform(size=(2, means.shape[0])) > 0.3
+
+    def dev_coeffs():
+        if not misalign:
+            return T(coeffs)
+        buf = torch.zeros(coeffs.size + 1, dtype=torch.float32, device="cuda")
+        buf[1:] = T(coeffs.ravel())
+        return buf[1:].view(coeffs.shape)   # 4-byte aligned only
+
     for m in (None, masks):
-        col = pipeline.sh_colors(3, T(means), T(views), T(coeffs), None if m is None else T(m))
-        e = oracle.sh_glue_fwd(3, means, views, coeffs, m)
+        col = pipeline.sh_colors(deg, T(means), T(views), dev_coeffs(), None if m is None else T(m))
+        e = oracle.sh_glue_fwd(deg, means, views, coeffs, m)
         assert_fwd_close(col, e, "glue fwd")
         vout = rng.normal(size=e.shape).astype(np.float32)
         vm0 = rng.normal(size=means.shape).astype(np.float32)
         v_means = T(vm0.copy())
-        vco = pipeline.sh_colors_backward(3, T(means), T(views), T(coeffs),
+        vco = pipeline.sh_colors_backward(deg, T(means), T(views), dev_coeffs(),
                                           None if m is None else T(m), T(vout), v_means)
-        eb = oracle.sh_glue_bwd(3, means, views, coeffs, vout, m)
+        eb = oracle.sh_glue_bwd(deg, means, views, coeffs, vout, m)
         assert_grad_close(vco, eb["v_coeffs"], "glue v_coeffs")
         assert_grad_close(to_np(v_means) - vm0, eb["v_means"], "glue v_means", atol_frac=1e-4)
 
@@ -336,6 +354,30 @@ def test_intersect_multi_image_and_empty(gs, oracle, cuda):
     assert z["isect_ids"].numel() == 0 and z["flatten_ids"].numel() == 0
     oz = gs.intersect_offset_forward(z["isect_ids"], I, 32, 32)
     assert int(oz.abs().max()) == 0
+
+
+def test_intersect_sorted_depth_bits(gs, oracle, cuda):
+    """The depth-first sorted encode orders by the raw depth bits like the
+    64-bit key sort: negative depths and -0.0 (sign bit set) after the
+    positives, heavy ties across many element-sort tiles, two images."""
+    rng = np.random.default_rng(9)
+    I, N = 2, 150_001
+    m2 = rng.uniform(-40, 700, size=(I, N, 2)).astype(np.float32)
+    rad = rng.integers(0, 24, size=(I, N, 2)).astype(np.int32)
+    dep = rng.choice(np.array([0.5, 1.0, 2.0, -1.0, 0.0, -0.0, 3.25], np.float32), size=(I, N))
+    dep[:, ::7] = rng.uniform(-5, 5, size=dep[:, ::7].shape).astype(np.float32)
+    g = gs.intersect_tile_forward({"means2d": T(m2), "radii": T(rad), "depths": T(dep)}, I, 16,
+                                  42, 40)
+    e = oracle.isect_tile(m2, rad, dep, I, 16, 42, 40)
+    for k in ("tiles_per_gauss", "isect_ids", "flatten_ids"):
+        assert_exact(g[k], e[k], k)
+    # the same as encode followed by the plain key sort
+    u = gs.intersect_tile_forward({"means2d": T(m2), "radii": T(rad), "depths": T(dep)}, I, 16,
+                                  42, 40, sort=False)
+    tb = gs.floor_log2_plus_one(42 * 40)
+    ib = gs.floor_log2_plus_one(I)
+    sk, sv = gs.intersect_tile_sort(u["isect_ids"], u["flatten_ids"], 32 + tb + ib)
+    assert torch.equal(sk, g["isect_ids"]) and torch.equal(sv, g["flatten_ids"])
 
 
 @pytest.mark.parametrize("n", [1, 31, 4095, 4096, 4097, 100_000, 1_000_003])
