@@ -55,15 +55,51 @@ def load_peaks():
         return PEAKS_FALLBACK, "fallback"
 
 
-def scene_for(rank, world, seed):
-    """Config 3; rank r > 0 views the same scene from its own camera."""
+WORKLOADS = {
+    # name: (description, scaling, cameras_total(world) or None = one per rank)
+    "cfg3": ("cfg3: N=1M SH3 Gaussians, 1 camera 1297x840 per GPU, tile 16", "weak"),
+    "cfg1": ("cfg1: N=10k SH0 Gaussians (colours as degree-0 SH), 1 camera 256x256 per GPU",
+             "weak"),
+    "cfg4": ("cfg4: N=3M SH3 Gaussians, 32 cameras 1920x1080 sharded over the GPUs", "strong"),
+    "cfg5": ("cfg5: N=6M SH3 Gaussians (log-scales U[-3,-1]), 8 cameras 3840x2160 sharded "
+             "over the GPUs", "strong"),
+}
+
+
+def _rotated(sc, rank, world):
+    """The scene seen from its first camera rotated by 2 pi rank / world
+    about the vertical axis through the origin."""
     from gsplat_core import synthetic as S
-    sc = S.config3(seed=seed)
-    if rank > 0:
-        th = 2.0 * np.pi * rank / max(world, 1)
-        p0 = np.array([0.0, -1.0, -3.87298])
-        rot = np.array([[np.cos(th), 0, np.sin(th)], [0, 1, 0], [-np.sin(th), 0, np.cos(th)]])
-        sc.viewmats = S.look_at(rot @ p0)[None]
+    if rank == 0:
+        return sc.viewmats[:1]
+    R, t = sc.viewmats[0, :3, :3], sc.viewmats[0, :3, 3]
+    p0 = -R.T @ t
+    th = 2.0 * np.pi * rank / max(world, 1)
+    rot = np.array([[np.cos(th), 0, np.sin(th)], [0, 1, 0], [-np.sin(th), 0, np.cos(th)]])
+    return S.look_at(rot @ p0)[None].astype(np.float32)
+
+
+def scene_for(rank, world, seed, workload="cfg3"):
+    """The workload's scene with every camera of the job in viewmats / Ks:
+    weak workloads give rank r its own camera (the first camera rotated),
+    strong ones keep the config's cameras."""
+    from gsplat_core import synthetic as S
+    if workload == "cfg3":
+        sc = S.config3(seed=seed)
+    elif workload == "cfg1":
+        sc = S.config1(seed=seed)
+        # colours passed directly (render_random_3dgs_png.py) expressed as the
+        # degree-0 SH coefficient that the clamp glue maps back to them
+        sc.coeffs = ((sc.colors - 0.5) / 0.28209479177387814)[:, None, :].astype(np.float32)
+        sc.sh_degree = 0
+    elif workload == "cfg4":
+        return S.config4(seed=seed)
+    elif workload == "cfg5":
+        return S.config5(seed=seed)
+    else:
+        raise ValueError(workload)
+    sc.viewmats = np.concatenate([_rotated(sc, r, world) for r in range(world)])
+    sc.Ks = np.repeat(sc.Ks[:1], world, 0)
     return sc
 
 
@@ -198,6 +234,25 @@ def cpu_step(checker, sc, vrc, vra, stride):
     return t3 - t0, full, int(it["isect_ids"].size), t_isect
 
 
+def composited_pairs(step):
+    """Pixel x Gaussian pairs the backward evaluates: per pixel, the
+    intersections of its tile from the first up to its last composited one
+    (sum over this rank's images)."""
+    import torch
+    li = step.last_ids.long()
+    offs = step.tile_offsets.long()
+    ty = torch.arange(step.H, device=li.device) // step.ts
+    tx = torch.arange(step.W, device=li.device) // step.ts
+    start = offs[:, ty][:, :, tx]
+    return int((li - start + 1).clamp(min=0).sum().item())
+
+
+def first_camera(sc):
+    """The scene restricted to its first camera (CPU baseline sample)."""
+    import dataclasses
+    return dataclasses.replace(sc, viewmats=sc.viewmats[:1], Ks=sc.Ks[:1])
+
+
 def make_checker():
     from oracle.oracle import Oracle, Reference
     if Reference.available():
@@ -262,19 +317,21 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    sc = scene_for(rank, world, args.seed)
-    vrc_np, vra_np = S.cotangents(args.seed + rank, 1, sc.height, sc.width)
-    # every rank holds the poses of all ranks' cameras (the SH exchange
-    # recomputes the colour basis of remote cameras)
-    views_all = np.concatenate([scene_for(r, world, args.seed).viewmats for r in range(world)])
-    Ks_all = np.repeat(sc.Ks[:1], world, 0)
+    desc, scaling = WORKLOADS[args.workload]
+    sc = scene_for(rank, world, args.seed, args.workload)
+    C_total = sc.cameras
+    from gsplat_core.sharded import camera_shard
+    c0, c1 = camera_shard(C_total, world, rank)
+    vrc_np, vra_np = S.cotangents(args.seed + rank, c1 - c0, sc.height, sc.width)
+    # every rank holds the poses of all cameras (the SH exchange recomputes
+    # the colour basis of remote cameras)
     host = {"means": sc.means, "quats": sc.quats, "scales": sc.scales,
-            "opacities": sc.opacities, "coeffs": sc.coeffs, "viewmats": views_all,
-            "Ks": Ks_all, "v_render_colors": vrc_np, "v_render_alphas": vra_np}
+            "opacities": sc.opacities, "coeffs": sc.coeffs, "viewmats": sc.viewmats,
+            "Ks": sc.Ks, "v_render_colors": vrc_np, "v_render_alphas": vra_np}
     order = list(host)
     d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in host.items()}
     pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in host.items()}
-    sharded = ShardedTrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], world, sc.width,
+    sharded = ShardedTrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], C_total, sc.width,
                                   sc.height, exchange=args.exchange, device=dev)
     step = sharded.step
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
@@ -324,7 +381,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     ms_step = total_ms / args.steps
-    pixels = sc.width * sc.height * world
+    pixels = sc.width * sc.height * C_total       # the whole job's pixels per step
     value = pixels * args.steps / (total_ms / 1e3) / 1e6
 
     # ---- e2e: the same step driven from pinned host buffers.  Every step
@@ -396,38 +453,42 @@ def run_ours(args):
         passes = (step.key_bits - 32 + 7) // 8
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
         top = max((k for k in avg if k != "exchange"), key=avg.get)
-        bytes_top = algorithmic_bytes(top, sc.n, visible, m, sc.width * sc.height, K, passes)
+        # this rank's units: (camera, Gaussian) elements and pixels
+        n_el, pix_local = sc.n * step.C, sc.width * sc.height * step.C
+        bytes_top = algorithmic_bytes(top, n_el, visible, m, pix_local, K, passes)
         achieved = bytes_top / (avg[top] / 1e3) / 1e9
         stages = {}
         for k, v in avg.items():
             if k == "exchange":
                 # NCCL exchange (+ the SH glue backward over all cameras in
                 # gather mode): bytes each rank sends, against the link
-                b = exchange_bytes(sharded.exchange, sc.n, K, 1, world)
+                b = exchange_bytes(sharded.exchange, sc.n, K, step.C, world)
                 stages[k] = {"ms": round(v, 4), "mode": sharded.exchange,
                              "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
                              "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
                 continue
-            b = algorithmic_bytes(k, sc.n, visible, m, sc.width * sc.height, K, passes)
+            b = algorithmic_bytes(k, n_el, visible, m, pix_local, K, passes)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             checker, kind = make_checker()
-            sc0 = scene_for(0, 1, args.seed)
-            _, full, _, _ = cpu_step(checker, sc0, vrc_np, vra_np, args.cpu_stride)
+            sc0 = first_camera(sc)
+            _, full, _, _ = cpu_step(checker, sc0, vrc_np[:1], vra_np[:1], args.cpu_stride)
             cpu = {"value": round(sc0.width * sc0.height / full / 1e6, 4), "unit": "Mpix/s",
                    "cores": 1, "kind": kind,
-                   "sample": (f"one config-3 step; rasterize fwd+bwd on every "
-                              f"{args.cpu_stride}th tile, raster time scaled "
-                              f"x{args.cpu_stride} (extrapolated); other stages in full")}
+                   "sample": (f"one camera of the {args.workload} step; rasterize fwd+bwd on "
+                              f"every {args.cpu_stride}th tile, raster time scaled "
+                              f"x{args.cpu_stride} (extrapolated); other stages in full; the "
+                              f"per-camera rate stands for all {C_total} cameras")}
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, BASELINE config 3 distributions)",
-            "config": {"workload": "cfg3: N=1M SH3 Gaussians, 1 camera 1297x840 per GPU, tile 16",
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": f"synthetic (seeded, BASELINE {args.workload} distributions)",
+            "config": {"workload": desc, "cameras": C_total,
                        "gaussians": sc.n, "visible": visible, "isects": m,
+                       "bwd_pixel_gaussian_pairs": composited_pairs(step),
                        "parallelism": f"camera-sharded dp{world}" if world > 1 else "single",
                        "exchange": sharded.exchange if world > 1 else None,
                        "l2": "flushed (256 MB write) between timed steps"},
@@ -463,6 +524,9 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-stride", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3",
+                    help="BASELINE config (cfg3 is the headline; the others fill the "
+                         "per-config records)")
     ap.add_argument("--exchange", choices=["auto", "allreduce", "gather"], default="auto",
                     help="gradient exchange of the camera-sharded step (N > 1)")
     args = ap.parse_args()

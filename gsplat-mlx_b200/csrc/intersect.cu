@@ -475,18 +475,20 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
 
 size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
-// Workspace of a sort of n keys: the ping-pong buffers, then one region
-// cleared per call (digit histograms of every pass, tile counters, the
-// error word, one tile-state slice shared by the passes).
+// Workspace of a sort of n keys: the look-back error word (first, so that
+// its place does not depend on n; cleared by the public entry points), the
+// ping-pong buffers, then one region cleared per sort (digit histograms of
+// every pass, tile counters, one tile-state slice shared by the passes).
 struct SortLayout {
-  size_t keys_alt, vals_alt, hist, ctrl, state, total;
+  size_t err, keys_alt, vals_alt, hist, ctrl, state, total;
 };
 
 SortLayout sort_layout(int64_t n) {
   SortLayout L;
   const int64_t n1 = n < 1 ? 1 : n;
   const int64_t tiles = ceil_div(n1, kSortTile);
-  L.keys_alt = 0;
+  L.err = 0;
+  L.keys_alt = 256;
   L.vals_alt = L.keys_alt + align256(sizeof(uint64_t) * (size_t)n1);
   L.hist = L.vals_alt + align256(sizeof(int32_t) * (size_t)n1);
   L.ctrl = L.hist + align256(sizeof(uint32_t) * kMaxPasses * kRadix);
@@ -514,7 +516,8 @@ void radix_passes(int64_t n, int begin_bit, int end_bit, const uint64_t* in_k, c
   uint64_t* alt_k = reinterpret_cast<uint64_t*>(ws + L.keys_alt);
   int32_t* alt_v = reinterpret_cast<int32_t*>(ws + L.vals_alt);
   uint32_t* hist = reinterpret_cast<uint32_t*>(ws + L.hist);
-  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ws + L.ctrl);  // [0..7] counters, [8] error
+  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ws + L.ctrl);  // tile counter per pass
+  uint32_t* err = reinterpret_cast<uint32_t*>(ws + L.err);
   uint64_t* state = reinterpret_cast<uint64_t*>(ws + L.state);
   const int tiles = (int)ceil_div(n, kSortTile);
   const int passes = (end_bit - begin_bit + 7) / 8;
@@ -534,7 +537,7 @@ void radix_passes(int64_t n, int begin_bit, int end_bit, const uint64_t* in_k, c
     int32_t* dst_v = to_out ? out_v : alt_v;
     radix_onesweep_kernel<<<tiles, kSortThreads, smem, s>>>(
         n, src_k, src_v, dst_k, dst_v, begin_bit + pass * 8, flip, pass, hist + pass * kRadix,
-        ctrl + pass, state, ctrl + kMaxPasses);
+        ctrl + pass, state, err);
     src_k = dst_k;
     src_v = dst_v;
   }
@@ -699,6 +702,7 @@ extern "C" int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float
   }
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
+  cudaMemsetAsync(ws + L.sort + sort_layout(1).err, 0, sizeof(uint32_t), s);
   auto K = [&](size_t off) { return reinterpret_cast<uint64_t*>(ws + off); };
   auto V = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
   depth_keys_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, depths, K(L.ek), V(L.ev));
@@ -742,10 +746,42 @@ extern "C" int gs_isect_sort(int64_t n, int32_t key_bits, const int64_t* isect_i
   }
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
+  cudaMemsetAsync(ws + L.err, 0, sizeof(uint32_t), s);
   radix_passes(n, 0, key_bits, reinterpret_cast<const uint64_t*>(isect_ids), flatten_ids,
                reinterpret_cast<uint64_t*>(sorted_isect_ids), sorted_flatten_ids,
                ws, s);
   return launch_status("intersect_tile_sort");
+}
+
+// The look-back error word of the last sort that used `ws` with n keys:
+// waits for `stream`, then GS_OK, or GS_ERR_DEVICE when a bounded wait gave up.
+static int read_sort_error(int64_t n, const char* ws, cudaStream_t s) {
+  const SortLayout L = sort_layout(n);
+  uint32_t word = 0;
+  if (cudaMemcpyAsync(&word, ws + L.err, sizeof(word), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return launch_status("intersect sort check");
+  if (word) {
+    set_error("intersect sort: a look-back wait gave up; the sorted output is invalid");
+    return GS_ERR_DEVICE;
+  }
+  return GS_OK;
+}
+
+extern "C" int gs_isect_sort_check(int64_t n_isects, const void* workspace, gs_stream_t stream) {
+  if (n_isects <= 0) return GS_OK;
+  if (!workspace) return invalid("intersect_tile_sort_check: missing workspace");
+  return read_sort_error(n_isects, static_cast<const char*>(workspace), as_stream(stream));
+}
+
+extern "C" int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_isects,
+                                                 const void* workspace, gs_stream_t stream) {
+  if (n_elements <= 0 || n_isects <= 0) return GS_OK;
+  if (!workspace) return invalid("intersect_tile_encode_sorted_check: missing workspace");
+  const SortedEncodeLayout L = sorted_encode_layout(n_elements, n_isects);
+  // one error word serves the depth passes and the tile passes
+  return read_sort_error(n_isects, static_cast<const char*>(workspace) + L.sort,
+                         as_stream(stream));
 }
 
 extern "C" int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,

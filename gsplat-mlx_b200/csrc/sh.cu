@@ -293,6 +293,19 @@ __device__ __forceinline__ bool visible(const uint8_t* __restrict__ masks,
   return true;
 }
 
+// Backward visibility: `visible`, and with skip_zero also a non-zero colour
+// cotangent (a zero cotangent contributes exactly nothing; used when the
+// radii of some cameras are not at hand).
+__device__ __forceinline__ bool bwd_visible(const uint8_t* __restrict__ masks,
+                                            const int32_t* __restrict__ radii,
+                                            const float* __restrict__ v_colors, int skip_zero,
+                                            int64_t e) {
+  if (!visible(masks, radii, e)) return false;
+  if (!skip_zero) return true;
+  const float* v = v_colors + e * 3;
+  return __ldg(v) != 0.0f || __ldg(v + 1) != 0.0f || __ldg(v + 2) != 0.0f;
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) glue_fwd_kernel(int C, int N, int K,
                                                        const float* __restrict__ means,
@@ -333,7 +346,8 @@ __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
                                                        const int32_t* __restrict__ radii,
                                                        const float* __restrict__ v_colors,
                                                        float* __restrict__ v_means,
-                                                       float* __restrict__ v_coeffs) {
+                                                       float* __restrict__ v_coeffs,
+                                                       int skip_zero) {
   for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
        n += (int64_t)gridDim.x * blockDim.x) {
     const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1), __ldg(means + n * 3 + 2)};
@@ -343,7 +357,7 @@ __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
     bool first = true;
     for (int c = 0; c < C; ++c) {
       const int64_t e = (int64_t)c * N + n;
-      if (!visible(masks, radii, e)) continue;
+      if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
       float cp[3];
       campos_of(viewmats + (int64_t)c * 16, cp);
       const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
@@ -551,13 +565,14 @@ __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
     const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
     const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
-    float* __restrict__ v_means, float* __restrict__ v_coeffs) {
+    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero) {
   constexpr int A = (D + 1) * (D + 1);
   constexpr int NV = (A * 3 + 3) / 4;
   for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
        n += (int64_t)gridDim.x * blockDim.x) {
     bool any = false;
-    for (int c = 0; c < C; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    for (int c = 0; c < C; ++c)
+      any |= bwd_visible(masks, radii, v_colors, skip_zero, (int64_t)c * N + n);
     float4* out = reinterpret_cast<float4*>(v_coeffs + n * (int64_t)K * 3);
     int first_zero = 0;  // first float4 of the row that still needs zeros
     if (any) {
@@ -577,7 +592,7 @@ __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
       bool first = true;
       for (int c = 0; c < C; ++c) {
         const int64_t e = (int64_t)c * N + n;
-        if (!visible(masks, radii, e)) continue;
+        if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
         float cp[3];
         campos_of(viewmats + (int64_t)c * 16, cp);
         const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
@@ -695,7 +710,7 @@ __global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
     const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
     const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
-    float* __restrict__ v_means, float* __restrict__ v_coeffs) {
+    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero) {
   extern __shared__ float smem[];
   const int R = K * 3, S = R | 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -709,7 +724,7 @@ __global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
     const int64_t n = e0 + lane;
     const bool live = lane < cnt;
     bool any = false;
-    for (int c = 0; c < C && live; ++c) any |= visible(masks, radii, (int64_t)c * N + n);
+    for (int c = 0; c < C && live; ++c) any |= bwd_visible(masks, radii, v_colors, skip_zero, (int64_t)c * N + n);
     const uint32_t need = __ballot_sync(0xffffffffu, any);
     ws_load_rows(coeffs, e0, cnt, need, R, S, sm, lane);
     float* myv = sv + lane * S;
@@ -721,7 +736,7 @@ __global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
       const float* co = sm + lane * S;
       for (int c = 0; c < C; ++c) {
         const int64_t e = (int64_t)c * N + n;
-        if (!visible(masks, radii, e)) continue;
+        if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
         float cp[3];
         campos_of(viewmats + (int64_t)c * 16, cp);
         const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
@@ -937,19 +952,21 @@ struct GlueBwdL {
     if (vec_ok<D>(p->K, coeffs, v_coeffs)) {
       glue_bwd_vec_kernel<(D < 3 ? D : 3)><<<grid_for(p->N, 128), 128, 0, s>>>(
           p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii,
-          v_colors, v_means, v_coeffs);
+          v_colors, v_means, v_coeffs, p->skip_zero_cotangents);
       return launch_status("sh_glue_bwd");
     }
     if (p->K * 3 <= kWsMaxR) {
       int C = p->C, N = p->N, K = p->K;
       const uint8_t* mk = p->use_masks ? masks : nullptr;
+      int skip = p->skip_zero_cotangents;
       void* args[] = {&C, &N, &K, &means, &viewmats, &coeffs, &mk, &radii, &v_colors, &v_means,
-                      &v_coeffs};
+                      &v_coeffs, &skip};
       return ws_launch(glue_bwd_ws_kernel<D>, N, K, 2, s, "sh_glue_bwd", args);
     }
     glue_bwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(p->C, p->N, p->K, means, viewmats,
                                                            coeffs, p->use_masks ? masks : nullptr,
-                                                           radii, v_colors, v_means, v_coeffs);
+                                                           radii, v_colors, v_means, v_coeffs,
+                                                           p->skip_zero_cotangents);
     return launch_status("sh_glue_bwd");
   }
 };

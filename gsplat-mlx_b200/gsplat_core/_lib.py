@@ -44,7 +44,7 @@ class SHParams(ct.Structure):
 
 class SHGlueParams(ct.Structure):
     _fields_ = [("C", _i32), ("N", _i32), ("K", _i32), ("degrees_to_use", _i32),
-                ("use_masks", _i32)]
+                ("use_masks", _i32), ("skip_zero_cotangents", _i32)]
 
 
 class IsectParams(ct.Structure):
@@ -82,6 +82,8 @@ SIGNATURES = {
     "gs_isect_tile_encode_sorted_workspace_size": (_sz, [_i64, _i64]),
     "gs_isect_tile_encode_sorted": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                                                _vp, _sz, _vp]),
+    "gs_isect_tile_encode_sorted_check": (ct.c_int, [_i64, _i64, _vp, _vp]),
+    "gs_isect_sort_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),

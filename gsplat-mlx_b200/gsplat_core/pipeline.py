@@ -52,15 +52,18 @@ def sh_colors(degree, means, viewmats, coeffs, masks=None, radii=None):
 
 
 def sh_colors_backward(degree, means, viewmats, coeffs, masks, v_colors, v_means_accum,
-                       radii=None, v_coeffs=None):
+                       radii=None, v_coeffs=None, skip_zero_cotangents=False):
     """Reverse mode of sh_colors as MLX autograd forms it; adds into
-    v_means_accum [N,3] and returns v_coeffs [N,K,3] (summed over cameras)."""
+    v_means_accum [N,3] and returns v_coeffs [N,K,3] (summed over cameras).
+    With skip_zero_cotangents, entries whose colour cotangent is zero are
+    skipped (they contribute nothing) -- the visibility test for cameras
+    whose radii are not at hand."""
     C = viewmats.numel() // 16
     N = means.shape[0]
     K = coeffs.shape[-2]
     if v_coeffs is None:
         v_coeffs = torch.empty_like(coeffs)
-    p = SHGlueParams(C, N, K, int(degree), int(masks is not None))
+    p = SHGlueParams(C, N, K, int(degree), int(masks is not None), int(skip_zero_cotangents))
     check(_lib.load().gs_sh_glue_bwd(ct.byref(p), _p(means), _p(viewmats), _p(coeffs), _p(masks),
                                      _p(radii), _p(v_colors), _p(v_means_accum), _p(v_coeffs),
                                      _s()), "sh_colors_backward")
@@ -217,6 +220,13 @@ class TrainingStep:
                                _p(self.v_coeffs), s), "sh_glue_bwd")
         self._mark("sh_bwd")
         return self.grad_flat, m
+
+    def check(self):
+        """Waits for the step and raises if a bounded on-device wait of the
+        intersection sort gave up (its output would be invalid)."""
+        if self.m > 0:
+            check(self.lib.gs_isect_tile_encode_sorted_check(
+                self.C * self.N, self.m, _p(self.sort_ws), _s()), "isect_encode_sort")
 
     def gradients(self):
         return {"v_means": self.v_means, "v_quats": self.v_quats, "v_scales": self.v_scales,

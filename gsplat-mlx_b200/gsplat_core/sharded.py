@@ -78,16 +78,21 @@ def exchange_gradients(mode, grad_flat, n, v_colors_local, v_colors_all, sh_back
     gradients; one all-reduce.  mode "gather": ``grad_flat`` holds the
     projection part (v_means without its SH part, v_quats, v_scales,
     v_opacities) and ``v_colors_local`` [C_local, N, 3] the colour
-    cotangents; after the gather ``sh_backward(v_colors_all)`` must write
-    v_coeffs and add the SH part of v_means for all cameras."""
+    cotangents.  After the gather, the all-reduce of the projection part
+    runs asynchronously while ``sh_backward(v_colors_all)`` writes v_coeffs
+    (``grad_flat[11N:]``, outside the reduced range) for all cameras and
+    returns the SH part of v_means, which is added once the reduction is
+    done."""
     if mode == "allreduce":
         dist.all_reduce(grad_flat, group=group)
         return
     if mode != "gather":
         raise ValueError(f"unknown exchange {mode!r}")
     _all_gather(v_colors_all.view(-1), v_colors_local.reshape(-1), group)
-    dist.all_reduce(grad_flat[:11 * n], group=group)
-    sh_backward(v_colors_all)
+    work = dist.all_reduce(grad_flat[:11 * n], group=group, async_op=True)
+    v_means_sh = sh_backward(v_colors_all)
+    work.wait()
+    grad_flat[:3 * n] += v_means_sh.reshape(-1)
 
 
 class ShardedTrainingStep:
@@ -114,10 +119,11 @@ class ShardedTrainingStep:
                          if exchange == "auto" else exchange)
         if self.exchange not in ("allreduce", "gather"):
             raise ValueError(f"unknown exchange {exchange!r}")
-        self.v_colors_all = None
+        self.v_colors_all = self.v_means_sh = None
         if self.exchange == "gather" and self.world > 1:
             self.v_colors_all = torch.empty((self.C_total, self.N, 3), dtype=torch.float32,
                                             device=self.step.dev)
+            self.v_means_sh = torch.empty((self.N, 3), dtype=torch.float32, device=self.step.dev)
 
     def local(self, t):
         """This rank's slice of a per-camera tensor [C_total, ...]."""
@@ -138,8 +144,11 @@ class ShardedTrainingStep:
             return flat, m
 
         def sh_bwd(v_all):
-            sh_colors_backward(self.deg, means, viewmats_all, coeffs, None, v_all, st.v_means,
-                               radii=None, v_coeffs=st.v_coeffs)
+            self.v_means_sh.zero_()
+            sh_colors_backward(self.deg, means, viewmats_all, coeffs, None, v_all,
+                               self.v_means_sh, radii=None, v_coeffs=st.v_coeffs,
+                               skip_zero_cotangents=True)
+            return self.v_means_sh
 
         exchange_gradients("gather" if gather else "allreduce", flat, self.N, st.v_colors,
                            self.v_colors_all, sh_bwd, self.group)

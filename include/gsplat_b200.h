@@ -138,6 +138,9 @@ int gs_sh_bwd(const gs_sh_params* p, const float* dirs, const float* coeffs,
 typedef struct {
   int32_t C, N, K, degrees_to_use;
   int32_t use_masks;
+  int32_t skip_zero_cotangents; /* bwd: an entry whose colour cotangent is 0
+                                   contributes nothing and is skipped (for
+                                   cameras whose radii are not at hand) */
 } gs_sh_glue_params;
 
 int gs_sh_glue_fwd(const gs_sh_glue_params* p, const float* means,
@@ -202,6 +205,16 @@ int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
                                 int64_t* isect_ids, int32_t* flatten_ids,
                                 void* workspace, size_t workspace_bytes,
                                 gs_stream_t stream);
+
+/* The radix passes of the two calls above and below wait on one another's
+ * tiles with bounded waits; a wait that gives up (a defect, not a workload
+ * condition) raises an error word in the workspace and the kernels finish
+ * with invalid output.  These read that word for the last call that used
+ * the workspace: they wait for `stream`, then return GS_OK or GS_ERR_DEVICE.
+ * No reference counterpart. */
+int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_isects,
+                                      const void* workspace, gs_stream_t stream);
+int gs_isect_sort_check(int64_t n_isects, const void* workspace, gs_stream_t stream);
 
 /* Stable ascending sort of (isect_ids, flatten_ids) by the signed 64-bit
  * key, equal keys kept in input order -- the result of MLX's argsort+take.

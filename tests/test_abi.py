@@ -53,7 +53,7 @@ def test_param_struct_layouts(gs):
     assert ct.sizeof(L.QS2CParams) == 24
     assert ct.sizeof(L.ProjectionParams) == 52
     assert ct.sizeof(L.SHParams) == 24
-    assert ct.sizeof(L.SHGlueParams) == 20
+    assert ct.sizeof(L.SHGlueParams) == 24
     assert ct.sizeof(L.IsectParams) == 20
     assert ct.sizeof(L.RasterParams) == 56
 

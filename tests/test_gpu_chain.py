@@ -72,6 +72,7 @@ def test_training_step_matches_oracle(gs, oracle, cuda, n, cams):
                        T(sc.opacities[idx]), T(sc.coeffs[idx]), T(sc.viewmats), T(sc.Ks),
                        T(vrc), T(vra))
     torch.cuda.synchronize()
+    step.check()   # no bounded on-device wait of the sort gave up
     assert m == it["isect_ids"].size
     assert_exact(step.sorted_ids[:m], it["isect_ids"], "sorted keys")
     assert_exact(step.sorted_flatten[:m], it["flatten_ids"], "sorted flatten ids")
@@ -94,6 +95,7 @@ def test_full_size_config3_properties(gs, oracle, cuda):
             T(sc.viewmats), T(sc.Ks), T(vrc), T(vra)]
     flat, m = step.run(*args)
     torch.cuda.synchronize()
+    step.check()
     p = oracle.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
                         quats=sc.quats[None], scales=sc.scales[None])
     assert_exact(step.radii[0], p["radii"][0, 0], "radii")

@@ -279,6 +279,17 @@ def test_sh_glue(gs, oracle, cuda, deg, K, misalign):
         eb = oracle.sh_glue_bwd(deg, means, views, coeffs, vout, m)
         assert_grad_close(vco, eb["v_coeffs"], "glue v_coeffs")
         assert_grad_close(to_np(v_means) - vm0, eb["v_means"], "glue v_means", atol_frac=1e-4)
+        # zero cotangents skipped: the same sums
+        vz = vout.copy()
+        vz[rng.uniform(size=vz.shape[:2]) < 0.4] = 0.0
+        v_means = T(vm0.copy())
+        vcz = pipeline.sh_colors_backward(deg, T(means), T(views), dev_coeffs(),
+                                          None if m is None else T(m), T(vz), v_means,
+                                          skip_zero_cotangents=True)
+        ez = oracle.sh_glue_bwd(deg, means, views, coeffs, vz, m)
+        assert_grad_close(vcz, ez["v_coeffs"], "glue v_coeffs (skip zero)")
+        assert_grad_close(to_np(v_means) - vm0, ez["v_means"], "glue v_means (skip zero)",
+                          atol_frac=1e-4)
 
 
 # ---------------------------------------------------------------- intersect
@@ -378,6 +389,25 @@ def test_intersect_sorted_depth_bits(gs, oracle, cuda):
     ib = gs.floor_log2_plus_one(I)
     sk, sv = gs.intersect_tile_sort(u["isect_ids"], u["flatten_ids"], 32 + tb + ib)
     assert torch.equal(sk, g["isect_ids"]) and torch.equal(sv, g["flatten_ids"])
+
+
+def test_sort_error_words_clear(gs, cuda):
+    """The bounded look-back waits of a sort end normally: the error word the
+    check entry points read stays clear (GS_OK) after real sorts."""
+    import ctypes as ct
+    from gsplat_core import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(3)
+    n = 3_000_001
+    keys = T(rng.integers(0, 1 << 40, size=n).astype(np.int64))
+    vals = T(np.arange(n, dtype=np.int32))
+    ok, ov = torch.empty_like(keys), torch.empty_like(vals)
+    ws = torch.empty(lib.gs_isect_sort_workspace_size(n), dtype=torch.uint8, device="cuda")
+    s = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ct.c_void_p(t.data_ptr())  # noqa: E731
+    assert lib.gs_isect_sort(n, 40, P(keys), P(vals), P(ok), P(ov), P(ws), ws.numel(), s) == 0
+    assert lib.gs_isect_sort_check(n, P(ws), s) == 0
+    assert bool((ok[1:] >= ok[:-1]).all())
 
 
 @pytest.mark.parametrize("n", [1, 31, 4095, 4096, 4097, 100_000, 1_000_003])

@@ -115,8 +115,8 @@ def _worker(rank, world, port, mode, out_dir):
         def sh_backward(v_colors_all):
             gb = oracle.sh_glue_bwd(sc.sh_degree, sc.means, sc.viewmats, sc.coeffs,
                                     v_colors_all.numpy(), None)
-            flat[:3 * n] += torch.from_numpy(gb["v_means"].ravel())
             flat[11 * n:] = torch.from_numpy(gb["v_coeffs"].ravel())
+            return torch.from_numpy(gb["v_means"])
 
         exchange_gradients(mode, flat, n, torch.from_numpy(np.ascontiguousarray(v_colors)), v_all,
                            sh_backward)
