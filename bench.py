@@ -63,6 +63,8 @@ WORKLOADS = {
     "cfg4": ("cfg4: N=3M SH3 Gaussians, 32 cameras 1920x1080 sharded over the GPUs", "strong"),
     "cfg5": ("cfg5: N=6M SH3 Gaussians (log-scales U[-3,-1]), 8 cameras 3840x2160 sharded "
              "over the GPUs", "strong"),
+    "cfg2": ("cfg2: 2D image fitting, N=100k, 512x512, L2 loss, MLX Adam lr 1e-2; one step = "
+             "render + loss + backward + Adam, loss read on the host every step", "replicas"),
 }
 
 
@@ -92,6 +94,11 @@ def scene_for(rank, world, seed, workload="cfg3"):
         # degree-0 SH coefficient that the clamp glue maps back to them
         sc.coeffs = ((sc.colors - 0.5) / 0.28209479177387814)[:, None, :].astype(np.float32)
         sc.sh_degree = 0
+    elif workload == "cfg2":
+        sc = S.config2(seed=seed)
+        sc.coeffs = ((sc.colors - 0.5) / 0.28209479177387814)[:, None, :].astype(np.float32)
+        sc.sh_degree = 0
+        return sc
     elif workload == "cfg4":
         return S.config4(seed=seed)
     elif workload == "cfg5":
@@ -267,7 +274,9 @@ def run_reference_arm(args):
         return 0
     from gsplat_core import synthetic as S
     checker, kind = make_checker()
-    sc = scene_for(0, 1, args.seed)
+    full_sc = scene_for(0, 1, args.seed, args.workload)
+    cams = full_sc.cameras
+    sc = first_camera(full_sc)
     vrc, vra = S.cotangents(args.seed, 1, sc.height, sc.width)
     stride = args.cpu_stride
     for _ in range(args.warmup):
@@ -279,18 +288,20 @@ def run_reference_arm(args):
         _, full, m, t_isect = cpu_step(checker, sc, vrc, vra, stride)
         fulls.append(full)
         isects.append(t_isect)
-    ms = 1e3 * float(np.mean(fulls))
-    pixels = sc.width * sc.height
+    ms = 1e3 * float(np.mean(fulls)) * cams
+    pixels = sc.width * sc.height * cams
     value = pixels / (ms / 1e3) / 1e6
-    sample = (f"config 3 step; projection/SH/intersect on all {sc.n} Gaussians, rasterize "
-              f"fwd+bwd on every {stride}th of {sc.tile_width * sc.tile_height} tiles, raster "
-              f"time scaled x{stride} (extrapolated)")
+    sample = (f"{args.workload} step of one camera; projection/SH/intersect on all {sc.n} "
+              f"Gaussians, rasterize fwd+bwd on every {stride}th of "
+              f"{sc.tile_width * sc.tile_height} tiles, raster time scaled x{stride} "
+              f"(extrapolated)" + (f"; x{cams} cameras (extrapolated)" if cams > 1 else ""))
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Mpix/s",
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-           "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 3 shapes)",
-           "config": {"workload": "cfg3: N=1M SH3, 1 camera 1297x840, tile 16",
-                      "gaussians": sc.n, "isects": m},
+           "ms_per_step": round(ms, 3), "higher_is_better": True,
+           "scaling": WORKLOADS[args.workload][1], "vs_baseline": None, "dtype": "f32",
+           "data": f"synthetic (seeded, BASELINE {args.workload} shapes)",
+           "config": {"workload": WORKLOADS[args.workload][0], "cameras": cams,
+                      "gaussians": sc.n, "isects_per_camera": m},
            "intersections_sorted_per_s": round(m / float(np.mean(isects)), 1),
            "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": 1,
                             "kind": kind, "sample": sample},
@@ -301,6 +312,62 @@ def run_reference_arm(args):
 
 
 # ------------------------------------------------------------------ GPU arm
+
+def run_fit(args):
+    """the image-fitting trainer's step on device
+    (gsplat_core.fitting), the loss read back every step as the trainer
+    does; with N GPUs every rank fits its own copy (replicas)."""
+    import torch
+    import torch.distributed as dist
+    from gsplat_core import fitting, synthetic as S
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    sc = S.config2(seed=args.seed)
+    target = S.fitting_target(args.seed, sc.width, sc.height)
+    logit = lambda x: np.log(np.clip(x, 1e-5, 1 - 1e-5) / (1 - np.clip(x, 1e-5, 1 - 1e-5)))  # noqa
+    fit = fitting.ImageFitStep(sc.means, sc.quats, np.log(sc.scales), logit(sc.colors),
+                               logit(sc.opacities), sc.viewmats[0], sc.Ks[0], target, sc.width,
+                               sc.height, device=dev)
+    losses = [float(fit.run().item()) for _ in range(args.warmup)]
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler("GPU-" + str(torch.cuda.get_device_properties(dev).uuid))
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        losses.append(float(fit.run().item()))   # the trainer's per-step loss read
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    t = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    if rank == 0:
+        out = {"metric": METRIC, "value": round(sc.width * sc.height * world / ms / 1e3, 3),
+               "unit": "Mpix/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+               "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE cfg2)",
+               "config": {"workload": WORKLOADS["cfg2"][0], "gaussians": sc.n,
+                          "isects_last_step": fit.step.m,
+                          "loss_first": losses[0], "loss_last": losses[-1],
+                          "steps_run": len(losses)},
+               "gpu_launches": None, "clocks": clk}
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
 
 def run_ours(args):
     import torch
@@ -534,6 +601,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "cfg2":
+        return run_fit(args)
     return run_ours(args)
 
 

@@ -557,10 +557,11 @@ __global__ void __launch_bounds__(256) glue_fwd_vec_kernel(
   }
 }
 
-// The v_coeffs row is written camera by camera (16-byte stores; cameras
-// after the first add to it) instead of being accumulated in registers,
-// which keeps the register count low enough for latency hiding.
-template <int D>
+// ACC = false (one camera): the v_coeffs row is written as it is formed
+// (16-byte stores), which keeps the register count low enough for latency
+// hiding.  ACC = true (several cameras): the row is summed over the cameras
+// in registers and written once.
+template <int D, bool ACC>
 __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
     const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
@@ -589,6 +590,9 @@ __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
       const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1),
                           __ldg(means + n * 3 + 2)};
       float vm[3] = {0.0f, 0.0f, 0.0f};
+      float acc[ACC ? NV * 4 : 1];
+#pragma unroll
+      for (int i = 0; i < (ACC ? NV * 4 : 1); ++i) acc[i] = 0.0f;
       bool first = true;
       for (int c = 0; c < C; ++c) {
         const int64_t e = (int64_t)c * N + n;
@@ -624,15 +628,20 @@ __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
             const int idx = 4 * v + t;  // (basis idx / 3, channel idx % 3)
             q[t] = idx < A * 3 ? b[idx / 3] * vc[idx % 3] : 0.0f;
           }
-          float4 val = make_float4(q[0], q[1], q[2], q[3]);
-          if (!first) {
-            const float4 o = out[v];
-            val.x += o.x;
-            val.y += o.y;
-            val.z += o.z;
-            val.w += o.w;
+          if (ACC) {
+#pragma unroll
+            for (int t = 0; t < 4; ++t) acc[(ACC ? 4 * v + t : 0)] += q[t];
+          } else {
+            float4 val = make_float4(q[0], q[1], q[2], q[3]);
+            if (!first) {
+              const float4 o = out[v];
+              val.x += o.x;
+              val.y += o.y;
+              val.z += o.z;
+              val.w += o.w;
+            }
+            out[v] = val;
           }
-          out[v] = val;
         }
         first = false;
         float vd[3];
@@ -646,6 +655,12 @@ __global__ void __launch_bounds__(128) glue_bwd_vec_kernel(
         }
       }
       if (!first) {
+        if (ACC) {
+#pragma unroll
+          for (int v = 0; v < NV; ++v)
+            out[v] = make_float4(acc[(ACC ? 4 * v : 0)], acc[(ACC ? 4 * v + 1 : 0)],
+                                 acc[(ACC ? 4 * v + 2 : 0)], acc[(ACC ? 4 * v + 3 : 0)]);
+        }
         first_zero = NV;
         v_means[n * 3] += vm[0];
         v_means[n * 3 + 1] += vm[1];
@@ -950,9 +965,11 @@ struct GlueBwdL {
                  const float* coeffs, const uint8_t* masks, const int32_t* radii,
                  const float* v_colors, float* v_means, float* v_coeffs, cudaStream_t s) {
     if (vec_ok<D>(p->K, coeffs, v_coeffs)) {
-      glue_bwd_vec_kernel<(D < 3 ? D : 3)><<<grid_for(p->N, 128), 128, 0, s>>>(
-          p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii,
-          v_colors, v_means, v_coeffs, p->skip_zero_cotangents);
+      constexpr int DV = D < 3 ? D : 3;
+      auto kern = p->C > 1 ? glue_bwd_vec_kernel<DV, true> : glue_bwd_vec_kernel<DV, false>;
+      kern<<<grid_for(p->N, 128), 128, 0, s>>>(p->C, p->N, p->K, means, viewmats, coeffs,
+                                                p->use_masks ? masks : nullptr, radii, v_colors,
+                                                v_means, v_coeffs, p->skip_zero_cotangents);
       return launch_status("sh_glue_bwd");
     }
     if (p->K * 3 <= kWsMaxR) {

@@ -47,6 +47,10 @@ class SHGlueParams(ct.Structure):
                 ("use_masks", _i32), ("skip_zero_cotangents", _i32)]
 
 
+class AdamParams(ct.Structure):
+    _fields_ = [("n", _i64), ("learning_rate", _f), ("beta1", _f), ("beta2", _f), ("eps", _f)]
+
+
 class IsectParams(ct.Structure):
     _fields_ = [("I", _i32), ("N", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32)]
@@ -88,6 +92,9 @@ SIGNATURES = {
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),
     "gs_isect_sort_noalloc": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gs_fit_activate": (ct.c_int, [_i64] + [_vp] * 9),
+    "gs_l2_loss_grad": (ct.c_int, [_i64] + [_vp] * 5),
+    "gs_fit_adam": (ct.c_int, [_P(AdamParams)] + [_vp] * 17),
     "gs_rasterize_fwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 12),
     "gs_rasterize_bwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 19),
 }

@@ -141,14 +141,21 @@ class TrainingStep:
             self.events.append((name, ev))
 
     def run(self, means, quats, scales, opacities, coeffs, viewmats, Ks, v_render_colors,
-            v_render_alphas, sh_backward=True):
+            v_render_alphas, sh_backward=True, colors=None, target=None):
         """Forward and backward; returns the flat gradient buffer (a view of
         self.grad_flat) and the intersection count of this step.
 
         With ``sh_backward=False`` the SH colour glue backward is left to the
         caller: v_coeffs is not written and v_means holds the projection part
         only, while ``self.v_colors`` holds the colour cotangents (the camera-
-        sharded step exchanges those instead of the SH gradients)."""
+        sharded step exchanges those instead of the SH gradients).
+
+        ``colors`` [C,N,3] (or [N,3] for one camera) replaces the SH colour
+        glue: the rasterizer uses them directly, no SH glue runs and
+        ``self.v_colors`` holds their gradient (the image-fitting trainer).
+        ``target`` [C,H,W,3] replaces the given cotangents by those of the
+        L2 loss mean((render - target)^2), whose value lands in the device
+        scalar ``self.loss``."""
         L, s = self.lib, _s()
         C, N = self.C, self.N
         self._mark("start")
@@ -159,9 +166,13 @@ class TrainingStep:
                                   _p(self.conics), None, _p(self.radii), s), "projection_fwd")
         self._mark("projection_fwd")
         gp = SHGlueParams(C, N, self.K, self.deg, 0)
-        check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
-                               _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
-        self._mark("sh_fwd")
+        if colors is None:
+            check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
+                                   _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
+            colors = self.colors
+            self._mark("sh_fwd")
+        else:
+            sh_backward = False
         ip = IsectParams(C, N, self.ts, self.tw, self.th)
         check(L.gs_isect_tile_count(ct.byref(ip), _p(self.means2d), _p(self.radii),
                                     _p(self.tiles_per_gauss), s), "isect_count")
@@ -192,13 +203,22 @@ class TrainingStep:
             opac = opacities
         rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
                           int(self.backgrounds is not None), 0, 0)
-        check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(self.colors),
+        check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(colors),
                                  _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
                                  _p(self.sorted_flatten), _p(self.render_colors),
                                  _p(self.render_alphas), _p(self.last_ids), s), "rasterize_fwd")
         self._mark("rasterize_fwd")
+        if target is not None:
+            if not hasattr(self, "loss"):
+                self.loss = torch.zeros((1,), dtype=torch.float32, device=self.dev)
+                self.v_rc_loss = torch.empty_like(self.render_colors)
+                self.v_ra_zero = torch.zeros_like(self.render_alphas)
+            check(L.gs_l2_loss_grad(self.render_colors.numel(), _p(self.render_colors),
+                                    _p(target), _p(self.v_rc_loss), _p(self.loss), s), "l2_loss")
+            v_render_colors, v_render_alphas = self.v_rc_loss, self.v_ra_zero
+            self._mark("loss")
         v_opac = self.v_opacities if C == 1 else self.v_opac_cn
-        check(L.gs_rasterize_bwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(self.colors),
+        check(L.gs_rasterize_bwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(colors),
                                  _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
                                  _p(self.sorted_flatten), _p(self.render_alphas),
                                  _p(self.last_ids), _p(v_render_colors), _p(v_render_alphas),

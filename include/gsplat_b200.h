@@ -288,6 +288,48 @@ int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
                      float* v_opacities, float* v_backgrounds,
                      gs_stream_t stream);
 
+/* ------------------------------------------------------------------ */
+/* training glue of the image-fitting trainer, on device               */
+/* Replaces the MLX elementwise ops and mlx.optimizers.Adam of         */
+/* scripts/test/train_image_fitting_3dgs_mlx.py (activations :33-36,   */
+/* :104-118; Adam updates :529-566).  No kernel counterpart in the     */
+/* reference (MLX runs these as generic array ops).                    */
+/* ------------------------------------------------------------------ */
+
+/* quats_n = quats / max(|quats|, 1e-8) [n,4] (16-byte aligned),
+ * scales = exp(log_scales) [n,3], colors = sigmoid(color_logits) [n,3],
+ * opacities = sigmoid(opacity_logits) [n]. */
+int gs_fit_activate(int64_t n, const float* quats, const float* log_scales,
+                    const float* color_logits, const float* opacity_logits,
+                    float* quats_n, float* scales, float* colors, float* opacities,
+                    gs_stream_t stream);
+
+/* L2 image loss: v_render = 2 (render - target) / count and
+ * *loss = mean((render - target)^2) (a device float; atomically summed, so
+ * its last bits depend on the order of the CTAs). */
+int gs_l2_loss_grad(int64_t count, const float* render, const float* target,
+                    float* v_render, float* loss, gs_stream_t stream);
+
+typedef struct {
+  int64_t n;
+  float learning_rate, beta1, beta2, eps; /* MLX Adam: 1e-2 (the trainer's
+                                             lr), 0.9, 0.999, 1e-8 */
+} gs_adam_params;
+
+/* One Adam step (MLX semantics: no bias correction) on the raw parameters,
+ * given the gradients of the activated ones (v_quats is d/d quats_n):
+ * reverse mode of the activations, the update, the trainer's quaternion
+ * renormalisation, and the activated parameters for the next step (written
+ * into quats_n / scales / colors / opacities, which must hold this step's
+ * activations on entry).  moment1 / moment2 [n,14] per Gaussian:
+ * [means 3 | quats 4 | log_scales 3 | color_logits 3 | opacity 1]. */
+int gs_fit_adam(const gs_adam_params* p, float* means, float* quats, float* log_scales,
+                float* color_logits, float* opacity_logits, const float* v_means,
+                const float* v_quats, const float* v_scales, const float* v_colors,
+                const float* v_opacities, float* moment1, float* moment2,
+                float* quats_n, float* scales, float* colors, float* opacities,
+                gs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
