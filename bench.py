@@ -178,7 +178,8 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
         "projection_fwd": n * (40 + 36),
         # means + campos in, colours out for all; coefficient rows of visible
         "sh_fwd": n * (12 + 8 + 12) + visible * K * 12,
-        "isect_count_scan": n * (16 + 4) + n * 8,
+        # rects from means2d/radii, counts out, their total
+        "isect_count": n * (16 + 4),
         # depth keys (4 B in, 12 out), 4 element passes at 24 B, permuted scan
         # (12 B), encode (24 B per element, 12 B per intersection out), then
         # 24 B per intersection per tile/image pass
@@ -193,11 +194,11 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
 
 
 def our_kernel_launches(sort_passes):
-    # projection fwd 1, glue fwd 1, count 1, scan 3, depth keys 1, element
-    # sort 4 x (upsweep + rowscan + downsweep), permuted scan 3, encode 1,
-    # tile/image passes x 3, offset 1, rasterize fwd 1, rasterize bwd 1,
-    # projection bwd 1, glue bwd 1
-    return 1 + 1 + 1 + 3 + 1 + 4 * 3 + 3 + 1 + sort_passes * 3 + 1 + 1 + 1 + 1 + 1
+    # projection fwd 1, glue fwd 1, count (+ total) 1, depth keys 1, element
+    # sort: digit histogram 1 + 4 onesweep passes, permuted scan 3, encode
+    # (+ tile/image digit histogram) 1, tile/image onesweep passes, offset 1,
+    # rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
+    return 1 + 1 + 1 + 1 + (1 + 4) + 3 + 1 + sort_passes + 1 + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -438,8 +439,12 @@ def run_ours(args):
         torch.cuda.synchronize()
         step_ms.append(s_ev.elapsed_time(e_ev))
         evs = step.events
+        this = {}
         for (n0, a), (n1, b) in zip(evs[:-1], evs[1:]):
-            stage_ms.setdefault(n1, []).append(a.elapsed_time(b))
+            if n1 != "start":
+                this[n1] = this.get(n1, 0.0) + a.elapsed_time(b)
+        for k, v in this.items():
+            stage_ms.setdefault(k, []).append(v)
     step.events = None
     clk = clocks.stop()
     local_ms = float(np.sum(step_ms))
@@ -521,8 +526,9 @@ def run_ours(args):
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
         top = max((k for k in avg if k != "exchange"), key=avg.get)
         # this rank's units: (camera, Gaussian) elements and pixels
-        n_el, pix_local = sc.n * step.C, sc.width * sc.height * step.C
-        bytes_top = algorithmic_bytes(top, n_el, visible, m, pix_local, K, passes)
+        n_el, pix_local = sc.n * sharded.C, sc.width * sc.height * sharded.C
+        vis_b = visible
+        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, passes)
         achieved = bytes_top / (avg[top] / 1e3) / 1e9
         stages = {}
         for k, v in avg.items():
@@ -534,7 +540,7 @@ def run_ours(args):
                              "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
                              "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
                 continue
-            b = algorithmic_bytes(k, n_el, visible, m, pix_local, K, passes)
+            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, passes)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
         cpu = None

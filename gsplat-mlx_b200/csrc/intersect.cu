@@ -36,16 +36,36 @@ __device__ __forceinline__ Rect tile_rect(float mx, float my, int rx, int ry, in
   return r;
 }
 
+// With `total`, the counts are also summed into *total (zeroed by the caller).
+// Rect clipped to the tile-row window [ty0, ty1) (the whole grid: 0, th).
+__device__ __forceinline__ Rect band_rect(float mx, float my, int rx, int ry, int ts, int tw,
+                                          int th, int ty0, int ty1) {
+  Rect r = tile_rect(mx, my, rx, ry, ts, tw, th);
+  r.y0 = max(r.y0, ty0);
+  r.y1 = min(r.y1, ty1);
+  if (r.y1 < r.y0) r.y1 = r.y0;
+  return r;
+}
+
 __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __restrict__ means2d,
                                                     const int32_t* __restrict__ radii, int ts,
-                                                    int tw, int th,
-                                                    int32_t* __restrict__ tiles_per_gauss) {
+                                                    int tw, int th, int ty0, int ty1,
+                                                    int32_t* __restrict__ tiles_per_gauss,
+                                                    unsigned long long* __restrict__ total) {
+  unsigned long long sum = 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
     const float2 m = __ldg(reinterpret_cast<const float2*>(means2d) + i);
-    const Rect r = tile_rect(m.x, m.y, rad.x, rad.y, ts, tw, th);
-    tiles_per_gauss[i] = (r.y1 - r.y0) * (r.x1 - r.x0);
+    const Rect r = band_rect(m.x, m.y, rad.x, rad.y, ts, tw, th, ty0, ty1);
+    const int c = (r.y1 - r.y0) * (r.x1 - r.x0);
+    tiles_per_gauss[i] = c;
+    sum += (unsigned long long)c;
+  }
+  if (total) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((threadIdx.x & 31) == 0 && sum) atomicAdd(total, sum);
   }
 }
 
@@ -66,8 +86,8 @@ constexpr int kEncodeWarps = kEncodeThreads / 32;
 __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
     int64_t n, int n_per_image, const float* __restrict__ means2d,
     const int32_t* __restrict__ radii, const float* __restrict__ depths,
-    const int32_t* __restrict__ offsets, int ts, int tw, int th, int tile_bits, int64_t n_isects,
-    int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids,
+    const int32_t* __restrict__ offsets, int ts, int tw, int th, int ty0, int ty1, int tile_bits,
+    int64_t n_isects, int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids,
     uint32_t* __restrict__ hist, int hist_passes) {
   __shared__ int s_pref[kEncodeWarps][32];
   __shared__ int s_x0[kEncodeWarps][32], s_y0[kEncodeWarps][32], s_w[kEncodeWarps][32];
@@ -88,7 +108,7 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
       const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
       if (rad.x > 0 && rad.y > 0) {
         const float2 m = __ldg(reinterpret_cast<const float2*>(means2d) + i);
-        const Rect r = tile_rect(m.x, m.y, rad.x, rad.y, ts, tw, th);
+        const Rect r = band_rect(m.x, m.y, rad.x, rad.y, ts, tw, th, ty0, ty1);
         const int w = r.x1 - r.x0;
         cnt = (r.y1 - r.y0) * w;
         if (cnt > 0) {
@@ -378,14 +398,23 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
     k[r] = i < n ? __ldg(keys_in + i) : 0ull;
   }
   // Stable ranks: a warp's keys in index order (round r covers keys
-  // r*32..r*32+31 of its span), lanes in lane order.
+  // r*32..r*32+31 of its span), lanes in lane order; invalid lanes (past
+  // n) form their own group and count nowhere.
   uint32_t rank[kSortItems];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
     const bool valid = base + r * 32 + lane < n;
     const uint32_t d = valid ? digit_of(k[r], shift, flip) : (uint32_t)kRadix;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    // lanes with the same digit: one ballot per digit bit (and one for
+    // validity) -- faster than __match_any_sync here
+    uint32_t peers = __ballot_sync(0xffffffffu, valid);
+    if (!valid) peers = ~peers;
+#pragma unroll
+    for (int bit = 0; bit < 8; ++bit) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (d >> bit) & 1u);
+      peers &= ((d >> bit) & 1u) ? bal : ~bal;
+    }
     const uint32_t before = __popc(peers & lt_mask);
     const int leader = __ffs(peers) - 1;
     uint32_t cur = 0;
@@ -580,16 +609,21 @@ SortedEncodeLayout sorted_encode_layout(int64_t n, int64_t m) {
 
 // ------------------------------------------------------------ offsets
 
-// tile_offsets[o] = lower bound of key(o) = (o / T) << tb | (o % T) in
-// isect_ids >> 32: one thread per slot, binary search over the sorted keys,
-// as the reference does (gsplat_intersect.cpp:605-641, metal :110-136).
+// tile_offsets[o] = lower bound of key(o) = (image << tb) | tile in
+// isect_ids >> 32, for the slots o of tile rows [ty0, ty0 + rows) of every
+// image (the whole grid: ty0 = 0, rows = th): one thread per slot, binary
+// search over the sorted keys, as the reference does
+// (gsplat_intersect.cpp:605-641, metal :110-136).
 __global__ void __launch_bounds__(256) offset_kernel(int64_t m, const int64_t* __restrict__ ids,
-                                                     int I, int T, int tb,
+                                                     int I, int tw, int ty0, int rows, int tb,
                                                      int32_t* __restrict__ offsets) {
-  const int64_t n_off = (int64_t)I * T;
+  const int64_t per_image = (int64_t)rows * tw;
+  const int64_t n_off = (int64_t)I * per_image;
   for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < n_off;
        o += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t key = ((o / T) << tb) | (o % T);
+    const int64_t image = o / per_image;
+    const int64_t tile = (int64_t)ty0 * tw + (o - image * per_image);
+    const int64_t key = (image << tb) | tile;
     int64_t lo = 0, hi = m;
     while (lo < hi) {
       const int64_t mid = lo + (hi - lo) / 2;
@@ -604,6 +638,16 @@ __global__ void __launch_bounds__(256) offset_kernel(int64_t m, const int64_t* _
 }  // namespace gsb
 
 using namespace gsb;
+
+// The tile-row window of the call: the whole grid unless tile_y1 > tile_y0.
+static void tile_rows(const gs_isect_params* p, int& ty0, int& ty1) {
+  ty0 = 0;
+  ty1 = p->tile_height;
+  if (p->tile_y1 > p->tile_y0) {
+    ty0 = p->tile_y0 < 0 ? 0 : (p->tile_y0 > p->tile_height ? p->tile_height : p->tile_y0);
+    ty1 = p->tile_y1 > p->tile_height ? p->tile_height : p->tile_y1;
+  }
+}
 
 static int check_isect(const gs_isect_params* p) {
   if (!p) return invalid("intersect: params missing");
@@ -621,9 +665,32 @@ extern "C" int gs_isect_tile_count(const gs_isect_params* p, const float* means2
   const int64_t n = (int64_t)p->I * p->N;
   if (n == 0) return GS_OK;
   if (!means2d || !radii || !tiles_per_gauss) return invalid("intersect_tile_count: missing buffer");
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
   count_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
-      n, means2d, radii, p->tile_size, p->tile_width, p->tile_height, tiles_per_gauss);
+      n, means2d, radii, p->tile_size, p->tile_width, p->tile_height, ty0, ty1, tiles_per_gauss,
+      nullptr);
   return launch_status("intersect_tile_count");
+}
+
+extern "C" int gs_isect_tile_count_total(const gs_isect_params* p, const float* means2d,
+                                         const int32_t* radii, int32_t* tiles_per_gauss,
+                                         int64_t* total_device, gs_stream_t stream) {
+  if (int rc = check_isect(p)) return rc;
+  if (!total_device) return invalid("intersect_tile_count_total: missing total");
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(total_device, 0, sizeof(int64_t), s) != cudaSuccess)
+    return launch_status("intersect_tile_count_total");
+  const int64_t n = (int64_t)p->I * p->N;
+  if (n == 0) return GS_OK;
+  if (!means2d || !radii || !tiles_per_gauss)
+    return invalid("intersect_tile_count_total: missing buffer");
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
+  count_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, means2d, radii, p->tile_size, p->tile_width,
+                                                  p->tile_height, ty0, ty1, tiles_per_gauss,
+                                                  reinterpret_cast<unsigned long long*>(total_device));
+  return launch_status("intersect_tile_count_total");
 }
 
 extern "C" size_t gs_isect_scan_workspace_size(int64_t n) { return scan_ws_bytes(n); }
@@ -655,9 +722,11 @@ extern "C" int gs_isect_tile_encode(const gs_isect_params* p, const float* means
   if (n == 0 || n_isects == 0) return GS_OK;
   if (!means2d || !radii || !depths || !offsets || !isect_ids || !flatten_ids)
     return invalid("intersect_tile_encode: missing buffer");
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
   encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, as_stream(stream)>>>(
       n, p->N, means2d, radii, depths, offsets, p->tile_size, p->tile_width,
-      p->tile_height, tile_bits, n_isects, isect_ids, flatten_ids, nullptr, 0);
+      p->tile_height, ty0, ty1, tile_bits, n_isects, isect_ids, flatten_ids, nullptr, 0);
   return launch_status("intersect_tile_encode");
 }
 
@@ -717,10 +786,12 @@ extern "C" int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float
   // The encode also counts the digits of the tile/image passes.
   const int hb = tile_bits + image_bits;
   uint32_t* hist = radix_reset(n_isects, ws + L.sort, s);
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
   encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, s>>>(
       n, p->N, means2d, radii, depths, V(L.offs), p->tile_size, p->tile_width,
-      p->tile_height, tile_bits, n_isects, reinterpret_cast<int64_t*>(K(L.dk)), V(L.dv), hist,
-      (hb + 7) / 8);
+      p->tile_height, ty0, ty1, tile_bits, n_isects, reinterpret_cast<int64_t*>(K(L.dk)), V(L.dv),
+      hist, (hb + 7) / 8);
   radix_passes(n_isects, 32, 32 + hb, K(L.dk), V(L.dv), reinterpret_cast<uint64_t*>(isect_ids),
                flatten_ids, ws + L.sort, s, /*hist_ready=*/true);
   return launch_status("intersect_tile_encode_sorted");
@@ -784,18 +855,28 @@ extern "C" int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_i
                          as_stream(stream));
 }
 
-extern "C" int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,
-                               int32_t tile_width, int32_t tile_height, int32_t* tile_offsets,
-                               gs_stream_t stream) {
+extern "C" int gs_isect_offset_rows(int64_t n_isects, const int64_t* isect_ids, int32_t I,
+                                    int32_t tile_width, int32_t tile_height, int32_t tile_y0,
+                                    int32_t tile_y1, int32_t* tile_offsets, gs_stream_t stream) {
   if (I <= 0 || tile_width <= 0 || tile_height <= 0)
     return invalid("intersect_offset expects positive image and tile dimensions.");
   if (n_isects < 0 || n_isects > INT32_MAX) return invalid("intersect_offset: bad n_isects");
+  if (tile_y0 < 0 || tile_y1 > tile_height || tile_y1 <= tile_y0)
+    return invalid("intersect_offset: bad tile-row window");
   const int T = tile_width * tile_height;
   const int tb = gs_floor_log2_plus_one(T);
   if (!tile_offsets || (n_isects > 0 && !isect_ids)) return invalid("intersect_offset: missing buffer");
-  offset_kernel<<<grid_for((int64_t)I * T, 256), 256, 0, as_stream(stream)>>>(n_isects, isect_ids,
-                                                                             I, T, tb, tile_offsets);
+  const int rows = tile_y1 - tile_y0;
+  offset_kernel<<<grid_for((int64_t)I * rows * tile_width, 256), 256, 0, as_stream(stream)>>>(
+      n_isects, isect_ids, I, tile_width, tile_y0, rows, tb, tile_offsets);
   return launch_status("intersect_offset");
+}
+
+extern "C" int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,
+                               int32_t tile_width, int32_t tile_height, int32_t* tile_offsets,
+                               gs_stream_t stream) {
+  return gs_isect_offset_rows(n_isects, isect_ids, I, tile_width, tile_height, 0, tile_height,
+                              tile_offsets, stream);
 }
 
 // ------------------------------------------------------------ no-alloc sort

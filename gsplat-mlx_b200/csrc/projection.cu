@@ -110,6 +110,7 @@ struct FwdArgs {
   int B, C, N, W, H;
   float eps2d, near_plane, far_plane, radius_clip;
   int calc_comp, camera_model, use_covars, use_opacities;
+  int quats16;  // quats on a 16-byte boundary: read them as one float4
   const float *means, *covars, *quats, *scales, *opacities, *viewmats, *Ks;
   float *means2d, *depths, *conics, *comps;
   int32_t* radii;
@@ -126,6 +127,21 @@ __global__ void __launch_bounds__(256) proj_fwd_kernel(FwdArgs a) {
     const Cam cam = load_cam(a.viewmats + bc * 16, a.Ks + bc * 9);
     const float mw[3] = {__ldg(a.means + g * 3), __ldg(a.means + g * 3 + 1),
                          __ldg(a.means + g * 3 + 2)};
+    // quats / scales are read together with the means (before the near/far
+    // test that may cull the entry), so their latency is not exposed twice
+    float q[4] = {0.f, 0.f, 0.f, 0.f}, sc[3] = {0.f, 0.f, 0.f};
+    if (!a.use_covars) {
+      if (a.quats16) {
+        const float4 q4 = __ldg(reinterpret_cast<const float4*>(a.quats) + g);
+        q[0] = q4.x; q[1] = q4.y; q[2] = q4.z; q[3] = q4.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __ldg(a.quats + g * 4 + k);
+      }
+      sc[0] = __ldg(a.scales + g * 3);
+      sc[1] = __ldg(a.scales + g * 3 + 1);
+      sc[2] = __ldg(a.scales + g * 3 + 2);
+    }
     const M3& R = cam.R;
     const float mc0 = R.v[0] * mw[0] + R.v[1] * mw[1] + R.v[2] * mw[2] + cam.t[0];
     const float mc1 = R.v[3] * mw[0] + R.v[4] * mw[1] + R.v[5] * mw[2] + cam.t[1];
@@ -139,11 +155,7 @@ __global__ void __launch_bounds__(256) proj_fwd_kernel(FwdArgs a) {
       if (a.use_covars) {
         cw = covar6(a.covars + g * 6);
       } else {
-        const float q[4] = {__ldg(a.quats + g * 4), __ldg(a.quats + g * 4 + 1),
-                            __ldg(a.quats + g * 4 + 2), __ldg(a.quats + g * 4 + 3)};
-        const float s[3] = {__ldg(a.scales + g * 3), __ldg(a.scales + g * 3 + 1),
-                            __ldg(a.scales + g * 3 + 2)};
-        cw = covar_qs(q, s);
+        cw = covar_qs(q, sc);
       }
       const M3 cc = mul(mul(R, cw), tr(R));
       const float x = mc0, y = mc1, z = mc2;
@@ -526,8 +538,9 @@ extern "C" int gs_projection_fwd(const gs_projection_params* p, const float* mea
   if (p->camera_model < 0 || p->camera_model > 2) return invalid("projection_fwd: camera_model");
   FwdArgs a{p->B, p->C, p->N, p->image_width, p->image_height, p->eps2d, p->near_plane,
             p->far_plane, p->radius_clip, p->calc_compensations, p->camera_model,
-            p->use_covars, p->use_opacities, means, covars, quats, scales, opacities,
-            viewmats, Ks, means2d, depths, conics, compensations, radii};
+            p->use_covars, p->use_opacities,
+            (int)((reinterpret_cast<uintptr_t>(quats) & 15) == 0), means, covars, quats, scales,
+            opacities, viewmats, Ks, means2d, depths, conics, compensations, radii};
   proj_fwd_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(a);
   return launch_status("projection_fwd");
 }

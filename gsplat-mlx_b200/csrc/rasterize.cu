@@ -47,6 +47,7 @@ __device__ __forceinline__ Sigma gauss_sigma(float dx, float dy, float c0, float
 
 struct RArgs {
   int I, N, CH, W, H, ts, tw, th;
+  int ty0, rows;  // tile rows [ty0, ty0 + rows) are rendered (all: 0, th)
   int64_t n_isects;
   const float* means2d;
   const float* conics;
@@ -58,10 +59,30 @@ struct RArgs {
   const int32_t* flatten_ids;
 };
 
-__device__ __forceinline__ void tile_range(const RArgs& a, int64_t tile, int& start, int& end) {
-  const int64_t n_tiles_total = (int64_t)a.I * a.tw * a.th;
-  start = __ldg(a.tile_offsets + tile);
-  end = (tile + 1 == n_tiles_total) ? (int)a.n_isects : __ldg(a.tile_offsets + tile + 1);
+// The CTA's tile: `slot` indexes tile_offsets ([I, rows, tw]), `mask` the
+// masks ([I, th, tw]).
+struct TileIdx {
+  int64_t slot, mask;
+  int image, tile_x, tile_y;
+};
+
+__device__ __forceinline__ TileIdx tile_of(const RArgs& a) {
+  TileIdx t;
+  t.slot = blockIdx.x;
+  const int64_t per = (int64_t)a.rows * a.tw;
+  t.image = (int)(t.slot / per);
+  const int loc = (int)(t.slot - (int64_t)t.image * per);
+  const int ly = loc / a.tw;
+  t.tile_x = loc - ly * a.tw;
+  t.tile_y = a.ty0 + ly;
+  t.mask = ((int64_t)t.image * a.th + t.tile_y) * a.tw + t.tile_x;
+  return t;
+}
+
+__device__ __forceinline__ void tile_range(const RArgs& a, int64_t slot, int& start, int& end) {
+  const int64_t n_slots = (int64_t)a.I * a.rows * a.tw;
+  start = __ldg(a.tile_offsets + slot);
+  end = (slot + 1 == n_slots) ? (int)a.n_isects : __ldg(a.tile_offsets + slot + 1);
 }
 
 // ------------------------------------------------------------------ forward
@@ -78,18 +99,15 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   float4* s_co = reinterpret_cast<float4*>(smem + 2 * BLOCK);  // conic xyz, opacity
   float* s_col = smem + 6 * BLOCK;                              // [BLOCK][ch]
 
-  const int64_t tile = blockIdx.x;
-  const int T = a.tw * a.th;
-  const int image = (int)(tile / T);
-  const int t = (int)(tile - (int64_t)image * T);
-  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const TileIdx ti = tile_of(a);
+  const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x;
   const int ly = tid / a.ts, lx = tid - ly * a.ts;
   const int x = tile_x * a.ts + lx, y = tile_y * a.ts + ly;
   const bool inside = tid < a.ts * a.ts && x < a.W && y < a.H;
   const int64_t pix = ((int64_t)image * a.H + y) * a.W + x;
 
-  if (a.masks && !a.masks[tile]) {
+  if (a.masks && !a.masks[ti.mask]) {
     if (inside) {
       for (int c = 0; c < ch; ++c)
         render_colors[pix * ch + c] = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
@@ -99,7 +117,7 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
     return;
   }
   int start, end;
-  tile_range(a, tile, start, end);
+  tile_range(a, ti.slot, start, end);
   const float px = (float)x + 0.5f, py = (float)y + 0.5f;
   float Tr = 1.0f;
   int cur = 0;
@@ -262,20 +280,17 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
   __shared__ int s_last;
   __shared__ float s_bg[kMaxChannels];
 
-  const int64_t tile = blockIdx.x;
-  const int T = a.tw * a.th;
-  const int image = (int)(tile / T);
-  const int t = (int)(tile - (int64_t)image * T);
-  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const TileIdx ti = tile_of(a);
+  const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x, lane = tid & 31;
   const int ly = tid / a.ts, lx = tid - ly * a.ts;
   const int x = tile_x * a.ts + lx, y = tile_y * a.ts + ly;
   const bool inside = tid < a.ts * a.ts && x < a.W && y < a.H;
   const int64_t pix = ((int64_t)image * a.H + y) * a.W + x;
 
-  if (a.masks && !a.masks[tile]) return;
+  if (a.masks && !a.masks[ti.mask]) return;
   int start, end;
-  tile_range(a, tile, start, end);
+  tile_range(a, ti.slot, start, end);
 
   const float px = (float)x + 0.5f, py = (float)y + 0.5f;
   const float T_final = inside ? 1.0f - __ldg(render_alphas + pix) : 1.0f;
@@ -418,13 +433,15 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
 }
 
 // ------------------------------------------------------------------ 16x16 tiles
-// The common 16x16 tile runs on 128 threads: thread t owns pixels
-// (t % 16, t / 16) and (t % 16, t / 16 + 8).  Per staged Gaussian the shared
-// loads, the loop control and -- in the backward -- the warp reduction are
-// shared by 64 pixels per warp instead of 32.  Gaussians are staged packed:
-// a = (mean x, mean y, conic0, conic1), b = (conic2, opacity, col0, col1),
-// c = (col2, col3).  Per-pixel arithmetic is unchanged.
-constexpr int kT16Threads = 128;
+// The common 16x16 tile runs on 256 / P threads, each owning P pixels of one
+// column: thread t has pixels (t % 16, t / 16 + q * 16 / P), q < P.  Per
+// staged Gaussian the shared loads, the loop control and -- in the backward
+// -- the warp reduction are shared by 32 P pixels per warp.  Gaussians are
+// staged packed: a = (mean x, mean y, conic0, conic1), b = (conic2, opacity,
+// col0, col1), c = (col2, col3), in batches of one per thread.  Per-pixel
+// arithmetic is unchanged.
+constexpr int kT16Pixels = 4;                     // P
+constexpr int kT16Threads = 256 / kT16Pixels;
 
 // Can the Gaussian reach alpha >= 1/255 at any pixel centre of the tile?
 // sigma(d) = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy is convex for a positive
@@ -531,31 +548,30 @@ __device__ __forceinline__ void composite16(float dx, float dy, const float4& A,
 }
 
 template <int CH>
-__global__ void __launch_bounds__(kT16Threads, 10) raster_fwd16_kernel(
+__global__ void __launch_bounds__(kT16Threads) raster_fwd16_kernel(
     RArgs a, float* __restrict__ render_colors, float* __restrict__ render_alphas,
     int32_t* __restrict__ last_ids) {
+  constexpr int P = kT16Pixels, RS = 16 / P;  // pixels per thread, row stride
   __shared__ float4 s_a[kT16Threads];
   __shared__ float4 s_b[kT16Threads];
   __shared__ float2 s_c[kT16Threads];
   __shared__ int s_idx[kT16Threads];
   __shared__ int s_wcnt[kT16Threads / 32];
-  const int64_t tile = blockIdx.x;
-  const int T = a.tw * a.th;
-  const int image = (int)(tile / T);
-  const int t = (int)(tile - (int64_t)image * T);
-  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const TileIdx ti = tile_of(a);
+  const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x;
   const int x = tile_x * 16 + (tid & 15);
-  const int y0 = tile_y * 16 + (tid >> 4), y1 = y0 + 8;
-  const bool in0 = x < a.W && y0 < a.H, in1 = x < a.W && y1 < a.H;
-  const int64_t pix0 = ((int64_t)image * a.H + y0) * a.W + x;
-  const int64_t pix1 = pix0 + 8 * (int64_t)a.W;
-
-  if (a.masks && !a.masks[tile]) {
+  const int ybase = tile_y * 16 + (tid >> 4);
+  bool in[P];
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      if (!(q ? in1 : in0)) continue;
-      const int64_t pix = q ? pix1 : pix0;
+  for (int q = 0; q < P; ++q) in[q] = x < a.W && ybase + q * RS < a.H;
+  const int64_t pix0 = ((int64_t)image * a.H + ybase) * a.W + x;
+
+  if (a.masks && !a.masks[ti.mask]) {
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      if (!in[q]) continue;
+      const int64_t pix = pix0 + (int64_t)q * RS * a.W;
 #pragma unroll
       for (int c = 0; c < CH; ++c)
         render_colors[pix * CH + c] = a.backgrounds ? __ldg(a.backgrounds + image * CH + c) : 0.0f;
@@ -565,21 +581,33 @@ __global__ void __launch_bounds__(kT16Threads, 10) raster_fwd16_kernel(
     return;
   }
   int start, end;
-  tile_range(a, tile, start, end);
-  const float px = (float)x + 0.5f, py0 = (float)y0 + 0.5f, py1 = (float)y1 + 0.5f;
-  float T0 = 1.0f, T1 = 1.0f;
-  int cur0 = 0, cur1 = 0;
-  bool d0 = !in0, d1 = !in1;
-  float acc0[CH], acc1[CH];
+  tile_range(a, ti.slot, start, end);
+  const float px = (float)x + 0.5f;
+  float py[P], Tr[P], acc[P][CH];
+  int cur[P];
+  bool dn[P];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) acc0[c] = acc1[c] = 0.0f;
+  for (int q = 0; q < P; ++q) {
+    py[q] = (float)(ybase + q * RS) + 0.5f;
+    Tr[q] = 1.0f;
+    cur[q] = 0;
+    dn[q] = !in[q];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) acc[q][c] = 0.0f;
+  }
+  auto all_done = [&]() {
+    bool d = true;
+#pragma unroll
+    for (int q = 0; q < P; ++q) d = d && dn[q];
+    return d;
+  };
 
   for (int b0 = start; b0 < end; b0 += kT16Threads) {
-    if (__syncthreads_count(!(d0 && d1)) == 0) break;
+    if (__syncthreads_count(!all_done()) == 0) break;
     const int cnt = stage16<CH>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
                                 s_c, s_idx, nullptr, s_wcnt);
     for (int j = 0; j < cnt; ++j) {
-      if (d0 && d1) break;
+      if (all_done()) break;
       const float4 A = s_a[j];
       const float4 B = s_b[j];
       float col[4] = {B.z, B.w, 0.0f, 0.0f};
@@ -590,22 +618,22 @@ __global__ void __launch_bounds__(kT16Threads, 10) raster_fwd16_kernel(
       }
       const float dx = A.x - px;
       const int idx = s_idx[j];
-      if (!d0) composite16<CH>(dx, A.y - py0, A, B, col, T0, acc0, cur0, d0, idx);
-      if (!d1) composite16<CH>(dx, A.y - py1, A, B, col, T1, acc1, cur1, d1, idx);
+#pragma unroll
+      for (int q = 0; q < P; ++q)
+        if (!dn[q]) composite16<CH>(dx, A.y - py[q], A, B, col, Tr[q], acc[q], cur[q], dn[q], idx);
     }
   }
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    if (!(q ? in1 : in0)) continue;
-    const int64_t pix = q ? pix1 : pix0;
-    const float Tr = q ? T1 : T0;
-    render_alphas[pix] = 1.0f - Tr;
+  for (int q = 0; q < P; ++q) {
+    if (!in[q]) continue;
+    const int64_t pix = pix0 + (int64_t)q * RS * a.W;
+    render_alphas[pix] = 1.0f - Tr[q];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const float bg = a.backgrounds ? __ldg(a.backgrounds + image * CH + c) : 0.0f;
-      render_colors[pix * CH + c] = (q ? acc1[c] : acc0[c]) + Tr * bg;
+      render_colors[pix * CH + c] = acc[q][c] + Tr[q] * bg;
     }
-    last_ids[pix] = q ? cur1 : cur0;
+    last_ids[pix] = cur[q];
   }
 }
 
@@ -661,12 +689,13 @@ __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, co
 }
 
 template <int CH, bool ABS>
-__global__ void __launch_bounds__(kT16Threads, 8) raster_bwd16_kernel(
+__global__ void __launch_bounds__(kT16Threads) raster_bwd16_kernel(
     RArgs a, const float* __restrict__ render_alphas, const int32_t* __restrict__ last_ids,
     const float* __restrict__ v_render_colors, const float* __restrict__ v_render_alphas,
     int absgrad, float* __restrict__ v_means2d_abs, float* __restrict__ v_means2d,
     float* __restrict__ v_conics, float* __restrict__ v_colors, float* __restrict__ v_opacities,
     float* __restrict__ v_backgrounds) {
+  constexpr int P = kT16Pixels, RS = 16 / P;  // pixels per thread, row stride
   constexpr int CB = ABS ? 8 : 6;  // index of the first colour term
   constexpr int NT = CB + CH;      // gradient terms per Gaussian
   __shared__ float4 s_a[kT16Threads];
@@ -678,53 +707,56 @@ __global__ void __launch_bounds__(kT16Threads, 8) raster_bwd16_kernel(
   __shared__ float s_acc[kT16Threads * NT];
   __shared__ int s_last;
   __shared__ float s_bg[4];
-  const int64_t tile = blockIdx.x;
-  const int T = a.tw * a.th;
-  const int image = (int)(tile / T);
-  const int t = (int)(tile - (int64_t)image * T);
-  const int tile_y = t / a.tw, tile_x = t - tile_y * a.tw;
+  const TileIdx ti = tile_of(a);
+  const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x, lane = tid & 31;
   const int x = tile_x * 16 + (tid & 15);
-  const int y0 = tile_y * 16 + (tid >> 4), y1 = y0 + 8;
-  const bool in0 = x < a.W && y0 < a.H, in1 = x < a.W && y1 < a.H;
-  const int64_t pix0 = ((int64_t)image * a.H + y0) * a.W + x;
-  const int64_t pix1 = pix0 + 8 * (int64_t)a.W;
-  if (a.masks && !a.masks[tile]) return;
+  const int ybase = tile_y * 16 + (tid >> 4);
+  if (a.masks && !a.masks[ti.mask]) return;
   int start, end;
-  tile_range(a, tile, start, end);
-  const float px = (float)x + 0.5f, py0 = (float)y0 + 0.5f, py1 = (float)y1 + 0.5f;
-  const float Tf0 = in0 ? 1.0f - __ldg(render_alphas + pix0) : 1.0f;
-  const float Tf1 = in1 ? 1.0f - __ldg(render_alphas + pix1) : 1.0f;
-  float T0 = Tf0, T1 = Tf1;
-  const int last0 = in0 ? min(end - 1, __ldg(last_ids + pix0)) : -1;
-  const int last1 = in1 ? min(end - 1, __ldg(last_ids + pix1)) : -1;
-  const float vra0 = in0 ? __ldg(v_render_alphas + pix0) : 0.0f;
-  const float vra1 = in1 ? __ldg(v_render_alphas + pix1) : 0.0f;
-  float vrc0[CH], vrc1[CH];
-  float bgd0 = 0.0f, bgd1 = 0.0f;
+  tile_range(a, ti.slot, start, end);
+  const float px = (float)x + 0.5f;
+  // per pixel: centre row, transmittance, last id, K = T_final (v_ra - bg.vrc),
+  // bufdot, colour cotangent
+  float py[P], Tr[P], K[P], bufdot[P], vrc[P][CH];
+  int last[P];
+  bool in[P];
+  int my_last = -1;
+  float bgsum[CH];
 #pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    vrc0[c] = in0 ? __ldg(v_render_colors + pix0 * CH + c) : 0.0f;
-    vrc1[c] = in1 ? __ldg(v_render_colors + pix1 * CH + c) : 0.0f;
-    if (a.backgrounds) {
-      const float bg = __ldg(a.backgrounds + image * CH + c);
-      bgd0 += bg * vrc0[c];
-      bgd1 += bg * vrc1[c];
+  for (int c = 0; c < CH; ++c) bgsum[c] = 0.0f;
+#pragma unroll
+  for (int q = 0; q < P; ++q) {
+    const int y = ybase + q * RS;
+    in[q] = x < a.W && y < a.H;
+    const int64_t pix = ((int64_t)image * a.H + y) * a.W + x;
+    py[q] = (float)y + 0.5f;
+    const float Tf = in[q] ? 1.0f - __ldg(render_alphas + pix) : 1.0f;
+    Tr[q] = Tf;
+    last[q] = in[q] ? min(end - 1, __ldg(last_ids + pix)) : -1;
+    my_last = max(my_last, last[q]);
+    const float vra = in[q] ? __ldg(v_render_alphas + pix) : 0.0f;
+    float bgd = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      vrc[q][c] = in[q] ? __ldg(v_render_colors + pix * CH + c) : 0.0f;
+      if (a.backgrounds) bgd += __ldg(a.backgrounds + image * CH + c) * vrc[q][c];
+      bgsum[c] += in[q] ? Tf * vrc[q][c] : 0.0f;
     }
+    K[q] = Tf * (vra - bgd);
+    bufdot[q] = 0.0f;
   }
-  const float K0 = Tf0 * (vra0 - bgd0), K1 = Tf1 * (vra1 - bgd1);
-  float bufdot0 = 0.0f, bufdot1 = 0.0f;
   if (tid < 4) s_bg[tid] = 0.0f;
   if (tid == 0) s_last = -1;
   __syncthreads();
   if (v_backgrounds) {
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const float v = warp_sum((in0 ? Tf0 * vrc0[c] : 0.0f) + (in1 ? Tf1 * vrc1[c] : 0.0f));
+      const float v = warp_sum(bgsum[c]);
       if (lane == 0) atomicAdd(&s_bg[c], v);
     }
   }
-  if (in0 || in1) atomicMax(&s_last, max(last0, last1));
+  if (my_last >= 0) atomicMax(&s_last, my_last);
   __syncthreads();
   if (v_backgrounds && tid < CH && s_bg[tid] != 0.0f)
     atomicAdd(v_backgrounds + image * CH + tid, s_bg[tid]);
@@ -751,15 +783,16 @@ __global__ void __launch_bounds__(kT16Threads, 8) raster_bwd16_kernel(
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = 0.0f;
       const float dx = A.x - px;
-      const bool v0 = backward16<CH, ABS>(idx <= last0, dx, A.y - py0, A, B, col, T0, bufdot0,
-                                          K0, vrc0, g);
-      const bool v1 = backward16<CH, ABS>(idx <= last1, dx, A.y - py1, A, B, col, T1, bufdot1,
-                                          K1, vrc1, g);
-      const unsigned active = __ballot_sync(0xffffffffu, v0 || v1);
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < P; ++q)
+        any |= backward16<CH, ABS>(idx <= last[q], dx, A.y - py[q], A, B, col, Tr[q], bufdot[q],
+                                   K[q], vrc[q], g);
+      const unsigned active = __ballot_sync(0xffffffffu, any);
       if (!active) continue;
       if (__popc(active) <= 2) {
         // Sparse warp: its one or two contributing lanes add directly.
-        if (v0 || v1) {
+        if (any) {
 #pragma unroll
           for (int k = 0; k < NT; ++k)
             if (g[k] != 0.0f) atomicAdd(&s_acc[j * NT + k], g[k]);
@@ -802,13 +835,13 @@ int smem_bytes(int block, int ch, bool bwd) {
 template <int CH>
 int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cudaStream_t s) {
   if (CH > 0 && a.ts == 16) {
-    raster_fwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.tw * a.th), kT16Threads, 0, s>>>(
+    raster_fwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.rows * a.tw), kT16Threads, 0, s>>>(
         a, rc, ra, li);
     return launch_status("rasterize_fwd");
   }
   const int smem = smem_bytes(block, a.CH, false);
   cudaFuncSetAttribute(raster_fwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const int64_t tiles = (int64_t)a.I * a.tw * a.th;
+  const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
   raster_fwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, rc, ra, li);
   return launch_status("rasterize_fwd");
 }
@@ -819,7 +852,7 @@ int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, co
                float* vop, float* vbg, cudaStream_t s) {
   if (CH > 0 && a.ts == 16) {
     constexpr int C1 = CH > 0 ? CH : 1;
-    const unsigned grid = (unsigned)((int64_t)a.I * a.tw * a.th);
+    const unsigned grid = (unsigned)((int64_t)a.I * a.rows * a.tw);
     if (absgrad)
       raster_bwd16_kernel<C1, true><<<grid, kT16Threads, 0, s>>>(a, ra, li, vrc, vra, absgrad,
                                                                  vabs, vm, vc, vcol, vop, vbg);
@@ -830,7 +863,7 @@ int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, co
   }
   const int smem = smem_bytes(block, a.CH, true);
   cudaFuncSetAttribute(raster_bwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const int64_t tiles = (int64_t)a.I * a.tw * a.th;
+  const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
   raster_bwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, ra, li, vrc, vra, absgrad, vabs, vm,
                                                              vc, vcol, vop, vbg);
   return launch_status("rasterize_bwd");
@@ -853,14 +886,22 @@ int check_raster(const gs_raster_params* p) {
   }
   if ((int64_t)p->I * p->tile_width * p->tile_height > INT32_MAX)
     return invalid("rasterize: too many tiles");
+  if (p->tile_y1 > p->tile_y0 && (p->tile_y0 < 0 || p->tile_y1 > p->tile_height))
+    return invalid("rasterize: bad tile-row window");
   return GS_OK;
 }
 
 RArgs make_args(const gs_raster_params* p, const float* means2d, const float* conics,
                 const float* colors, const float* opacities, const float* backgrounds,
                 const uint8_t* masks, const int32_t* tile_offsets, const int32_t* flatten_ids) {
+  int ty0 = 0, rows = p->tile_height;
+  if (p->tile_y1 > p->tile_y0) {
+    ty0 = p->tile_y0;
+    rows = p->tile_y1 - p->tile_y0;
+  }
   return RArgs{p->I, p->N, p->channels, p->image_width, p->image_height, p->tile_size,
-               p->tile_width, p->tile_height, p->n_isects, means2d, conics, colors, opacities,
+               p->tile_width, p->tile_height, ty0, rows, p->n_isects, means2d, conics, colors,
+               opacities,
                p->use_backgrounds ? backgrounds : nullptr, p->use_masks ? masks : nullptr,
                tile_offsets, flatten_ids};
 }
@@ -918,14 +959,15 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
   cudaStream_t s = as_stream(stream);
   const int64_t nG = (int64_t)p->I * p->N;
   const size_t f = sizeof(float);
-  if (nG > 0) {
+  if (nG > 0 && !p->accumulate) {
     if (cudaMemsetAsync(v_means2d, 0, f * 2 * nG, s) || cudaMemsetAsync(v_conics, 0, f * 3 * nG, s) ||
         cudaMemsetAsync(v_colors, 0, f * p->channels * nG, s) ||
         cudaMemsetAsync(v_opacities, 0, f * nG, s) ||
         (p->absgrad && cudaMemsetAsync(v_means2d_abs, 0, f * 2 * nG, s)))
       return launch_status("rasterize_bwd: zero gradients");
   }
-  if (p->use_backgrounds && cudaMemsetAsync(v_backgrounds, 0, f * p->I * p->channels, s))
+  if (p->use_backgrounds && !p->accumulate &&
+      cudaMemsetAsync(v_backgrounds, 0, f * p->I * p->channels, s))
     return launch_status("rasterize_bwd: zero v_backgrounds");
   if ((int64_t)p->image_width * p->image_height == 0) return launch_status("rasterize_bwd");
   if (!tile_offsets || !render_alphas || !last_ids || !v_render_colors || !v_render_alphas)

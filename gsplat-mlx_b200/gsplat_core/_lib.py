@@ -53,14 +53,15 @@ class AdamParams(ct.Structure):
 
 class IsectParams(ct.Structure):
     _fields_ = [("I", _i32), ("N", _i32), ("tile_size", _i32), ("tile_width", _i32),
-                ("tile_height", _i32)]
+                ("tile_height", _i32), ("tile_y0", _i32), ("tile_y1", _i32)]
 
 
 class RasterParams(ct.Structure):
     _fields_ = [("I", _i32), ("N", _i32), ("channels", _i32), ("image_width", _i32),
                 ("image_height", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32), ("n_isects", _i64), ("use_backgrounds", _i32),
-                ("use_masks", _i32), ("absgrad", _i32)]
+                ("use_masks", _i32), ("absgrad", _i32), ("tile_y0", _i32), ("tile_y1", _i32),
+                ("accumulate", _i32)]
 
 
 _P = ct.POINTER
@@ -80,6 +81,7 @@ SIGNATURES = {
     "gs_sh_glue_fwd": (ct.c_int, [_P(SHGlueParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gs_sh_glue_bwd": (ct.c_int, [_P(SHGlueParams), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gs_isect_tile_count": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp]),
+    "gs_isect_tile_count_total": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _vp]),
     "gs_isect_scan_workspace_size": (_sz, [_i64]),
     "gs_isect_scan": (ct.c_int, [_i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_tile_encode": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
@@ -91,6 +93,7 @@ SIGNATURES = {
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "gs_isect_offset_rows": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "gs_isect_sort_noalloc": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gs_fit_activate": (ct.c_int, [_i64] + [_vp] * 9),
     "gs_l2_loss_grad": (ct.c_int, [_i64] + [_vp] * 5),

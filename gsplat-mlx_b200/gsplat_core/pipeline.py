@@ -77,7 +77,8 @@ class TrainingStep:
     C cameras of one scene (B = 1, I = C images)."""
 
     def __init__(self, n, sh_degree, K, cameras, width, height, tile_size=16, eps2d=0.3,
-                 near_plane=0.01, far_plane=1e10, device=None, use_background=True):
+                 near_plane=0.01, far_plane=1e10, device=None, use_background=True,
+                 max_isects_per_pass=1 << 30):
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
         self.N, self.deg, self.K, self.C = int(n), int(sh_degree), int(K), int(cameras)
         self.W, self.H, self.ts = int(width), int(height), int(tile_size)
@@ -85,6 +86,8 @@ class TrainingStep:
         self.th = (self.H + self.ts - 1) // self.ts
         self.eps2d, self.near, self.far = float(eps2d), float(near_plane), float(far_plane)
         self.lib = _lib.load()
+        self.max_isects_per_pass = int(max_isects_per_pass)
+        self.bands = 1
         f32, i32 = torch.float32, torch.int32
         C, N = self.C, self.N
         e = lambda shape, dt=f32: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
@@ -93,10 +96,9 @@ class TrainingStep:
         self.conics, self.radii = e((C, N, 3)), e((C, N, 2), i32)
         self.colors = e((C, N, 3))
         self.opac_cn = e((C, N)) if C > 1 else None
-        self.tiles_per_gauss, self.g_offsets = e((C, N), i32), e((C, N), i32)
+        self.tiles_per_gauss = e((C, N), i32)
         self.total = torch.zeros((1,), dtype=torch.int64, device=self.dev)
         self.total_host = torch.zeros((1,), dtype=torch.int64, pin_memory=True)
-        self.scan_ws = e((max(1, self.lib.gs_isect_scan_workspace_size(C * N)),), torch.uint8)
         self.tile_offsets = e((C, self.th, self.tw), i32)
         self.render_colors = e((C, self.H, self.W, 3))
         self.render_alphas = e((C, self.H, self.W, 1))
@@ -155,7 +157,14 @@ class TrainingStep:
         ``self.v_colors`` holds their gradient (the image-fitting trainer).
         ``target`` [C,H,W,3] replaces the given cotangents by those of the
         L2 loss mean((render - target)^2), whose value lands in the device
-        scalar ``self.loss``."""
+        scalar ``self.loss``.
+
+        When the step has more than ``max_isects_per_pass`` intersections
+        (the int32 offsets of the operator surface cap one pass at 2^31), the
+        image is processed in bands of tile rows: each band gets its own
+        count / sorted encode / offsets / rasterize forward and backward
+        (accumulating into the same gradients), all bit-identical to one
+        pass over the rows of the band; projection and SH run once."""
         L, s = self.lib, _s()
         C, N = self.C, self.N
         self._mark("start")
@@ -173,57 +182,78 @@ class TrainingStep:
             self._mark("sh_fwd")
         else:
             sh_backward = False
-        ip = IsectParams(C, N, self.ts, self.tw, self.th)
-        check(L.gs_isect_tile_count(ct.byref(ip), _p(self.means2d), _p(self.radii),
-                                    _p(self.tiles_per_gauss), s), "isect_count")
-        check(L.gs_isect_scan(C * N, _p(self.tiles_per_gauss), _p(self.g_offsets),
-                              _p(self.total), _p(self.scan_ws), self.scan_ws.numel(), s),
-              "isect_scan")
-        self.total_host.copy_(self.total, non_blocking=True)
-        self._mark("isect_count_scan")
-        torch.cuda.current_stream().synchronize()  # the reference's host read of the total
-        m = int(self.total_host.item())
-        if m >= 2 ** 31:
-            raise RuntimeError(f"{m} intersections exceed the int32 index range")
-        self._ensure_capacity(m)
-        self.m = m
-        check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d), _p(self.radii),
-                                            _p(self.depths), _p(self.tiles_per_gauss), m,
-                                            _p(self.sorted_ids), _p(self.sorted_flatten),
-                                            _p(self.sort_ws), self.sort_ws.numel(), s),
-              "isect_encode_sort")
-        self._mark("isect_encode_sort")
-        check(L.gs_isect_offset(m, _p(self.sorted_ids), C, self.tw, self.th,
-                                _p(self.tile_offsets), s), "isect_offset")
-        self._mark("isect_offset")
         if C > 1:
             self.opac_cn.copy_(opacities.view(1, N).expand(C, N))
             opac = self.opac_cn
         else:
             opac = opacities
-        rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
-                          int(self.backgrounds is not None), 0, 0)
-        check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(colors),
-                                 _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
-                                 _p(self.sorted_flatten), _p(self.render_colors),
-                                 _p(self.render_alphas), _p(self.last_ids), s), "rasterize_fwd")
-        self._mark("rasterize_fwd")
-        if target is not None:
-            if not hasattr(self, "loss"):
-                self.loss = torch.zeros((1,), dtype=torch.float32, device=self.dev)
-                self.v_rc_loss = torch.empty_like(self.render_colors)
-                self.v_ra_zero = torch.zeros_like(self.render_alphas)
-            check(L.gs_l2_loss_grad(self.render_colors.numel(), _p(self.render_colors),
-                                    _p(target), _p(self.v_rc_loss), _p(self.loss), s), "l2_loss")
-            v_render_colors, v_render_alphas = self.v_rc_loss, self.v_ra_zero
-            self._mark("loss")
         v_opac = self.v_opacities if C == 1 else self.v_opac_cn
-        check(L.gs_rasterize_bwd(ct.byref(rp), _p(self.means2d), _p(self.conics), _p(colors),
-                                 _p(opac), _p(self.backgrounds), None, _p(self.tile_offsets),
-                                 _p(self.sorted_flatten), _p(self.render_alphas),
-                                 _p(self.last_ids), _p(v_render_colors), _p(v_render_alphas),
-                                 None, _p(self.v_means2d), _p(self.v_conics), _p(self.v_colors),
-                                 _p(v_opac), _p(self.v_backgrounds), s), "rasterize_bwd")
+        m_total = 0
+        bands = [(0, 0)]  # (0, 0): every tile row in one pass
+        b = 0
+        while b < len(bands):
+            y0, y1 = bands[b]
+            ip = IsectParams(C, N, self.ts, self.tw, self.th, y0, y1)
+            check(L.gs_isect_tile_count_total(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                              _p(self.tiles_per_gauss), _p(self.total), s),
+                  "isect_count")
+            self.total_host.copy_(self.total, non_blocking=True)
+            self._mark("isect_count")
+            torch.cuda.current_stream().synchronize()  # the reference's host read of the total
+            m = int(self.total_host.item())
+            if m > self.max_isects_per_pass and y1 == 0:
+                # too many intersections for one pass (int32 offsets, memory):
+                # bands of tile rows, each with its own intersection pass
+                if target is not None:
+                    raise RuntimeError("the L2-target mode renders in one pass; "
+                                       f"{m} intersections exceed max_isects_per_pass")
+                rows = max(1, int(self.th * self.max_isects_per_pass // (2 * m)))
+                bands = [(r, min(r + rows, self.th)) for r in range(0, self.th, rows)]
+                continue
+            if m >= 2 ** 31:
+                raise RuntimeError(f"{m} intersections exceed the int32 index range"
+                                   + (f" in tile rows {y0}..{y1}" if y1 else ""))
+            self._ensure_capacity(m)
+            self.m = m
+            m_total += m
+            check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                                _p(self.depths), _p(self.tiles_per_gauss), m,
+                                                _p(self.sorted_ids), _p(self.sorted_flatten),
+                                                _p(self.sort_ws), self.sort_ws.numel(), s),
+                  "isect_encode_sort")
+            self._mark("isect_encode_sort")
+            r0, r1 = (y0, y1) if y1 else (0, self.th)
+            check(L.gs_isect_offset_rows(m, _p(self.sorted_ids), C, self.tw, self.th, r0, r1,
+                                         _p(self.tile_offsets), s), "isect_offset")
+            self._mark("isect_offset")
+            rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
+                              int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0))
+            check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics),
+                                     _p(colors), _p(opac), _p(self.backgrounds), None,
+                                     _p(self.tile_offsets), _p(self.sorted_flatten),
+                                     _p(self.render_colors), _p(self.render_alphas),
+                                     _p(self.last_ids), s), "rasterize_fwd")
+            self._mark("rasterize_fwd")
+            if target is not None:
+                if not hasattr(self, "loss"):
+                    self.loss = torch.zeros((1,), dtype=torch.float32, device=self.dev)
+                    self.v_rc_loss = torch.empty_like(self.render_colors)
+                    self.v_ra_zero = torch.zeros_like(self.render_alphas)
+                check(L.gs_l2_loss_grad(self.render_colors.numel(), _p(self.render_colors),
+                                        _p(target), _p(self.v_rc_loss), _p(self.loss), s),
+                      "l2_loss")
+                v_render_colors, v_render_alphas = self.v_rc_loss, self.v_ra_zero
+                self._mark("loss")
+            check(L.gs_rasterize_bwd(ct.byref(rp), _p(self.means2d), _p(self.conics),
+                                     _p(colors), _p(opac), _p(self.backgrounds), None,
+                                     _p(self.tile_offsets), _p(self.sorted_flatten),
+                                     _p(self.render_alphas), _p(self.last_ids),
+                                     _p(v_render_colors), _p(v_render_alphas), None,
+                                     _p(self.v_means2d), _p(self.v_conics), _p(self.v_colors),
+                                     _p(v_opac), _p(self.v_backgrounds), s), "rasterize_bwd")
+            b += 1
+        m = m_total
+        self.bands = len(bands)
         self._mark("rasterize_bwd")
         if C > 1:
             torch.sum(self.v_opac_cn, dim=0, out=self.v_opacities)

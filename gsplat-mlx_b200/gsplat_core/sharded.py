@@ -125,6 +125,7 @@ class ShardedTrainingStep:
                                             device=self.step.dev)
             self.v_means_sh = torch.empty((self.N, 3), dtype=torch.float32, device=self.step.dev)
 
+
     def local(self, t):
         """This rank's slice of a per-camera tensor [C_total, ...]."""
         return t[self.start:self.stop]

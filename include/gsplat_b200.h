@@ -166,12 +166,22 @@ typedef struct {
   int32_t I;          /* images (B*C)                                    */
   int32_t N;          /* Gaussians per image                             */
   int32_t tile_size, tile_width, tile_height;
+  int32_t tile_y0, tile_y1; /* when tile_y1 > tile_y0: only tile rows
+                               [tile_y0, tile_y1) are intersected (a band of
+                               the image; keys keep absolute tile ids); else
+                               all rows, as the reference */
 } gs_isect_params;
 
 /* tiles_per_gauss [I,N] int32 */
 int gs_isect_tile_count(const gs_isect_params* p, const float* means2d,
                         const int32_t* radii, int32_t* tiles_per_gauss,
                         gs_stream_t stream);
+/* The same counts and, in one pass, their total into a device int64 (the
+ * total that gs_isect_scan also produces), for callers that need only the
+ * total before the sorted encode.  No reference counterpart. */
+int gs_isect_tile_count_total(const gs_isect_params* p, const float* means2d,
+                              const int32_t* radii, int32_t* tiles_per_gauss,
+                              int64_t* total_device, gs_stream_t stream);
 
 /* Exclusive prefix sum of n int32 counts into offsets (int32, as the
  * reference's cumsum), and the 64-bit total into *total_device (a device
@@ -248,6 +258,12 @@ int gs_isect_sort_noalloc(int64_t n_isects, int32_t key_bits,
 int gs_isect_offset(int64_t n_isects, const int64_t* isect_ids, int32_t I,
                     int32_t tile_width, int32_t tile_height,
                     int32_t* tile_offsets, gs_stream_t stream);
+/* The offsets of tile rows [tile_y0, tile_y1) only, into tile_offsets
+ * [I, tile_y1 - tile_y0, tile_width] (a band of the image, with isect_ids
+ * from an intersect call with the same window).  No reference counterpart. */
+int gs_isect_offset_rows(int64_t n_isects, const int64_t* isect_ids, int32_t I,
+                         int32_t tile_width, int32_t tile_height, int32_t tile_y0,
+                         int32_t tile_y1, int32_t* tile_offsets, gs_stream_t stream);
 
 /* Helper of the staged pipeline: tile_bits = floor(log2(n)) + 1, the
  * reference's floor_log2_plus_one (gsplat_intersect.cpp:60-65). */
@@ -266,6 +282,12 @@ typedef struct {
   int64_t n_isects;
   int32_t use_backgrounds, use_masks;
   int32_t absgrad; /* bwd: write v_means2d_abs */
+  int32_t tile_y0, tile_y1; /* when tile_y1 > tile_y0: only tile rows
+                               [tile_y0, tile_y1) are rendered (a band;
+                               tile_offsets is then [I, rows, tile_width] and
+                               flatten_ids / n_isects the band's); else all */
+  int32_t accumulate; /* bwd: add into the gradient outputs instead of
+                         zeroing them first (bands after the first) */
 } gs_raster_params;
 
 /* render_colors [I,H,W,ch], render_alphas [I,H,W,1], last_ids [I,H,W] */

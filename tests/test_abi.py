@@ -54,8 +54,8 @@ def test_param_struct_layouts(gs):
     assert ct.sizeof(L.ProjectionParams) == 52
     assert ct.sizeof(L.SHParams) == 24
     assert ct.sizeof(L.SHGlueParams) == 24
-    assert ct.sizeof(L.IsectParams) == 20
-    assert ct.sizeof(L.RasterParams) == 56
+    assert ct.sizeof(L.IsectParams) == 28
+    assert ct.sizeof(L.RasterParams) == 64
 
 
 def test_host_helpers(gs):

@@ -121,3 +121,32 @@ def test_full_size_config3_properties(gs, oracle, cuda):
     assert m2 == m
     assert torch.equal(last0, step.last_ids)
     assert_grad_close(flat2, g, "repeat step", atol_frac=1e-5)
+
+
+
+def test_banded_passes_match_one_pass(gs, cuda):
+    """Past max_isects_per_pass the step renders bands of tile rows, each
+    with its own intersection pass: the same image bit for bit, and the
+    same gradients up to the order of the atomic additions."""
+    from gsplat_core import pipeline, synthetic as S
+    sc = S.config3(seed=2, n=200_000)
+    views = S.orbit(2, 4.0)
+    Ks = np.repeat(sc.Ks[:1], 2, 0).copy()
+    Ks[:, :2, :] /= 4
+    W, H = sc.width // 4, sc.height // 4
+    idx = np.sort(np.random.default_rng(1).choice(sc.n, size=30_000, replace=False))
+    vrc, vra = S.cotangents(8, 2, H, W)
+    args = [T(sc.means[idx]), T(sc.quats[idx]), T(sc.scales[idx]), T(sc.opacities[idx]),
+            T(sc.coeffs[idx]), T(views), T(Ks), T(vrc), T(vra)]
+    one = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H)
+    flat1, m1 = one.run(*args)
+    flat1 = flat1.clone()
+    banded = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H, max_isects_per_pass=m1 // 3)
+    flat2, m2 = banded.run(*args)
+    torch.cuda.synchronize()
+    banded.check()
+    assert one.bands == 1 and banded.bands > 2
+    assert m2 == m1
+    assert torch.equal(one.render_colors, banded.render_colors)
+    assert torch.equal(one.render_alphas, banded.render_alphas)
+    assert_grad_close(flat2, flat1, "banded vs one pass", atol_frac=1e-4)

@@ -121,6 +121,23 @@ def test_projection_fwd_exact(gs, oracle, cuda, cfg, n, use_opac, comp):
         assert tuple(g["compensations"].shape) == (0,)
 
 
+def test_projection_misaligned_quats(gs, oracle, cuda):
+    """Quaternions on a 4-byte (not 16-byte) boundary take the scalar load
+    path and give the same bits."""
+    sc, idx = _scene_subset("config3", 20_000)
+    quats = sc.quats[idx][None]
+    buf = torch.zeros(quats.size + 1, dtype=torch.float32, device="cuda")
+    buf[1:] = T(quats.ravel())
+    q_odd = buf[1:].view(quats.shape)
+    assert q_odd.data_ptr() % 16 != 0
+    base = {"means": T(sc.means[idx][None]), "scales": T(sc.scales[idx][None]),
+            "viewmats": T(sc.viewmats[None]), "Ks": T(sc.Ks[None])}
+    a = gs.projection_ewa_3dgs_fused_forward(dict(base, quats=T(quats)), sc.width, sc.height)
+    b = gs.projection_ewa_3dgs_fused_forward(dict(base, quats=q_odd), sc.width, sc.height)
+    for k in ("radii", "means2d", "depths", "conics"):
+        assert torch.equal(a[k], b[k]), k
+
+
 def test_projection_golden_and_covars(gs, golden, cuda):
     d = golden("ops")
     W, H = int(d["pc_width"]), int(d["pc_height"])
