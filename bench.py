@@ -194,11 +194,12 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
 
 
 def our_kernel_launches(sort_passes):
-    # projection fwd 1, glue fwd 1, count (+ total) 1, depth keys 1, element
-    # sort: digit histogram 1 + 4 onesweep passes, permuted scan 3, encode
-    # (+ tile/image digit histogram) 1, tile/image onesweep passes, offset 1,
-    # rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
-    return 1 + 1 + 1 + 1 + (1 + 4) + 3 + 1 + sort_passes + 1 + 1 + 1 + 1 + 1
+    # projection fwd 1, glue fwd 1, count (+ total) 1, visible compaction 3
+    # (block counts, their scan, packed depth words), element sort: digit
+    # histogram 1 + 4 onesweep passes, permuted scan 3, encode (+ tile/image
+    # digit histogram) 1, tile/image onesweep passes, offset 1, rasterize
+    # fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
+    return 1 + 1 + 1 + 3 + (1 + 4) + 3 + 1 + sort_passes + 1 + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -561,7 +562,10 @@ def run_ours(args):
             "data": f"synthetic (seeded, BASELINE {args.workload} distributions)",
             "config": {"workload": desc, "cameras": C_total,
                        "gaussians": sc.n, "visible": visible, "isects": m,
-                       "bwd_pixel_gaussian_pairs": composited_pairs(step),
+                       # (per band when the step renders bands of tile rows)
+                       "bwd_pixel_gaussian_pairs": (composited_pairs(step) if step.bands == 1
+                                                    else None),
+                       "bands": step.bands,
                        "parallelism": f"camera-sharded dp{world}" if world > 1 else "single",
                        "exchange": sharded.exchange if world > 1 else None,
                        "l2": "flushed (256 MB write) between timed steps"},

@@ -62,10 +62,17 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
     tiles_per_gauss[i] = c;
     sum += (unsigned long long)c;
   }
-  if (total) {
+  if (total) {  // one atomic per CTA
+    __shared__ unsigned long long s_sum[8];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((threadIdx.x & 31) == 0 && sum) atomicAdd(total, sum);
+    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long t = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_sum[w];
+      if (t) atomicAdd(total, t);
+    }
   }
 }
 
@@ -77,9 +84,11 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
 // starts at offsets[i] -- the reference's scan order (adjacent runs, so
 // stores are coalesced) or any other order of the runs; every write is
 // bounds-checked like the CPU path (gsplat_intersect.cpp:473).  With
-// `hist`, the kernel also counts the digits of the key bits above the depth
+// `packed_out`, each intersection is written there as one word (high key
+// word << 32 | element id) instead of to isect_ids / flatten_ids.
+// With `hist`, the kernel also counts the digits of the key bits above the depth
 // word for the radix passes that follow (hist[p][d], 8-bit digits from
-// bit 32).
+// bit 32, sign bit xor hist_flip: the digits the passes see).
 constexpr int kEncodeThreads = 256;
 constexpr int kEncodeWarps = kEncodeThreads / 32;
 
@@ -88,7 +97,8 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
     const int32_t* __restrict__ radii, const float* __restrict__ depths,
     const int32_t* __restrict__ offsets, int ts, int tw, int th, int ty0, int ty1, int tile_bits,
     int64_t n_isects, int64_t* __restrict__ isect_ids, int32_t* __restrict__ flatten_ids,
-    uint32_t* __restrict__ hist, int hist_passes) {
+    uint64_t* __restrict__ packed_out, uint32_t* __restrict__ hist, int hist_passes,
+    uint32_t hist_flip) {
   __shared__ int s_pref[kEncodeWarps][32];
   __shared__ int s_x0[kEncodeWarps][32], s_y0[kEncodeWarps][32], s_w[kEncodeWarps][32];
   __shared__ float s_invw[kEncodeWarps][32];
@@ -155,11 +165,16 @@ __global__ void __launch_bounds__(kEncodeThreads) encode_kernel(
         const int64_t pos = s_off[warp][o] + k;
         const int64_t key = s_base[warp][o] | ((int64_t)(y * tw + x) << 32);
         if (pos >= 0 && pos < n_isects) {
-          isect_ids[pos] = key;
-          flatten_ids[pos] = s_e[warp][o];
+          const uint32_t hi = (uint32_t)((uint64_t)key >> 32);
+          if (packed_out) {
+            packed_out[pos] = ((uint64_t)hi << 32) | (uint32_t)s_e[warp][o];
+          } else {
+            isect_ids[pos] = key;
+            flatten_ids[pos] = s_e[warp][o];
+          }
           if (hist) {
-            const uint32_t hi = (uint32_t)((uint64_t)key >> 32);
-            for (int p = 0; p < hist_passes; ++p) atomicAdd(&s_hist[p][(hi >> (8 * p)) & 0xFFu], 1u);
+            const uint32_t h = hi ^ hist_flip;
+            for (int p = 0; p < hist_passes; ++p) atomicAdd(&s_hist[p][(h >> (8 * p)) & 0xFFu], 1u);
           }
         }
       }
@@ -212,18 +227,28 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, int64_t* s_wa
   return excl;
 }
 
-// With `perm`, element i of the scanned sequence is in[perm[i]].
+// With `perm`, element i of the scanned sequence is in[perm[i * stride]]
+// (stride 2: the low words of packed 64-bit sort words); with `n_dev`, the
+// length is *n_dev (the grid covers the host bound n).
+__device__ __forceinline__ int32_t scan_value(const int32_t* in, const int32_t* perm, int stride,
+                                              int64_t i) {
+  return __ldg(in + (perm ? (int64_t)__ldg(perm + i * stride) : i));
+}
+
 __global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(int64_t n,
                                                                     const int32_t* __restrict__ in,
                                                                     const int32_t* __restrict__ perm,
+                                                                    int stride,
+                                                                    const int64_t* __restrict__ n_dev,
                                                                     int64_t* __restrict__ sums) {
   __shared__ int64_t s_warp[32];
+  if (n_dev) n = *n_dev;
   const int64_t base = (int64_t)blockIdx.x * kScanChunk;
   int64_t acc = 0;
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    if (i < n) acc += __ldg(in + (perm ? (int64_t)__ldg(perm + i) : i));
+    if (i < n) acc += scan_value(in, perm, stride, i);
   }
   int64_t total;
   block_exclusive_scan<kScanThreads>(acc, s_warp, &total);
@@ -255,16 +280,19 @@ __global__ void __launch_bounds__(1024) scan_sums_kernel(int64_t nb, int64_t* __
 // position i is stored at out[perm[i]] (scattered back to element order).
 __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, const int32_t* in,
                                                                   const int32_t* __restrict__ perm,
+                                                                  int stride,
+                                                                  const int64_t* __restrict__ n_dev,
                                                                   const int64_t* __restrict__ sums,
                                                                   int32_t* out) {
   __shared__ int64_t s_warp[32];
+  if (n_dev) n = *n_dev;
   const int64_t base = (int64_t)blockIdx.x * kScanChunk;
   int32_t v[kScanItems];
   int64_t acc = 0;
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    v[k] = i < n ? in[perm ? (int64_t)__ldg(perm + i) : i] : 0;
+    v[k] = i < n ? (perm ? scan_value(in, perm, stride, i) : in[i]) : 0;
     acc += v[k];
   }
   int64_t total;
@@ -272,7 +300,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, cons
 #pragma unroll
   for (int k = 0; k < kScanItems; ++k) {
     const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    if (i < n) out[perm ? (int64_t)__ldg(perm + i) : i] = (int32_t)run;
+    if (i < n) out[perm ? (int64_t)__ldg(perm + i * stride) : i] = (int32_t)run;
     run += v[k];
   }
 }
@@ -283,7 +311,8 @@ size_t scan_ws_bytes(int64_t n) {
 }
 
 int scan_i32(int64_t n, const int32_t* in, int32_t* out, int64_t* total, void* ws, size_t ws_bytes,
-             cudaStream_t s, const int32_t* perm = nullptr) {
+             cudaStream_t s, const int32_t* perm = nullptr, int perm_stride = 1,
+             const int64_t* n_dev = nullptr) {
   if (n <= 0) {
     if (total) cudaMemsetAsync(total, 0, sizeof(int64_t), s);
     return launch_status("scan");
@@ -294,10 +323,59 @@ int scan_i32(int64_t n, const int32_t* in, int32_t* out, int64_t* total, void* w
   }
   const int64_t nb = ceil_div(n, kScanChunk);
   int64_t* sums = static_cast<int64_t*>(ws);
-  scan_reduce_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, sums);
+  scan_reduce_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, perm_stride, n_dev, sums);
   scan_sums_kernel<<<1, 1024, 0, s>>>(nb, sums, total);
-  scan_down_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, sums, out);
+  scan_down_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, in, perm, perm_stride, n_dev, sums, out);
   return launch_status("scan");
+}
+
+// Visible elements -- both radii positive, a superset of the elements with
+// tiles in any tile-row window -- in element order: block counts, then
+// (with the scanned counts) packed words (depth bits << 32 | element) at
+// their compacted positions, the input of the depth sort.
+__device__ __forceinline__ int visible_at(const int32_t* radii, int64_t i) {
+  const int2 r = __ldg(reinterpret_cast<const int2*>(radii) + i);
+  return (r.x > 0 && r.y > 0) ? 1 : 0;
+}
+
+__global__ void __launch_bounds__(kScanThreads) visible_count_kernel(
+    int64_t n, const int32_t* __restrict__ radii, int64_t* __restrict__ sums) {
+  __shared__ int64_t s_warp[32];
+  const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int64_t acc = 0;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    if (i < n) acc += visible_at(radii, i);
+  }
+  int64_t total;
+  block_exclusive_scan<kScanThreads>(acc, s_warp, &total);
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kScanThreads) visible_depth_keys_kernel(
+    int64_t n, const int32_t* __restrict__ radii, const float* __restrict__ depths,
+    const int64_t* __restrict__ sums, uint64_t* __restrict__ words) {
+  __shared__ int64_t s_warp[32];
+  const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int f[kScanItems];
+  int64_t acc = 0;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    f[k] = i < n ? visible_at(radii, i) : 0;
+    acc += f[k];
+  }
+  int64_t total;
+  int64_t run = block_exclusive_scan<kScanThreads>(acc, s_warp, &total) + sums[blockIdx.x];
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    if (f[k]) {
+      const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+      words[run] = ((uint64_t)__float_as_uint(__ldg(depths + i)) << 32) | (uint32_t)i;
+      ++run;
+    }
+  }
 }
 
 // ------------------------------------------------------------ radix sort
@@ -334,8 +412,10 @@ __device__ __forceinline__ uint32_t digit_of(uint64_t k, int shift, uint64_t fli
 __global__ void __launch_bounds__(256) radix_hist_kernel(int64_t n,
                                                          const uint64_t* __restrict__ keys,
                                                          int begin_bit, int passes, uint64_t flip,
+                                                         const int64_t* __restrict__ n_dev,
                                                          uint32_t* __restrict__ hist) {
   __shared__ uint32_t s_hist[kMaxPasses][kRadix];
+  if (n_dev) n = *n_dev;
   for (int i = threadIdx.x; i < kMaxPasses * kRadix; i += blockDim.x) (&s_hist[0][0])[i] = 0;
   __syncthreads();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
@@ -357,14 +437,39 @@ __global__ void __launch_bounds__(256) radix_hist_kernel(int64_t n,
   }
 }
 
+// Key sources and sinks of a pass.
+//   kKV     64-bit keys and int32 values in two arrays (the plain key sort);
+//   kPacked one 64-bit word per key: (high key word << 32) | 32-bit value;
+//   kFinal  sink only: the word's value is an element e; the pass writes the
+//           full key (high word | bits of depths[e]) and e.
+enum PassIO { kKV = 0, kPacked = 1, kFinal = 2 };
+
+template <bool VALS>
 struct PassSmem {
   uint64_t keys[kSortTile];
-  int32_t vals[kSortTile];
+  int32_t vals[VALS ? kSortTile : 1];
   uint32_t hist[kSortWarps][kRadix];  // warp counts -> warp exclusive offsets
   uint32_t digit_start[kRadix];       // CTA-local exclusive prefix over digits
   uint64_t goff[kRadix];              // global offset of each digit for this tile
   int64_t warp_tot[32];
   int tile;
+};
+
+struct PassArgs {
+  int64_t n;
+  const uint64_t* keys_in;
+  const int32_t* vals_in;  // kKV
+  uint64_t* keys_out;      // kKV, kPacked; kFinal: the int64 keys
+  int32_t* vals_out;       // kKV; kFinal: the element ids
+  const float* depths;     // kFinal
+  int shift;
+  uint64_t flip;
+  int pass;
+  const uint32_t* pass_hist;
+  uint32_t* tile_counter;
+  uint64_t* state;
+  uint32_t* error_word;
+  const int64_t* n_dev;  // when set, the length is *n_dev (the grid covers n)
 };
 
 __device__ __forceinline__ uint64_t load_state(const uint64_t* p) {
@@ -377,30 +482,37 @@ __device__ __forceinline__ void store_state(uint64_t* p, uint64_t v) {
 // One digit pass.  state[tile][digit] = (tag << 32) | value with tag
 // 2*pass+1 (value = this tile's count) or 2*pass+2 (value = inclusive
 // prefix over tiles 0..tile); words of other passes or zero mean "not yet".
-__global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
-    int64_t n, const uint64_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
-    uint64_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int shift, uint64_t flip,
-    int pass, const uint32_t* __restrict__ pass_hist, uint32_t* __restrict__ tile_counter,
-    uint64_t* __restrict__ state, uint32_t* __restrict__ error_word) {
+template <int IN, int OUT>
+__global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(const PassArgs a) {
+  constexpr bool VALS = IN == kKV;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  PassSmem& sm = *reinterpret_cast<PassSmem*>(smem_raw);
+  PassSmem<VALS>& sm = *reinterpret_cast<PassSmem<VALS>*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) sm.tile = (int)atomicAdd(tile_counter, 1u);
+  if (threadIdx.x == 0) sm.tile = (int)atomicAdd(a.tile_counter, 1u);
   for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
   const int tile = sm.tile;
   const int64_t tile_base = (int64_t)tile * kSortTile;
+  int64_t n = a.n;
+  if (a.n_dev) {
+    // the grid covers the host bound; tiles past the device length leave
+    // (nothing waits on them: look-back only reads earlier tiles)
+    n = *a.n_dev;
+    if (tile_base >= n) return;
+  }
+  const int shift = a.shift;
+  const uint64_t flip = a.flip;
   const int64_t base = tile_base + (int64_t)warp * kWarpSpan;
   uint64_t k[kSortItems];
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {  // all loads in flight before ranking
     const int64_t i = base + r * 32 + lane;
-    k[r] = i < n ? __ldg(keys_in + i) : 0ull;
+    k[r] = i < n ? __ldg(a.keys_in + i) : 0ull;
   }
   // Stable ranks: a warp's keys in index order (round r covers keys
   // r*32..r*32+31 of its span), lanes in lane order; invalid lanes (past
-  // n) form their own group and count nowhere.
-  uint32_t rank[kSortItems];
+  // n) form their own group and count nowhere.  Two 16-bit ranks per word.
+  uint32_t rank[kSortItems / 2];
   const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
   for (int r = 0; r < kSortItems; ++r) {
@@ -422,7 +534,9 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
     __syncwarp();
     if (valid && lane == leader) sm.hist[warp][d] = cur + __popc(peers);
     __syncwarp();
-    rank[r] = cur + before;
+    const uint32_t rk = cur + before;
+    if (r & 1) rank[r >> 1] |= rk << 16;
+    else rank[r >> 1] = rk;
   }
   __syncthreads();
   const int d = threadIdx.x;  // one thread per digit
@@ -434,9 +548,9 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
     cta_count += c;
   }
   // Publish, then look back for the exclusive prefix over earlier tiles.
-  const uint64_t tag_agg = (uint64_t)(2 * pass + 1) << 32;
-  const uint64_t tag_inc = (uint64_t)(2 * pass + 2) << 32;
-  uint64_t* my = state + (int64_t)tile * kRadix + d;
+  const uint64_t tag_agg = (uint64_t)(2 * a.pass + 1) << 32;
+  const uint64_t tag_inc = (uint64_t)(2 * a.pass + 2) << 32;
+  uint64_t* my = a.state + (int64_t)tile * kRadix + d;
   uint64_t excl = 0;
   if (tile == 0) {
     store_state(my, tag_inc | cta_count);
@@ -451,16 +565,16 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
       uint64_t w[kLookback];
 #pragma unroll
       for (int i = 0; i < kLookback; ++i)
-        w[i] = t0 - i >= 0 ? load_state(state + (int64_t)(t0 - i) * kRadix + d) : tag_inc;
+        w[i] = t0 - i >= 0 ? load_state(a.state + (int64_t)(t0 - i) * kRadix + d) : tag_inc;
 #pragma unroll
       for (int i = 0; i < kLookback; ++i) {
         if (found) break;
-        const uint64_t* q = state + (int64_t)(t0 - i) * kRadix + d;
+        const uint64_t* q = a.state + (int64_t)(t0 - i) * kRadix + d;
         uint64_t v = w[i];
         uint32_t spins = 0;
         while ((v & ~0xFFFFFFFFull) != tag_agg && (v & ~0xFFFFFFFFull) != tag_inc) {
           if (++spins > kSpinLimit) {
-            atomicOr(error_word, 1u);
+            atomicOr(a.error_word, 1u);
             v = tag_inc;  // give up: count 0, stop walking
             break;
           }
@@ -475,7 +589,8 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
   }
   // Global digit bases: exclusive scan of this pass's digit totals.
   int64_t unused;
-  const int64_t dbase = block_exclusive_scan<kSortThreads>(__ldg(pass_hist + d), sm.warp_tot, &unused);
+  const int64_t dbase =
+      block_exclusive_scan<kSortThreads>(__ldg(a.pass_hist + d), sm.warp_tot, &unused);
   sm.goff[d] = (uint64_t)dbase + excl;
   int64_t total;
   const int64_t start = block_exclusive_scan<kSortThreads>(cta_count, sm.warp_tot, &total);
@@ -486,19 +601,41 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(
     const int64_t i = base + r * 32 + lane;
     if (i < n) {
       const uint32_t dg = digit_of(k[r], shift, flip);
-      const uint32_t p = sm.digit_start[dg] + sm.hist[warp][dg] + rank[r];
+      const uint32_t rk = (rank[r >> 1] >> ((r & 1) * 16)) & 0xFFFFu;
+      const uint32_t p = sm.digit_start[dg] + sm.hist[warp][dg] + rk;
       sm.keys[p] = k[r];
-      sm.vals[p] = __ldg(vals_in + i);
+      if constexpr (VALS) sm.vals[p] = __ldg(a.vals_in + i);
     }
   }
   __syncthreads();
   const int64_t tile_n = (n - tile_base) < kSortTile ? (n - tile_base) : kSortTile;
-  for (int i = threadIdx.x; i < tile_n; i += kSortThreads) {
-    const uint64_t key = sm.keys[i];
-    const uint32_t dg = digit_of(key, shift, flip);
-    const int64_t dst = (int64_t)sm.goff[dg] + (i - (int64_t)sm.digit_start[dg]);
-    keys_out[dst] = key;
-    vals_out[dst] = sm.vals[i];
+  if constexpr (OUT == kFinal) {
+    // all depth gathers of this thread in flight before the stores
+    uint32_t dep[kSortItems];
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const int i = threadIdx.x + r * kSortThreads;
+      dep[r] = i < tile_n ? __float_as_uint(__ldg(a.depths + (uint32_t)sm.keys[i])) : 0u;
+    }
+#pragma unroll
+    for (int r = 0; r < kSortItems; ++r) {
+      const int i = threadIdx.x + r * kSortThreads;
+      if (i < tile_n) {
+        const uint64_t key = sm.keys[i];
+        const uint32_t dg = digit_of(key, shift, flip);
+        const int64_t dst = (int64_t)sm.goff[dg] + (i - (int64_t)sm.digit_start[dg]);
+        a.keys_out[dst] = (key & 0xFFFFFFFF00000000ull) | (uint64_t)dep[r];
+        a.vals_out[dst] = (int32_t)(uint32_t)key;
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < tile_n; i += kSortThreads) {
+      const uint64_t key = sm.keys[i];
+      const uint32_t dg = digit_of(key, shift, flip);
+      const int64_t dst = (int64_t)sm.goff[dg] + (i - (int64_t)sm.digit_start[dg]);
+      a.keys_out[dst] = key;
+      if constexpr (OUT == kKV) a.vals_out[dst] = sm.vals[i];
+    }
   }
 }
 
@@ -526,10 +663,6 @@ SortLayout sort_layout(int64_t n) {
   return L;
 }
 
-// LSD passes over key bits [begin_bit, end_bit) with the scratch of
-// sort_layout(n) at `ws`; the last pass lands in (out_k, out_v) and the
-// input is only read.  With end_bit == 64 the sign bit is flipped so that
-// the unsigned digit order is the signed int64 order.
 // Clears the per-call region of sort_layout(n) at `ws` and returns its
 // digit histograms, for a producer that counts the digits itself.
 uint32_t* radix_reset(int64_t n, char* ws, cudaStream_t s) {
@@ -538,71 +671,97 @@ uint32_t* radix_reset(int64_t n, char* ws, cudaStream_t s) {
   return reinterpret_cast<uint32_t*>(ws + L.hist);
 }
 
-void radix_passes(int64_t n, int begin_bit, int end_bit, const uint64_t* in_k, const int32_t* in_v,
-                  uint64_t* out_k, int32_t* out_v, char* ws, cudaStream_t s,
-                  bool hist_ready = false) {
+template <int IN, int OUT>
+void launch_pass(int tiles, const PassArgs& a, cudaStream_t s) {
+  const int smem = (int)sizeof(PassSmem<IN == kKV>);
+  cudaFuncSetAttribute(radix_onesweep_kernel<IN, OUT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       smem);
+  radix_onesweep_kernel<IN, OUT><<<tiles, kSortThreads, smem, s>>>(a);
+}
+
+void launch_pass(int in, int out, int tiles, const PassArgs& a, cudaStream_t s) {
+  if (in == kKV) launch_pass<kKV, kKV>(tiles, a, s);
+  else if (out == kPacked) launch_pass<kPacked, kPacked>(tiles, a, s);
+  else launch_pass<kPacked, kFinal>(tiles, a, s);
+}
+
+// LSD passes over key bits [begin_bit, end_bit) with the scratch of
+// sort_layout(n) at `ws`; the last pass lands in (out_k, out_v) and the
+// input is only read.  `in` is the source form (kKV or kPacked), `out` the
+// sink form of the last pass (kKV, kPacked or kFinal); the passes between
+// move kKV (kKV sorts) or kPacked words through the scratch and out_k.  With end_bit == 64 and signed_keys the
+// sign bit is flipped so that the unsigned digit order is the signed int64
+// order.
+// The digit histograms come from radix_hist_kernel, or from the producer
+// of the keys after radix_reset (hist_ready).
+void sort_passes(int64_t n, int begin_bit, int end_bit, int in, int out, const uint64_t* in_k,
+                 const int32_t* in_v, uint64_t* out_k, int32_t* out_v, char* ws, cudaStream_t s,
+                 bool hist_ready = false, const int64_t* n_dev = nullptr,
+                 const float* depths = nullptr, bool signed_keys = true) {
   const SortLayout L = sort_layout(n);
   uint64_t* alt_k = reinterpret_cast<uint64_t*>(ws + L.keys_alt);
   int32_t* alt_v = reinterpret_cast<int32_t*>(ws + L.vals_alt);
   uint32_t* hist = reinterpret_cast<uint32_t*>(ws + L.hist);
-  uint32_t* ctrl = reinterpret_cast<uint32_t*>(ws + L.ctrl);  // tile counter per pass
-  uint32_t* err = reinterpret_cast<uint32_t*>(ws + L.err);
-  uint64_t* state = reinterpret_cast<uint64_t*>(ws + L.state);
   const int tiles = (int)ceil_div(n, kSortTile);
   const int passes = (end_bit - begin_bit + 7) / 8;
-  const uint64_t flip = end_bit == 64 ? (1ull << 63) : 0ull;
+  const uint64_t flip = signed_keys && end_bit == 64 ? (1ull << 63) : 0ull;
   if (!hist_ready) {  // else radix_reset ran and the producer counted the digits
     cudaMemsetAsync(ws + L.hist, 0, L.total - L.hist, s);
-    radix_hist_kernel<<<grid_for(ceil_div(n, 4), 256, 2), 256, 0, s>>>(n, in_k, begin_bit, passes,
-                                                                         flip, hist);
+    radix_hist_kernel<<<grid_for(ceil_div(n, 4), 256, 2), 256, 0, s>>>(
+        n, in_k, begin_bit, passes, flip, n_dev, hist);
   }
-  const int smem = (int)sizeof(PassSmem);
-  cudaFuncSetAttribute(radix_onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  const uint64_t* src_k = in_k;
-  const int32_t* src_v = in_v;
+  PassArgs a{};
+  a.n = n;
+  a.keys_in = in_k;
+  a.vals_in = in_v;
+  a.depths = depths;
+  a.flip = flip;
+  a.state = reinterpret_cast<uint64_t*>(ws + L.state);
+  a.error_word = reinterpret_cast<uint32_t*>(ws + L.err);
+  a.n_dev = n_dev;
+  int src = in;
   for (int pass = 0; pass < passes; ++pass) {
+    const bool last = pass == passes - 1;
     const bool to_out = ((passes - 1 - pass) % 2) == 0;
-    uint64_t* dst_k = to_out ? out_k : alt_k;
-    int32_t* dst_v = to_out ? out_v : alt_v;
-    radix_onesweep_kernel<<<tiles, kSortThreads, smem, s>>>(
-        n, src_k, src_v, dst_k, dst_v, begin_bit + pass * 8, flip, pass, hist + pass * kRadix,
-        ctrl + pass, state, err);
-    src_k = dst_k;
-    src_v = dst_v;
+    const int dst = last ? out : (in == kKV ? kKV : kPacked);
+    a.keys_out = to_out ? out_k : alt_k;
+    a.vals_out = to_out ? out_v : alt_v;
+    a.shift = begin_bit + pass * 8;
+    a.pass = pass;
+    a.pass_hist = hist + pass * kRadix;
+    a.tile_counter = reinterpret_cast<uint32_t*>(ws + L.ctrl) + pass;
+    launch_pass(src, dst, tiles, a, s);
+    a.keys_in = a.keys_out;
+    a.vals_in = a.vals_out;
+    src = dst;
   }
 }
 
-// keys[e] = bits of depths[e] (the low word of every intersection key of
-// element e), vals[e] = e.
-__global__ void __launch_bounds__(256) depth_keys_kernel(int64_t n, const float* __restrict__ depths,
-                                                         uint64_t* __restrict__ keys,
-                                                         int32_t* __restrict__ vals) {
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    keys[e] = (uint64_t)__float_as_uint(__ldg(depths + e));
-    vals[e] = (int32_t)e;
-  }
+void radix_passes(int64_t n, int begin_bit, int end_bit, const uint64_t* in_k, const int32_t* in_v,
+                  uint64_t* out_k, int32_t* out_v, char* ws, cudaStream_t s) {
+  sort_passes(n, begin_bit, end_bit, kKV, kKV, in_k, in_v, out_k, out_v, ws, s);
 }
 
 // Workspace of the depth-first sorted encode (n elements, m intersections).
 struct SortedEncodeLayout {
-  size_t sort, ek, ev, pk, pv, offs, scan, dk, dv, total;
+  size_t sort, nvis, ek, pk, offs, scan, dk, total;
 };
 
 SortedEncodeLayout sorted_encode_layout(int64_t n, int64_t m) {
+  // element arrays first (their places depend on n only, so that a later
+  // call with the same elements can reuse the depth order), then the sort
+  // scratch and the depth-ordered intersections (sized by m)
   SortedEncodeLayout L;
   const int64_t big = (n > m ? n : m) < 1 ? 1 : (n > m ? n : m);
   const int64_t n1 = n < 1 ? 1 : n, m1 = m < 1 ? 1 : m;
   size_t o = 0;
-  L.sort = o; o += sort_layout(big).total;
+  L.nvis = o; o += 256;
   L.ek = o; o += align256(8 * (size_t)n1);
-  L.ev = o; o += align256(4 * (size_t)n1);
   L.pk = o; o += align256(8 * (size_t)n1);
-  L.pv = o; o += align256(4 * (size_t)n1);
   L.offs = o; o += align256(4 * (size_t)n1);
   L.scan = o; o += scan_ws_bytes(n1);
+  L.sort = o; o += sort_layout(big).total;
   L.dk = o; o += align256(8 * (size_t)m1);
-  L.dv = o; o += align256(4 * (size_t)m1);
   L.total = o;
   return L;
 }
@@ -726,7 +885,7 @@ extern "C" int gs_isect_tile_encode(const gs_isect_params* p, const float* means
   tile_rows(p, ty0, ty1);
   encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, as_stream(stream)>>>(
       n, p->N, means2d, radii, depths, offsets, p->tile_size, p->tile_width,
-      p->tile_height, ty0, ty1, tile_bits, n_isects, isect_ids, flatten_ids, nullptr, 0);
+      p->tile_height, ty0, ty1, tile_bits, n_isects, isect_ids, flatten_ids, nullptr, nullptr, 0, 0u);
   return launch_status("intersect_tile_encode");
 }
 
@@ -735,8 +894,8 @@ extern "C" size_t gs_isect_tile_encode_sorted_workspace_size(int64_t n_elements,
   return sorted_encode_layout(n_elements, n_isects).total;
 }
 
-// Depth-first sorted encode: the elements (i, n) are first put in stable
-// order of their depth bits (4 radix passes over I*N elements), the
+// Depth-first sorted encode: the visible elements (i, n) are first put in
+// stable order of their depth bits (4 radix passes over them), the
 // intersections are then encoded in that order, and a stable sort over the
 // key bits above the depth word (tile and image: 2 passes at 1297x840)
 // finishes the job.  Within one (image, tile) the order is by depth bits,
@@ -774,11 +933,24 @@ extern "C" int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float
   cudaMemsetAsync(ws + L.sort + sort_layout(1).err, 0, sizeof(uint32_t), s);
   auto K = [&](size_t off) { return reinterpret_cast<uint64_t*>(ws + off); };
   auto V = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
-  depth_keys_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, depths, K(L.ek), V(L.ev));
-  radix_passes(n, 0, 32, K(L.ek), V(L.ev), K(L.pk), V(L.pv), ws + L.sort, s);
-  const int32_t* perm = V(L.pv);
+  int64_t* n_vis = reinterpret_cast<int64_t*>(ws + L.nvis);
+  if (!p->reuse_depth_order) {
+    // only the visible elements take part in the depth order; their count
+    // stays on the device and bounds the passes and the scan below
+    const int64_t nb = ceil_div(n, kScanChunk);
+    int64_t* sums = reinterpret_cast<int64_t*>(ws + L.scan);
+    visible_count_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, radii, sums);
+    scan_sums_kernel<<<1, 1024, 0, s>>>(nb, sums, n_vis);
+    visible_depth_keys_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n, radii, depths, sums,
+                                                                     K(L.ek));
+    // the depth bits are the low key word: unsigned order
+    sort_passes(n, 32, 64, kPacked, kPacked, K(L.ek), nullptr, K(L.pk), nullptr, ws + L.sort, s,
+                false, n_vis, nullptr, /*signed_keys=*/false);
+  }
+  // element of each depth-ordered place: the low words of the sorted words
+  const int32_t* perm = V(L.pk);
   if (int rc = scan_i32(n, tiles_per_gauss, V(L.offs), nullptr, ws + L.scan, scan_ws_bytes(n), s,
-                        perm))
+                        perm, 2, n_vis))
     return rc;
   // V(L.offs)[e] is now element e's offset in depth order; encoding in
   // element order keeps the warps' work as balanced as the plain encode
@@ -790,10 +962,13 @@ extern "C" int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float
   tile_rows(p, ty0, ty1);
   encode_kernel<<<grid_for((n + 31) / 32, kEncodeWarps), kEncodeThreads, 0, s>>>(
       n, p->N, means2d, radii, depths, V(L.offs), p->tile_size, p->tile_width,
-      p->tile_height, ty0, ty1, tile_bits, n_isects, reinterpret_cast<int64_t*>(K(L.dk)), V(L.dv),
-      hist, (hb + 7) / 8);
-  radix_passes(n_isects, 32, 32 + hb, K(L.dk), V(L.dv), reinterpret_cast<uint64_t*>(isect_ids),
-               flatten_ids, ws + L.sort, s, /*hist_ready=*/true);
+      p->tile_height, ty0, ty1, tile_bits, n_isects, nullptr, nullptr, K(L.dk), hist, (hb + 7) / 8,
+      hb == 32 ? 0x80000000u : 0u);  // keys with the sign bit set sort first
+  // the passes move (high word << 32 | element) words; the last one writes
+  // the full keys (depth bits gathered) and the element ids
+  sort_passes(n_isects, 32, 32 + hb, kPacked, kFinal, K(L.dk), nullptr,
+              reinterpret_cast<uint64_t*>(isect_ids), flatten_ids, ws + L.sort, s,
+              /*hist_ready=*/true, nullptr, depths);
   return launch_status("intersect_tile_encode_sorted");
 }
 

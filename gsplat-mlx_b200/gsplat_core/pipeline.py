@@ -126,8 +126,9 @@ class TrainingStep:
         self.events = None
 
     def _ensure_capacity(self, m):
+        """Grows the intersection buffers; True when they were reallocated."""
         if m <= self.capacity:
-            return
+            return False
         cap = max(int(m * 1.25) + 1024, 1 << 16)
         e = lambda shape, dt: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
         self.sorted_ids = e((cap,), torch.int64)
@@ -135,6 +136,7 @@ class TrainingStep:
         self.sort_ws = e((self.lib.gs_isect_tile_encode_sorted_workspace_size(self.C * self.N, cap),),
                          torch.uint8)
         self.capacity = cap
+        return True
 
     def _mark(self, name):
         if self.events is not None:
@@ -213,7 +215,9 @@ class TrainingStep:
             if m >= 2 ** 31:
                 raise RuntimeError(f"{m} intersections exceed the int32 index range"
                                    + (f" in tile rows {y0}..{y1}" if y1 else ""))
-            self._ensure_capacity(m)
+            # bands after the first reuse the depth order of the elements left
+            # in the workspace (unless the workspace was just reallocated)
+            ip.reuse_depth_order = int(not self._ensure_capacity(m) and b > 0 and y1 > 0)
             self.m = m
             m_total += m
             check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d), _p(self.radii),
@@ -251,10 +255,10 @@ class TrainingStep:
                                      _p(v_render_colors), _p(v_render_alphas), None,
                                      _p(self.v_means2d), _p(self.v_conics), _p(self.v_colors),
                                      _p(v_opac), _p(self.v_backgrounds), s), "rasterize_bwd")
+            self._mark("rasterize_bwd")
             b += 1
         m = m_total
         self.bands = len(bands)
-        self._mark("rasterize_bwd")
         if C > 1:
             torch.sum(self.v_opac_cn, dim=0, out=self.v_opacities)
         check(L.gs_projection_bwd(ct.byref(pp), _p(means), None, _p(quats), _p(scales),

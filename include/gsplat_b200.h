@@ -170,6 +170,11 @@ typedef struct {
                                [tile_y0, tile_y1) are intersected (a band of
                                the image; keys keep absolute tile ids); else
                                all rows, as the reference */
+  int32_t reuse_depth_order; /* gs_isect_tile_encode_sorted: 1 = the
+                                workspace holds the depth order of an earlier
+                                call with the same I, N, radii and depths (the
+                                other bands of a step); its element sort is
+                                skipped */
 } gs_isect_params;
 
 /* tiles_per_gauss [I,N] int32 */
