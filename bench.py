@@ -169,10 +169,10 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ helpers
 
-def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
-    """Bytes each stage must move at minimum (the roofline convention).
-    ``sort_passes``: radix passes over the tile and image bits of the keys
-    (the depth word is ordered per element, 4 passes over the N elements)."""
+def algorithmic_bytes(stage, n, visible, m, pixels, K, slots):
+    """Bytes each stage must move at minimum (the roofline convention):
+    what it reads once and writes once, not what an implementation's
+    intermediate passes move.  ``slots``: tile offsets written."""
     return {
         # means/quats/scales in (40 B), 2D outputs out (36 B) per Gaussian
         "projection_fwd": n * (40 + 36),
@@ -180,10 +180,9 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
         "sh_fwd": n * (12 + 8 + 12) + visible * K * 12,
         # rects from means2d/radii, counts out, their total
         "isect_count": n * (16 + 4),
-        # depth keys (4 B in, 12 out), 4 element passes at 24 B, permuted scan
-        # (12 B), encode (24 B per element, 12 B per intersection out), then
-        # 24 B per intersection per tile/image pass
-        "isect_encode_sort": n * (16 + 4 * 24 + 12 + 24) + m * 12 + m * 24 * sort_passes,
+        # means2d, radii, depths in; sorted keys + flatten ids and the tile
+        # offsets out (the binned encode writes the offsets itself)
+        "isect_encode_sort": n * (8 + 8 + 4) + m * 12 + slots * 4,
         "isect_offset": m * 8,
         # per intersection: flatten id + Gaussian record; per pixel: outputs
         "rasterize_fwd": m * 40 + pixels * 20,
@@ -193,13 +192,27 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, sort_passes):
     }[stage]
 
 
-def our_kernel_launches(sort_passes):
-    # projection fwd 1, glue fwd 1, count (+ total) 1, visible compaction 3
-    # (block counts, their scan, packed depth words), element sort: digit
-    # histogram 1 + 4 onesweep passes, permuted scan 3, encode (+ tile/image
-    # digit histogram) 1, tile/image onesweep passes, offset 1, rasterize
-    # fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
-    return 1 + 1 + 1 + 3 + (1 + 4) + 3 + 1 + sort_passes + 1 + 1 + 1 + 1 + 1
+def bin_count(cameras, tw, th):
+    """4x4-tile bins of the binned encode."""
+    return cameras * -(-tw // 4) * -(-th // 4)
+
+
+def bin_sort_passes(cameras, tw, th):
+    """Radix passes of the binned encode's entry sort: 32 depth bits plus
+    the bits of the bin ids."""
+    return (32 + (bin_count(cameras, tw, th) - 1).bit_length() + 7) // 8
+
+
+def our_kernel_launches(entry_passes, bins, slots):
+    # projection fwd 1, glue fwd 1, count (+ totals) 1; binned encode: bin
+    # counts 1, their scan 1, entry emit 1, digit histogram 1, entry passes,
+    # bin starts + rects 1, item counts per bin 1 and their scan, item count
+    # phase 1, slot counts 1 and their scan, item write phase 1 (a scan is
+    # one launch up to 16384 values, else 3); rasterize fwd 1, rasterize
+    # bwd 1, projection bwd 1, glue bwd 1
+    scan = lambda n: 1 if n <= 16384 else 3  # noqa: E731
+    binned = 3 + 1 + entry_passes + 1 + 1 + scan(bins) + 1 + 1 + scan(slots) + 1
+    return 1 + 1 + 1 + binned + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -523,13 +536,14 @@ def run_ours(args):
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
         visible = int(((step.radii[..., 0] > 0) & (step.radii[..., 1] > 0)).sum().item())
         K = sc.coeffs.shape[1]
-        passes = (step.key_bits - 32 + 7) // 8
+        passes = bin_sort_passes(sharded.C, sc.tile_width, sc.tile_height)
+        slots = sharded.C * sc.tile_width * sc.tile_height
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
         top = max((k for k in avg if k != "exchange"), key=avg.get)
         # this rank's units: (camera, Gaussian) elements and pixels
         n_el, pix_local = sc.n * sharded.C, sc.width * sc.height * sharded.C
         vis_b = visible
-        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, passes)
+        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, slots)
         achieved = bytes_top / (avg[top] / 1e3) / 1e9
         stages = {}
         for k, v in avg.items():
@@ -541,7 +555,7 @@ def run_ours(args):
                              "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
                              "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
                 continue
-            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, passes)
+            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, slots)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
         cpu = None
@@ -582,7 +596,8 @@ def run_ours(args):
                     "how": "all inputs uploaded and the flat gradient downloaded every step "
                            "from pinned host memory; copies double-buffered on their own "
                            "streams, overlapping the neighbouring steps' kernels"},
-            "gpu_launches": our_kernel_launches(passes) * args.steps,
+            "gpu_launches": our_kernel_launches(
+                passes, bin_count(sharded.C, sc.tile_width, sc.tile_height), slots) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(out), flush=True)

@@ -10,6 +10,8 @@
 //
 // All integer work; this file is compiled without FMA contraction so that
 // the float tile-rect arithmetic (divide, floor, ceil) rounds like the CPU.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace gsb {
@@ -47,12 +49,28 @@ __device__ __forceinline__ Rect band_rect(float mx, float my, int rx, int ry, in
   return r;
 }
 
+// Bins of the binned encode: blocks of kBinTiles x kBinTiles tiles.
+constexpr int kBinTiles = 4;
+
+// Number of bins along one axis that the tile range [a0, a1) touches.
+__device__ __forceinline__ int bin_span(int a0, int a1) {
+  return a1 > a0 ? (a1 - 1) / kBinTiles - a0 / kBinTiles + 1 : 0;
+}
+
+// Bins a rect touches (0 for an empty rect).
+__device__ __forceinline__ int rect_bins(const Rect& r) {
+  return (r.x1 > r.x0 && r.y1 > r.y0) ? bin_span(r.x0, r.x1) * bin_span(r.y0, r.y1) : 0;
+}
+
+// With `totals`, the tile counts are summed into totals[0] and, with
+// `bins`, the bin counts into totals[1] (zeroed by the caller).
 __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __restrict__ means2d,
                                                     const int32_t* __restrict__ radii, int ts,
                                                     int tw, int th, int ty0, int ty1,
                                                     int32_t* __restrict__ tiles_per_gauss,
-                                                    unsigned long long* __restrict__ total) {
-  unsigned long long sum = 0;
+                                                    unsigned long long* __restrict__ totals,
+                                                    int bins) {
+  unsigned long long sum = 0, sum_b = 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
@@ -61,17 +79,24 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
     const int c = (r.y1 - r.y0) * (r.x1 - r.x0);
     tiles_per_gauss[i] = c;
     sum += (unsigned long long)c;
+    if (bins) sum_b += (unsigned long long)rect_bins(r);
   }
-  if (total) {  // one atomic per CTA
-    __shared__ unsigned long long s_sum[8];
+  if (totals) {  // one atomic per CTA and total
+    __shared__ unsigned long long s_sum[2][8];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sum;
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sum_b += __shfl_xor_sync(0xffffffffu, sum_b, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      s_sum[0][threadIdx.x >> 5] = sum;
+      s_sum[1][threadIdx.x >> 5] = sum_b;
+    }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 2 && (threadIdx.x == 0 || bins)) {
       unsigned long long t = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_sum[w];
-      if (t) atomicAdd(total, t);
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += s_sum[threadIdx.x][w];
+      if (t) atomicAdd(totals + threadIdx.x, t);
     }
   }
 }
@@ -305,6 +330,39 @@ __global__ void __launch_bounds__(kScanThreads) scan_down_kernel(int64_t n, cons
   }
 }
 
+// The whole scan in one CTA of kScanThreads threads, chunk by chunk with a
+// running carry (no perm, no device length): for short sequences, where
+// the three-launch scan is all latency.
+constexpr int64_t kSmallScan = 4 * kScanChunk;
+
+__global__ void __launch_bounds__(kScanThreads) scan_small_kernel(int64_t n,
+                                                                   const int32_t* __restrict__ in,
+                                                                   int32_t* __restrict__ out,
+                                                                   int64_t* __restrict__ total_out) {
+  __shared__ int64_t s_warp[32];
+  int64_t carry = 0;
+  for (int64_t base = 0; base < n; base += kScanChunk) {
+    int32_t v[kScanItems];
+    int64_t acc = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+      const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+      v[k] = i < n ? __ldg(in + i) : 0;
+      acc += v[k];
+    }
+    int64_t total;
+    int64_t run = block_exclusive_scan<kScanThreads>(acc, s_warp, &total) + carry;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k) {
+      const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+      if (i < n) out[i] = (int32_t)run;
+      run += v[k];
+    }
+    carry += total;
+  }
+  if (threadIdx.x == 0 && total_out) *total_out = carry;
+}
+
 size_t scan_ws_bytes(int64_t n) {
   const int64_t nb = ceil_div(n < 1 ? 1 : n, kScanChunk);
   return (size_t)((nb * 8 + 255) / 256 * 256);
@@ -320,6 +378,10 @@ int scan_i32(int64_t n, const int32_t* in, int32_t* out, int64_t* total, void* w
   if (!ws || ws_bytes < scan_ws_bytes(n)) {
     set_error("scan: workspace of %zu bytes needed", scan_ws_bytes(n));
     return GS_ERR_WORKSPACE;
+  }
+  if (n <= kSmallScan && !perm && !n_dev && in != out) {
+    scan_small_kernel<<<1, kScanThreads, 0, s>>>(n, in, out, total);
+    return launch_status("scan");
   }
   const int64_t nb = ceil_div(n, kScanChunk);
   int64_t* sums = static_cast<int64_t*>(ws);
@@ -489,6 +551,7 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(const P
   PassSmem<VALS>& sm = *reinterpret_cast<PassSmem<VALS>*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) sm.tile = (int)atomicAdd(a.tile_counter, 1u);
+  const uint32_t hist_d = __ldg(a.pass_hist + threadIdx.x);  // this pass's total of digit tid
   for (int i = threadIdx.x; i < kSortWarps * kRadix; i += kSortThreads) (&sm.hist[0][0])[i] = 0;
   __syncthreads();
   const int tile = sm.tile;
@@ -547,19 +610,36 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(const P
     sm.hist[w][d] = cta_count;
     cta_count += c;
   }
-  // Publish, then look back for the exclusive prefix over earlier tiles.
+  // Publish this tile's counts before anything else, so that later tiles
+  // can sum them while this one stages its keys.
   const uint64_t tag_agg = (uint64_t)(2 * a.pass + 1) << 32;
   const uint64_t tag_inc = (uint64_t)(2 * a.pass + 2) << 32;
   uint64_t* my = a.state + (int64_t)tile * kRadix + d;
+  store_state(my, (tile == 0 ? tag_inc : tag_agg) | cta_count);
+  int64_t total;
+  const int64_t start = block_exclusive_scan<kSortThreads>(cta_count, sm.warp_tot, &total);
+  sm.digit_start[d] = (uint32_t)start;
+  __syncthreads();
+  // Stage the keys at their places in this tile's digit order; the
+  // registers that held them serve the look-back below.
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const int64_t i = base + r * 32 + lane;
+    if (i < n) {
+      const uint32_t dg = digit_of(k[r], shift, flip);
+      const uint32_t rk = (rank[r >> 1] >> ((r & 1) * 16)) & 0xFFFFu;
+      const uint32_t p = sm.digit_start[dg] + sm.hist[warp][dg] + rk;
+      sm.keys[p] = k[r];
+      if constexpr (VALS) sm.vals[p] = __ldg(a.vals_in + i);
+    }
+  }
+  // Look back for the exclusive prefix over earlier tiles, kLookback tile
+  // states per round with all their loads in flight: when every tile of a
+  // small sort runs at once, the inclusive prefixes advance kLookback tiles
+  // per memory round trip.
   uint64_t excl = 0;
-  if (tile == 0) {
-    store_state(my, tag_inc | cta_count);
-  } else {
-    store_state(my, tag_agg | cta_count);
-    // Walk back kLookback tiles per round with all their states loaded at
-    // once, so that a long run of not-yet-inclusive predecessors costs one
-    // memory round trip per kLookback tiles instead of one per tile.
-    constexpr int kLookback = 8;
+  if (tile > 0) {
+    constexpr int kLookback = 32;
     bool found = false;
     for (int t0 = tile - 1; t0 >= 0 && !found; t0 -= kLookback) {
       uint64_t w[kLookback];
@@ -589,24 +669,8 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(const P
   }
   // Global digit bases: exclusive scan of this pass's digit totals.
   int64_t unused;
-  const int64_t dbase =
-      block_exclusive_scan<kSortThreads>(__ldg(a.pass_hist + d), sm.warp_tot, &unused);
+  const int64_t dbase = block_exclusive_scan<kSortThreads>(hist_d, sm.warp_tot, &unused);
   sm.goff[d] = (uint64_t)dbase + excl;
-  int64_t total;
-  const int64_t start = block_exclusive_scan<kSortThreads>(cta_count, sm.warp_tot, &total);
-  sm.digit_start[d] = (uint32_t)start;
-  __syncthreads();
-#pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const int64_t i = base + r * 32 + lane;
-    if (i < n) {
-      const uint32_t dg = digit_of(k[r], shift, flip);
-      const uint32_t rk = (rank[r >> 1] >> ((r & 1) * 16)) & 0xFFFFu;
-      const uint32_t p = sm.digit_start[dg] + sm.hist[warp][dg] + rk;
-      sm.keys[p] = k[r];
-      if constexpr (VALS) sm.vals[p] = __ldg(a.vals_in + i);
-    }
-  }
   __syncthreads();
   const int64_t tile_n = (n - tile_base) < kSortTile ? (n - tile_base) : kSortTile;
   if constexpr (OUT == kFinal) {
@@ -766,6 +830,373 @@ SortedEncodeLayout sorted_encode_layout(int64_t n, int64_t m) {
   return L;
 }
 
+// ------------------------------------------------------------ binned encode
+// The tile grid is cut into bins of kBinTiles x kBinTiles tiles.  Every
+// element lists itself once per bin its tile rect touches, as the entry
+// (bin << 32 | depth bits, element); a stable sort of those entries groups
+// them by bin, in depth-bit order and, for equal depth bits, in element
+// order.  One CTA per tile then walks its bin's list and keeps the elements
+// whose rect covers the tile: its intersections, already in the order of
+// the full 64-bit key sort, written at the tile's offset.  The walk runs
+// over work items of at most kItemEntries entries of one bin (so that the
+// dense bins do not set the kernel's length), each for all 16 tiles of its
+// bin: a count phase, a scan of the tiles' counts into their offsets, and a
+// write phase.
+
+// Element rect in 16-bit tile units: x = x0 | x1 << 16, y = y0 | y1 << 16.
+__device__ __forceinline__ uint2 pack_rect(const Rect& r) {
+  return make_uint2((uint32_t)r.x0 | ((uint32_t)r.x1 << 16), (uint32_t)r.y0 | ((uint32_t)r.y1 << 16));
+}
+
+struct BinArgs {
+  int64_t n;  // elements I*N
+  int n_per_image, ts, tw, th, ty0, ty1;
+  int sw, n_bins_per_image;  // bins per row, bins per image
+  const float* means2d;
+  const int32_t* radii;
+  const float* depths;
+};
+
+__device__ __forceinline__ Rect element_rect(const BinArgs& a, int64_t i) {
+  const int2 rad = __ldg(reinterpret_cast<const int2*>(a.radii) + i);
+  const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + i);
+  return band_rect(m.x, m.y, rad.x, rad.y, a.ts, a.tw, a.th, a.ty0, a.ty1);
+}
+
+// Block sums of the per-element bin counts (the scan's first half).
+__global__ void __launch_bounds__(kScanThreads) bin_count_kernel(const BinArgs a,
+                                                                 int64_t* __restrict__ sums) {
+  __shared__ int64_t s_warp[32];
+  const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int64_t acc = 0;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    if (i < a.n) acc += rect_bins(element_rect(a, i));
+  }
+  int64_t total;
+  block_exclusive_scan<kScanThreads>(acc, s_warp, &total);
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+// With the scanned block sums: each element's entries at its place in
+// element order and its packed rect.  A block takes its kScanChunk elements
+// in kScanItems rounds of one element per thread; each warp then writes the
+// entries of its 32 elements together (entry j of the warp's run: owner
+// from a bit mask of run starts, as in the encode), so that the stores are
+// coalesced.  Entries past n_entries are dropped.
+constexpr int kScanWarps = kScanThreads / 32;
+
+__global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
+    const BinArgs a, const int64_t* __restrict__ sums, int64_t n_entries,
+    uint64_t* __restrict__ keys, int32_t* __restrict__ vals, uint2* __restrict__ rects) {
+  __shared__ int64_t s_warp[32];
+  __shared__ int s_pref[kScanWarps][32], s_start[kScanWarps][32], s_bw[kScanWarps][32];
+  __shared__ int64_t s_bin0[kScanWarps][32];
+  __shared__ uint32_t s_low[kScanWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int64_t block_run = sums[blockIdx.x];
+  for (int round = 0; round < kScanItems; ++round) {
+    const int64_t i = base + (int64_t)round * kScanThreads + threadIdx.x;
+    int c = 0;
+    if (i < a.n) {
+      const Rect q = element_rect(a, i);
+      c = rect_bins(q);
+      if (c > 0) {
+        const int64_t image = i / a.n_per_image;
+        rects[i] = pack_rect(q);
+        const int bx0 = q.x0 / kBinTiles, by0 = q.y0 / kBinTiles;
+        s_bw[warp][lane] = (q.x1 - 1) / kBinTiles - bx0 + 1;
+        s_bin0[warp][lane] = image * a.n_bins_per_image + (int64_t)by0 * a.sw + bx0;
+        s_low[warp][lane] = __float_as_uint(__ldg(a.depths + i));
+      }
+    }
+    int64_t tot;
+    const int64_t excl = block_exclusive_scan<kScanThreads>(c, s_warp, &tot);
+    const int64_t excl0 = __shfl_sync(0xffffffffu, excl, 0);
+    const int wexcl = (int)(excl - excl0);  // within the warp
+    const int wtot = __shfl_sync(0xffffffffu, wexcl + c, 31);
+    const int64_t wpos = block_run + excl0;
+    s_pref[warp][lane] = wexcl;
+    __syncwarp();
+    int carry = 0;  // owner of the last entry of the previous window
+    for (int j0 = 0; j0 < wtot; j0 += 32) {
+      const bool st = c > 0 && wexcl >= j0 && wexcl < j0 + 32;
+      if (st) s_start[warp][wexcl - j0] = lane;
+      const uint32_t starts = __reduce_or_sync(0xffffffffu, st ? 1u << (wexcl - j0) : 0u);
+      __syncwarp();
+      const uint32_t upto = starts & (0xFFFFFFFFu >> (31 - lane));
+      const int o = upto ? s_start[warp][31 - __clz(upto)] : carry;
+      carry = __shfl_sync(0xffffffffu, o, 31);
+      const int j = j0 + lane;
+      if (j < wtot) {
+        const int k = j - s_pref[warp][o];
+        const int bw = s_bw[warp][o];
+        const int dy = k / bw;
+        const int64_t bin = s_bin0[warp][o] + (int64_t)dy * a.sw + (k - dy * bw);
+        const int64_t pos = wpos + j;
+        if (pos >= 0 && pos < n_entries) {
+          keys[pos] = ((uint64_t)bin << 32) | s_low[warp][o];
+          vals[pos] = (int32_t)(base + (int64_t)round * kScanThreads + warp * 32 + o);
+        }
+      }
+      __syncwarp();
+    }
+    block_run += tot;
+  }
+}
+
+// One pass over the sorted entries: bin_start[b] = first entry of bin b
+// (bins without entries point at the next one; bin_start[n_bins] =
+// n_entries), and the rect of every entry next to it (an empty rect for an
+// element id outside [0, n), which only a wrong entry total can leave).
+__global__ void __launch_bounds__(256) bin_finish_kernel(int64_t n_entries, int64_t n,
+                                                         const uint64_t* __restrict__ keys,
+                                                         const int32_t* __restrict__ vals,
+                                                         const uint2* __restrict__ rects,
+                                                         int64_t n_bins,
+                                                         int32_t* __restrict__ bin_start,
+                                                         uint2* __restrict__ sorted_rects) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n_entries;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = (int64_t)(__ldg(keys + p) >> 32);
+    const int64_t bp = p > 0 ? (int64_t)(__ldg(keys + p - 1) >> 32) : -1;
+    for (int64_t q = bp + 1; q <= b && q <= n_bins; ++q) bin_start[q] = (int32_t)p;
+    if (p == n_entries - 1)
+      for (int64_t q = b + 1; q <= n_bins; ++q) bin_start[q] = (int32_t)n_entries;
+    const int32_t e = __ldg(vals + p);
+    sorted_rects[p] = (e >= 0 && e < n) ? __ldg(rects + e) : make_uint2(0u, 0u);
+  }
+}
+
+// Work items of the tile pass: a bin's sorted entries cut into chunks of
+// kItemEntries.  Every item handles its bin's 16 tiles at once: per entry a
+// 16-bit mask of the covered tiles, per tile counts packed four to a 64-bit
+// word (16-bit fields: a CTA holds at most kItemEntries entries).
+constexpr int kItemThreads = 256;
+constexpr int kItemPer = 8;  // consecutive entries per thread
+constexpr int kItemEntries = kItemThreads * kItemPer;
+
+// chunks[b] = items of bin b.
+__global__ void __launch_bounds__(256) bin_chunks_kernel(int64_t n_bins,
+                                                         const int32_t* __restrict__ bin_start,
+                                                         int32_t* __restrict__ chunks) {
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < n_bins;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    const int len = __ldg(bin_start + b + 1) - __ldg(bin_start + b);
+    chunks[b] = (len + kItemEntries - 1) / kItemEntries;
+  }
+}
+
+// Tiles of a bin an entry's rect covers: bit 4j+i for tile (bx*4+i, by*4+j).
+__device__ __forceinline__ uint32_t cover_mask(uint2 r, int tx0, int ty0_) {
+  const int x0 = (int)(r.x & 0xFFFFu) - tx0, x1 = (int)(r.x >> 16) - tx0;
+  const int y0 = (int)(r.y & 0xFFFFu) - ty0_, y1 = (int)(r.y >> 16) - ty0_;
+  auto span = [](int a0, int a1) -> uint32_t {  // bits [max(a0,0), min(a1,4))
+    const int lo = a0 < 0 ? 0 : (a0 > 4 ? 4 : a0), hi = a1 < 0 ? 0 : (a1 > 4 ? 4 : a1);
+    return hi > lo ? ((1u << hi) - 1u) & ~((1u << lo) - 1u) : 0u;
+  };
+  const uint32_t xm = span(x0, x1), ym = span(y0, y1);
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((ym >> j) & 1u) m |= xm << (4 * j);
+  return m;
+}
+
+// Bit t of a 16-bit mask to 16-bit field t of four words (tiles 4w..4w+3
+// in word w).
+__device__ __forceinline__ void spread16(uint32_t m, uint64_t f[4]) {
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint64_t x = (m >> (4 * w)) & 0xFu;
+    x = (x | (x << 30)) & 0x0000000300000003ull;  // bits 2,3 -> bits 32,33
+    x = (x | (x << 15)) & 0x0001000100010001ull;  // bits 1,33 -> bits 16,48
+    f[w] = x;
+  }
+}
+
+struct ItemArgs {
+  int64_t n_bins, per_image;
+  int sw, tw, ty0, rows;
+  const int32_t* bin_start;
+  const int32_t* chunk_prefix;  // exclusive prefix of the bins' item counts
+  const int64_t* n_items;       // device total of items
+  const uint2* sorted_rects;
+};
+
+// The item of this CTA: its bin and its entries [lo, hi).  False past the
+// device's item total.
+__device__ __forceinline__ bool item_of(const ItemArgs& a, int64_t item, int64_t& bin, int& lo,
+                                        int& hi) {
+  if (item >= *a.n_items) return false;
+  int64_t l = 0, h = a.n_bins;  // last bin whose prefix is <= item
+  while (l < h) {
+    const int64_t mid = l + (h - l) / 2;
+    if (__ldg(a.chunk_prefix + mid) <= item) l = mid + 1;
+    else h = mid;
+  }
+  bin = l - 1;
+  const int chunk = (int)(item - __ldg(a.chunk_prefix + bin));
+  const int b0 = __ldg(a.bin_start + bin), b1 = __ldg(a.bin_start + bin + 1);
+  lo = b0 + chunk * kItemEntries;
+  hi = lo + kItemEntries < b1 ? lo + kItemEntries : b1;
+  return true;
+}
+
+__device__ __forceinline__ void bin_origin(const ItemArgs& a, int64_t bin, int64_t& image, int& tx0,
+                                           int& ty0_) {
+  image = bin / a.per_image;
+  const int rem = (int)(bin - image * a.per_image);
+  tx0 = (rem % a.sw) * kBinTiles;
+  ty0_ = (rem / a.sw) * kBinTiles;
+}
+
+// Sums four packed words over the CTA: returns this thread's exclusive
+// prefix; the CTA totals land in s_tot.
+__device__ __forceinline__ void block_scan_packed(uint64_t v[4], uint64_t pre[4],
+                                                  uint64_t (*s_w)[4], uint64_t* s_tot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t inc[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    inc[w] = v[w];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t t = __shfl_up_sync(0xffffffffu, inc[w], o);
+      if (lane >= o) inc[w] += t;
+    }
+    if (lane == 31) s_w[warp][w] = inc[w];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint64_t before = 0, tot = 0;
+#pragma unroll
+    for (int k = 0; k < kItemThreads / 32; ++k) {
+      const uint64_t x = s_w[k][w];
+      before += k < warp ? x : 0;
+      tot += x;
+    }
+    pre[w] = before + inc[w] - v[w];
+    if (threadIdx.x == 0) s_tot[w] = tot;
+  }
+  __syncthreads();
+}
+
+// Count phase: item_counts[item][16] = entries of the item covering each
+// of its bin's tiles.
+__global__ void __launch_bounds__(kItemThreads) item_count_kernel(const ItemArgs a,
+                                                                  int32_t* __restrict__ item_counts) {
+  __shared__ uint64_t s_w[kItemThreads / 32][4];
+  __shared__ uint64_t s_tot[4];
+  int64_t bin;
+  int lo, hi;
+  if (!item_of(a, blockIdx.x, bin, lo, hi)) return;
+  int64_t image;
+  int tx0, ty0_;
+  bin_origin(a, bin, image, tx0, ty0_);
+  const int p0 = lo + threadIdx.x * kItemPer;
+  uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < kItemPer; ++k) {
+    const int p = p0 + k;
+    if (p < hi) {
+      uint64_t f[4];
+      spread16(cover_mask(__ldg(a.sorted_rects + p), tx0, ty0_), f);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) acc[w] += f[w];
+    }
+  }
+  uint64_t pre[4];
+  block_scan_packed(acc, pre, s_w, s_tot);
+  if (threadIdx.x < 16)
+    item_counts[(int64_t)blockIdx.x * 16 + threadIdx.x] =
+        (int32_t)((s_tot[threadIdx.x >> 2] >> (16 * (threadIdx.x & 3))) & 0xFFFFu);
+}
+
+// Per tile slot: its intersection count, summed over its bin's items.
+__global__ void __launch_bounds__(256) slot_count_kernel(const ItemArgs a, int64_t n_slots,
+                                                         const int32_t* __restrict__ item_counts,
+                                                         int32_t* __restrict__ counts) {
+  const int64_t per_image_slots = (int64_t)a.rows * a.tw;
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n_slots;
+       s += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t image = s / per_image_slots;
+    const int rem = (int)(s - image * per_image_slots);
+    const int y = a.ty0 + rem / a.tw, x = rem % a.tw;
+    const int64_t bin = image * a.per_image + (int64_t)(y / kBinTiles) * a.sw + x / kBinTiles;
+    const int t = (y % kBinTiles) * kBinTiles + x % kBinTiles;
+    const int i0 = __ldg(a.chunk_prefix + bin);
+    const int i1 = bin + 1 < a.n_bins ? __ldg(a.chunk_prefix + bin + 1) : (int)*a.n_items;
+    int32_t c = 0;
+    for (int i = i0; i < i1; ++i) c += __ldg(item_counts + (int64_t)i * 16 + t);
+    counts[s] = c;
+  }
+}
+
+// Write phase: every entry of the item at its place in each tile it covers
+// -- the tile's offset, the counts of the bin's earlier items, the covering
+// entries before it in this item -- as the full key and the element id.
+// Rounds of one entry per thread (consecutive entries on consecutive
+// threads) and, within a round, tile by tile: the lanes that cover a tile
+// store to consecutive places.
+__global__ void __launch_bounds__(kItemThreads) item_write_kernel(
+    const ItemArgs a, int tile_bits, const int32_t* __restrict__ item_counts,
+    const int32_t* __restrict__ offsets, const uint64_t* __restrict__ keys,
+    const int32_t* __restrict__ vals, int64_t n_isects, int64_t* __restrict__ isect_ids,
+    int32_t* __restrict__ flatten_ids) {
+  __shared__ uint64_t s_w[kItemThreads / 32][4];
+  __shared__ uint64_t s_tot[4];
+  __shared__ int64_t s_base[16];
+  __shared__ uint32_t s_tile[16];  // image << tile_bits | tile id
+  int64_t bin;
+  int lo, hi;
+  if (!item_of(a, blockIdx.x, bin, lo, hi)) return;
+  int64_t image;
+  int tx0, ty0_;
+  bin_origin(a, bin, image, tx0, ty0_);
+  if (threadIdx.x < 16) {
+    const int t = threadIdx.x;
+    const int x = tx0 + (t & 3), y = ty0_ + (t >> 2);
+    int64_t base = 0;
+    if (x < a.tw && y >= a.ty0 && y < a.ty0 + a.rows) {
+      base = __ldg(offsets + image * a.rows * a.tw + (int64_t)(y - a.ty0) * a.tw + x);
+      for (int i = __ldg(a.chunk_prefix + bin); i < (int)blockIdx.x; ++i)
+        base += __ldg(item_counts + (int64_t)i * 16 + t);
+    }
+    s_base[t] = base;
+    s_tile[t] = (uint32_t)((image << tile_bits) | ((int64_t)y * a.tw + x));
+  }
+  uint64_t run[4] = {0, 0, 0, 0};  // covering entries of earlier rounds, per tile
+  for (int r = 0; r < kItemPer; ++r) {
+    const int p = lo + r * kItemThreads + threadIdx.x;
+    const uint32_t m = p < hi ? cover_mask(__ldg(a.sorted_rects + p), tx0, ty0_) : 0u;
+    uint64_t f[4], pre[4];
+    spread16(m, f);
+    block_scan_packed(f, pre, s_w, s_tot);  // the first also orders s_base / s_tile
+    if (m) {
+      const uint64_t low = __ldg(keys + p) & 0xFFFFFFFFull;
+      const int32_t e = __ldg(vals + p);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        if ((m >> t) & 1u) {
+          const int w = t >> 2, sh = 16 * (t & 3);
+          const int64_t pos = s_base[t] + (int64_t)(((run[w] + pre[w]) >> sh) & 0xFFFFu);
+          if (pos >= 0 && pos < n_isects) {
+            isect_ids[pos] = (int64_t)(((uint64_t)s_tile[t] << 32) | low);
+            flatten_ids[pos] = e;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int w = 0; w < 4; ++w) run[w] += s_tot[w];
+    if (lo + (r + 1) * kItemThreads >= hi) break;  // uniform: the item's entries are done
+  }
+}
+
 // ------------------------------------------------------------ offsets
 
 // tile_offsets[o] = lower bound of key(o) = (image << tb) | tile in
@@ -828,7 +1259,7 @@ extern "C" int gs_isect_tile_count(const gs_isect_params* p, const float* means2
   tile_rows(p, ty0, ty1);
   count_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
       n, means2d, radii, p->tile_size, p->tile_width, p->tile_height, ty0, ty1, tiles_per_gauss,
-      nullptr);
+      nullptr, 0);
   return launch_status("intersect_tile_count");
 }
 
@@ -848,7 +1279,8 @@ extern "C" int gs_isect_tile_count_total(const gs_isect_params* p, const float* 
   tile_rows(p, ty0, ty1);
   count_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, means2d, radii, p->tile_size, p->tile_width,
                                                   p->tile_height, ty0, ty1, tiles_per_gauss,
-                                                  reinterpret_cast<unsigned long long*>(total_device));
+                                                  reinterpret_cast<unsigned long long*>(total_device),
+                                                  0);
   return launch_status("intersect_tile_count_total");
 }
 
@@ -1028,6 +1460,184 @@ extern "C" int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_i
   // one error word serves the depth passes and the tile passes
   return read_sort_error(n_isects, static_cast<const char*>(workspace) + L.sort,
                          as_stream(stream));
+}
+
+extern "C" int gs_isect_tile_count_totals(const gs_isect_params* p, const float* means2d,
+                                          const int32_t* radii, int32_t* tiles_per_gauss,
+                                          int64_t* totals_device, gs_stream_t stream) {
+  if (int rc = check_isect(p)) return rc;
+  if (!totals_device) return invalid("intersect_tile_count_totals: missing totals");
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemsetAsync(totals_device, 0, 2 * sizeof(int64_t), s) != cudaSuccess)
+    return launch_status("intersect_tile_count_totals");
+  const int64_t n = (int64_t)p->I * p->N;
+  if (n == 0) return GS_OK;
+  if (!means2d || !radii || !tiles_per_gauss)
+    return invalid("intersect_tile_count_totals: missing buffer");
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
+  count_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, means2d, radii, p->tile_size, p->tile_width,
+                                                  p->tile_height, ty0, ty1, tiles_per_gauss,
+                                                  reinterpret_cast<unsigned long long*>(totals_device),
+                                                  1);
+  return launch_status("intersect_tile_count_totals");
+}
+
+// Bins of the binned encode and their key bits.
+struct BinGeom {
+  int sw, sh;
+  int64_t per_image, total;
+  int bits;
+};
+
+static BinGeom bin_geom(const gs_isect_params* p) {
+  BinGeom g;
+  g.sw = (int)ceil_div(p->tile_width, kBinTiles);
+  g.sh = (int)ceil_div(p->tile_height, kBinTiles);
+  g.per_image = (int64_t)g.sw * g.sh;
+  g.total = (int64_t)p->I * g.per_image;
+  g.bits = g.total > 1 ? 64 - __builtin_clzll((unsigned long long)(g.total - 1)) : 0;
+  return g;
+}
+
+// Workspace of the binned encode; the sort scratch comes first, so that its
+// error word sits at offset 0.
+struct BinnedLayout {
+  size_t sort, nent, nitems, keys, vals, skeys, svals, rects, srects, bstart, chunks, cprefix,
+      icounts, counts, offs, scan, total;
+  int64_t items;  // bound on the work items
+};
+
+static BinnedLayout binned_layout(const gs_isect_params* p, int64_t n_entries) {
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
+  const BinGeom g = bin_geom(p);
+  const int64_t n = (int64_t)p->I * p->N;
+  const int64_t slots = (int64_t)p->I * (ty1 - ty0) * p->tile_width;
+  const int64_t e1 = n_entries < 1 ? 1 : n_entries, n1 = n < 1 ? 1 : n;
+  BinnedLayout L;
+  size_t o = 0;
+  L.sort = o; o += sort_layout(e1).total;
+  L.nent = o; o += 256;
+  L.keys = o; o += align256(8 * (size_t)e1);
+  L.vals = o; o += align256(4 * (size_t)e1);
+  L.skeys = o; o += align256(8 * (size_t)e1);
+  L.svals = o; o += align256(4 * (size_t)e1);
+  L.rects = o; o += align256(8 * (size_t)n1);
+  L.srects = o; o += align256(8 * (size_t)e1);
+  L.items = ceil_div(e1, kItemEntries) + g.total;
+  L.nitems = o; o += 256;
+  L.bstart = o; o += align256(4 * (size_t)(g.total + 1));
+  L.chunks = o; o += align256(4 * (size_t)g.total);
+  L.cprefix = o; o += align256(4 * (size_t)g.total);
+  L.icounts = o; o += align256(64 * (size_t)L.items);
+  L.counts = o; o += align256(4 * (size_t)(slots < 1 ? 1 : slots));
+  L.offs = o; o += align256(4 * (size_t)(slots < 1 ? 1 : slots));
+  L.scan = o;
+  o += std::max(std::max(scan_ws_bytes(n1), scan_ws_bytes(slots < 1 ? 1 : slots)),
+                scan_ws_bytes(g.total));
+  L.total = o;
+  return L;
+}
+
+extern "C" size_t gs_isect_tile_encode_binned_workspace_size(const gs_isect_params* p,
+                                                            int64_t n_bin_entries) {
+  if (!p || check_isect(p) != GS_OK) return 0;
+  return binned_layout(p, n_bin_entries).total;
+}
+
+// Binned sorted encode (see the kernels above): the same isect_ids /
+// flatten_ids as the encode followed by the stable 64-bit key sort, plus
+// the tile offsets of the call's tile rows when tile_offsets is given.
+// n_bin_entries is the second total of gs_isect_tile_count_totals.
+extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float* means2d,
+                                           const int32_t* radii, const float* depths,
+                                           int64_t n_isects, int64_t n_bin_entries,
+                                           int64_t* isect_ids, int32_t* flatten_ids,
+                                           int32_t* tile_offsets, void* workspace,
+                                           size_t workspace_bytes, gs_stream_t stream) {
+  if (int rc = check_isect(p)) return rc;
+  if (n_isects < 0 || n_bin_entries < 0 || n_bin_entries > n_isects)
+    return invalid("intersect_tile_encode_binned: bad intersection / bin entry totals");
+  if (n_isects > INT32_MAX) {
+    set_error("intersect_tile_encode: %lld intersections exceed the int32 offsets", (long long)n_isects);
+    return GS_ERR_OVERFLOW;
+  }
+  const int n_tiles = p->tile_width * p->tile_height;
+  const int tile_bits = gs_floor_log2_plus_one(n_tiles);
+  const int image_bits = gs_floor_log2_plus_one(p->I);
+  if (image_bits + tile_bits > 32)
+    return invalid("intersect_tile_encode image id and tile id require more than 32 bits.");
+  if (p->tile_width > 65535 || p->tile_height > 65535)
+    return invalid("intersect_tile_encode_binned: more than 65535 tiles per row or column "
+                   "(use gs_isect_tile_encode_sorted)");
+  int ty0, ty1;
+  tile_rows(p, ty0, ty1);
+  const int rows = ty1 - ty0;
+  const int64_t slots = (int64_t)p->I * rows * p->tile_width;
+  cudaStream_t s = as_stream(stream);
+  const int64_t n = (int64_t)p->I * p->N;
+  if (n == 0 || n_isects == 0) {
+    if (tile_offsets && slots > 0 &&
+        cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t) * (size_t)slots, s) != cudaSuccess)
+      return launch_status("intersect_tile_encode_binned");
+    return GS_OK;
+  }
+  if (!means2d || !radii || !depths || !isect_ids || !flatten_ids)
+    return invalid("intersect_tile_encode_binned: missing buffer");
+  const BinnedLayout L = binned_layout(p, n_bin_entries);
+  if (!workspace || workspace_bytes < L.total) {
+    set_error("intersect_tile_encode_binned: workspace of %zu bytes needed", L.total);
+    return GS_ERR_WORKSPACE;
+  }
+  char* ws = static_cast<char*>(workspace);
+  const BinGeom g = bin_geom(p);
+  auto K = [&](size_t off) { return reinterpret_cast<uint64_t*>(ws + off); };
+  auto V = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
+  auto R = [&](size_t off) { return reinterpret_cast<uint2*>(ws + off); };
+  cudaMemsetAsync(ws + L.sort + sort_layout(1).err, 0, sizeof(uint32_t), s);
+  BinArgs a{n, p->N, p->tile_size, p->tile_width, p->tile_height, ty0, ty1,
+            g.sw, (int)g.per_image, means2d, radii, depths};
+  const int64_t nb = ceil_div(n, kScanChunk);
+  const size_t scan_bytes = L.total - L.scan;
+  int64_t* sums = reinterpret_cast<int64_t*>(ws + L.scan);
+  bin_count_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(a, sums);
+  scan_sums_kernel<<<1, 1024, 0, s>>>(nb, sums, reinterpret_cast<int64_t*>(ws + L.nent));
+  bin_emit_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(a, sums, n_bin_entries, K(L.keys),
+                                                        V(L.vals), R(L.rects));
+  if (n_bin_entries > 0) {
+    // the depth bits are the low key word and bin ids are unsigned
+    sort_passes(n_bin_entries, 0, 32 + g.bits, kKV, kKV, K(L.keys), V(L.vals), K(L.skeys),
+                V(L.svals), ws + L.sort, s, false, nullptr, nullptr, /*signed_keys=*/false);
+    bin_finish_kernel<<<grid_for(n_bin_entries, 256), 256, 0, s>>>(
+        n_bin_entries, n, K(L.skeys), V(L.svals), R(L.rects), g.total, V(L.bstart), R(L.srects));
+  } else {
+    cudaMemsetAsync(ws + L.bstart, 0, 4 * (size_t)(g.total + 1), s);
+  }
+  // work items: bins cut into chunks
+  bin_chunks_kernel<<<grid_for(g.total, 256), 256, 0, s>>>(g.total, V(L.bstart), V(L.chunks));
+  int64_t* n_items = reinterpret_cast<int64_t*>(ws + L.nitems);
+  if (int rc = scan_i32(g.total, V(L.chunks), V(L.cprefix), n_items, ws + L.scan, scan_bytes, s))
+    return rc;
+  ItemArgs ia{g.total, g.per_image, g.sw, p->tile_width, ty0, rows,
+              V(L.bstart), V(L.cprefix), n_items, R(L.srects)};
+  item_count_kernel<<<(unsigned)L.items, kItemThreads, 0, s>>>(ia, V(L.icounts));
+  int32_t* offs = tile_offsets ? tile_offsets : V(L.offs);
+  if (slots > 0) {
+    slot_count_kernel<<<grid_for(slots, 256), 256, 0, s>>>(ia, slots, V(L.icounts), V(L.counts));
+    if (int rc = scan_i32(slots, V(L.counts), offs, nullptr, ws + L.scan, scan_bytes, s)) return rc;
+  }
+  item_write_kernel<<<(unsigned)L.items, kItemThreads, 0, s>>>(
+      ia, tile_bits, V(L.icounts), offs, K(L.skeys), V(L.svals), n_isects, isect_ids, flatten_ids);
+  return launch_status("intersect_tile_encode_binned");
+}
+
+extern "C" int gs_isect_tile_encode_binned_check(int64_t n_bin_entries, const void* workspace,
+                                                 gs_stream_t stream) {
+  if (n_bin_entries <= 0) return GS_OK;
+  if (!workspace) return invalid("intersect_tile_encode_binned_check: missing workspace");
+  // the sort scratch starts the workspace
+  return read_sort_error(n_bin_entries, static_cast<const char*>(workspace), as_stream(stream));
 }
 
 extern "C" int gs_isect_offset_rows(int64_t n_isects, const int64_t* isect_ids, int32_t I,

@@ -361,6 +361,48 @@ def intersect_tile_encode_sorted(means2d, radii, depths, tiles_per_gauss, I, til
     return isect_ids, flatten_ids
 
 
+def intersect_tile_count_totals(means2d, radii, I, tile_size, tile_width, tile_height):
+    """Tile counts per (image, Gaussian) and, read on the host, the totals
+    of intersections and of the binned encode's entries."""
+    N = means2d.shape[-2]
+    numel = radii.numel() // 2
+    if I <= 0 or numel % I != 0 or numel != I * N:
+        raise RuntimeError("intersect_tile_count dense path expects depths size to equal I * N.")
+    out = _empty(tuple(radii.shape[:-1]), torch.int32)
+    totals = torch.zeros((2,), dtype=torch.int64, device=_device())
+    p = IsectParams(int(I), int(N), int(tile_size), int(tile_width), int(tile_height))
+    check(_lib.load().gs_isect_tile_count_totals(ct.byref(p), _ptr(means2d), _ptr(radii),
+                                                 _ptr(out), _ptr(totals), _stream()),
+          "intersect_tile_count")
+    m, bins = (int(v) for v in totals.tolist())
+    return out, m, bins
+
+
+def intersect_tile_encode_binned(means2d, radii, depths, I, tile_size, tile_width, tile_height,
+                                 total_isects, n_bin_entries, tile_offsets=None):
+    """Encode + stable sort through 4x4-tile bins (one native call);
+    bit-identical to encode then sort.  With ``tile_offsets`` (int32
+    [I, tile_height, tile_width]) the tile offsets are written too."""
+    N = means2d.shape[-2]
+    if total_isects < 0:
+        raise RuntimeError("intersect_tile_encode expects non-negative total_isects.")
+    if total_isects >= 2 ** 31:
+        raise RuntimeError(
+            f"intersect_tile_encode: {total_isects} intersections exceed the int32 index range")
+    isect_ids = _empty((total_isects,), torch.int64)
+    flatten_ids = _empty((total_isects,), torch.int32)
+    lib = _lib.load()
+    p = IsectParams(int(I), int(N), int(tile_size), int(tile_width), int(tile_height))
+    ws = _empty((max(1, lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(p),
+                                                                      n_bin_entries)),),
+                torch.uint8)
+    check(lib.gs_isect_tile_encode_binned(ct.byref(p), _ptr(means2d), _ptr(radii), _ptr(depths),
+                                          int(total_isects), int(n_bin_entries), _ptr(isect_ids),
+                                          _ptr(flatten_ids), _ptr(tile_offsets), _ptr(ws),
+                                          ws.numel(), _stream()), "intersect_tile_encode_binned")
+    return isect_ids, flatten_ids
+
+
 def intersect_tile_sort(isect_ids, flatten_ids, key_bits=64):
     """Stable sort by key (gsplat_intersect.cpp:266-286: argsort + take)."""
     if isect_ids.dtype != torch.int64:
@@ -394,12 +436,22 @@ def intersect_tile_forward(inputs, I, tile_size, tile_width, tile_height, sort=T
     _validate_intersect(means2d, radii, depths, conics, opacities, image_ids, gaussian_ids,
                         segmented)
     means2d, radii, depths = _cuda(means2d, radii, depths)
-    tiles_per_gauss = intersect_tile_count(means2d, radii, I, tile_size, tile_width, tile_height)
-    offsets, total = intersect_tile_offsets(tiles_per_gauss)
-    m = int(total.item()) if tiles_per_gauss.numel() else 0
     n_tiles = tile_width * tile_height
     tile_bits = floor_log2_plus_one(n_tiles)
     image_bits = floor_log2_plus_one(I)
+    if sort and max(tile_width, tile_height) <= 65535:
+        tiles_per_gauss, m, bins = intersect_tile_count_totals(means2d, radii, I, tile_size,
+                                                               tile_width, tile_height)
+        if image_bits + tile_bits > 32:
+            raise RuntimeError(
+                "intersect_tile_encode image id and tile id require more than 32 bits.")
+        isect_ids, flatten_ids = intersect_tile_encode_binned(
+            means2d, radii, depths, I, tile_size, tile_width, tile_height, m, bins)
+        return {"tiles_per_gauss": tiles_per_gauss, "isect_ids": isect_ids,
+                "flatten_ids": flatten_ids}
+    tiles_per_gauss = intersect_tile_count(means2d, radii, I, tile_size, tile_width, tile_height)
+    offsets, total = intersect_tile_offsets(tiles_per_gauss)
+    m = int(total.item()) if tiles_per_gauss.numel() else 0
     if image_bits + tile_bits > 32:
         raise RuntimeError("intersect_tile_encode image id and tile id require more than 32 bits.")
     if sort:

@@ -90,6 +90,11 @@ SIGNATURES = {
     "gs_isect_tile_encode_sorted": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64, _vp, _vp,
                                                _vp, _sz, _vp]),
     "gs_isect_tile_encode_sorted_check": (ct.c_int, [_i64, _i64, _vp, _vp]),
+    "gs_isect_tile_count_totals": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _vp]),
+    "gs_isect_tile_encode_binned_workspace_size": (_sz, [_P(IsectParams), _i64]),
+    "gs_isect_tile_encode_binned": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _i64, _i64, _vp,
+                                               _vp, _vp, _vp, _sz, _vp]),
+    "gs_isect_tile_encode_binned_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -97,17 +97,22 @@ class TrainingStep:
         self.colors = e((C, N, 3))
         self.opac_cn = e((C, N)) if C > 1 else None
         self.tiles_per_gauss = e((C, N), i32)
-        self.total = torch.zeros((1,), dtype=torch.int64, device=self.dev)
-        self.total_host = torch.zeros((1,), dtype=torch.int64, pin_memory=True)
+        # [intersections, bin entries of the binned encode]
+        self.total = torch.zeros((2,), dtype=torch.int64, device=self.dev)
+        self.total_host = torch.zeros((2,), dtype=torch.int64, pin_memory=True)
         self.tile_offsets = e((C, self.th, self.tw), i32)
         self.render_colors = e((C, self.H, self.W, 3))
         self.render_alphas = e((C, self.H, self.W, 1))
         self.last_ids = e((C, self.H, self.W), i32)
         self.backgrounds = torch.zeros((C, 3), dtype=f32, device=self.dev) if use_background else None
         self.v_backgrounds = e((C, 3)) if use_background else None
-        # intersections (grown on demand)
+        # intersections (grown on demand); the binned encode needs 16-bit
+        # tile coordinates, else the depth-first sorted encode runs
+        self.binned = max(self.tw, self.th) <= 65535
         self.capacity = 0
+        self.sort_ws = torch.empty((0,), dtype=torch.uint8, device=self.dev)
         self.m = 0
+        self.bins = 0
         # backward state
         self.v_means2d, self.v_conics = e((C, N, 2)), e((C, N, 3))
         self.v_colors, self.v_opac_cn = e((C, N, 3)), e((C, N))
@@ -125,18 +130,28 @@ class TrainingStep:
             self.lib.gs_floor_log2_plus_one(C)
         self.events = None
 
-    def _ensure_capacity(self, m):
-        """Grows the intersection buffers; True when they were reallocated."""
-        if m <= self.capacity:
-            return False
-        cap = max(int(m * 1.25) + 1024, 1 << 16)
+    def _ensure_capacity(self, m, bins=0):
+        """Grows the intersection buffers and the workspace of the encode;
+        True when the workspace was reallocated."""
         e = lambda shape, dt: torch.empty(shape, dtype=dt, device=self.dev)  # noqa: E731
-        self.sorted_ids = e((cap,), torch.int64)
-        self.sorted_flatten = e((cap,), torch.int32)
-        self.sort_ws = e((self.lib.gs_isect_tile_encode_sorted_workspace_size(self.C * self.N, cap),),
-                         torch.uint8)
-        self.capacity = cap
-        return True
+        grew = False
+        if m > self.capacity:
+            cap = max(int(m * 1.25) + 1024, 1 << 16)
+            self.sorted_ids = e((cap,), torch.int64)
+            self.sorted_flatten = e((cap,), torch.int32)
+            self.capacity = cap
+            if not self.binned:
+                self.sort_ws = e((self.lib.gs_isect_tile_encode_sorted_workspace_size(
+                    self.C * self.N, cap),), torch.uint8)
+                grew = True
+        if self.binned:
+            # sized for every tile row: a band needs less
+            ip = IsectParams(self.C, self.N, self.ts, self.tw, self.th, 0, 0)
+            need = self.lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(ip), bins)
+            if need > self.sort_ws.numel():
+                self.sort_ws = e((int(need * 1.25) + (1 << 20),), torch.uint8)
+                grew = True
+        return grew
 
     def _mark(self, name):
         if self.events is not None:
@@ -164,9 +179,9 @@ class TrainingStep:
         When the step has more than ``max_isects_per_pass`` intersections
         (the int32 offsets of the operator surface cap one pass at 2^31), the
         image is processed in bands of tile rows: each band gets its own
-        count / sorted encode / offsets / rasterize forward and backward
-        (accumulating into the same gradients), all bit-identical to one
-        pass over the rows of the band; projection and SH run once."""
+        count / sorted encode (with its tile offsets) / rasterize forward and
+        backward (accumulating into the same gradients), all bit-identical to
+        one pass over the rows of the band; projection and SH run once."""
         L, s = self.lib, _s()
         C, N = self.C, self.N
         self._mark("start")
@@ -196,13 +211,13 @@ class TrainingStep:
         while b < len(bands):
             y0, y1 = bands[b]
             ip = IsectParams(C, N, self.ts, self.tw, self.th, y0, y1)
-            check(L.gs_isect_tile_count_total(ct.byref(ip), _p(self.means2d), _p(self.radii),
-                                              _p(self.tiles_per_gauss), _p(self.total), s),
+            check(L.gs_isect_tile_count_totals(ct.byref(ip), _p(self.means2d), _p(self.radii),
+                                               _p(self.tiles_per_gauss), _p(self.total), s),
                   "isect_count")
             self.total_host.copy_(self.total, non_blocking=True)
             self._mark("isect_count")
             torch.cuda.current_stream().synchronize()  # the reference's host read of the total
-            m = int(self.total_host.item())
+            m, bins = (int(v) for v in self.total_host.tolist())
             if m > self.max_isects_per_pass and y1 == 0:
                 # too many intersections for one pass (int32 offsets, memory):
                 # bands of tile rows, each with its own intersection pass
@@ -215,21 +230,33 @@ class TrainingStep:
             if m >= 2 ** 31:
                 raise RuntimeError(f"{m} intersections exceed the int32 index range"
                                    + (f" in tile rows {y0}..{y1}" if y1 else ""))
-            # bands after the first reuse the depth order of the elements left
-            # in the workspace (unless the workspace was just reallocated)
-            ip.reuse_depth_order = int(not self._ensure_capacity(m) and b > 0 and y1 > 0)
-            self.m = m
+            grew = self._ensure_capacity(m, bins)
+            self.m, self.bins = m, bins
             m_total += m
-            check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d), _p(self.radii),
-                                                _p(self.depths), _p(self.tiles_per_gauss), m,
-                                                _p(self.sorted_ids), _p(self.sorted_flatten),
-                                                _p(self.sort_ws), self.sort_ws.numel(), s),
-                  "isect_encode_sort")
-            self._mark("isect_encode_sort")
-            r0, r1 = (y0, y1) if y1 else (0, self.th)
-            check(L.gs_isect_offset_rows(m, _p(self.sorted_ids), C, self.tw, self.th, r0, r1,
-                                         _p(self.tile_offsets), s), "isect_offset")
-            self._mark("isect_offset")
+            if self.binned:
+                # sorted intersections and the band's tile offsets in one call
+                check(L.gs_isect_tile_encode_binned(ct.byref(ip), _p(self.means2d),
+                                                    _p(self.radii), _p(self.depths), m, bins,
+                                                    _p(self.sorted_ids), _p(self.sorted_flatten),
+                                                    _p(self.tile_offsets), _p(self.sort_ws),
+                                                    self.sort_ws.numel(), s),
+                      "isect_encode_sort")
+                self._mark("isect_encode_sort")
+            else:
+                # bands after the first reuse the depth order of the elements
+                # left in the workspace (unless it was just reallocated)
+                ip.reuse_depth_order = int(not grew and b > 0 and y1 > 0)
+                check(L.gs_isect_tile_encode_sorted(ct.byref(ip), _p(self.means2d),
+                                                    _p(self.radii), _p(self.depths),
+                                                    _p(self.tiles_per_gauss), m,
+                                                    _p(self.sorted_ids), _p(self.sorted_flatten),
+                                                    _p(self.sort_ws), self.sort_ws.numel(), s),
+                      "isect_encode_sort")
+                self._mark("isect_encode_sort")
+                r0, r1 = (y0, y1) if y1 else (0, self.th)
+                check(L.gs_isect_offset_rows(m, _p(self.sorted_ids), C, self.tw, self.th, r0, r1,
+                                             _p(self.tile_offsets), s), "isect_offset")
+                self._mark("isect_offset")
             rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
                               int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0))
             check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics),
@@ -278,7 +305,10 @@ class TrainingStep:
     def check(self):
         """Waits for the step and raises if a bounded on-device wait of the
         intersection sort gave up (its output would be invalid)."""
-        if self.m > 0:
+        if self.m > 0 and self.binned:
+            check(self.lib.gs_isect_tile_encode_binned_check(self.bins, _p(self.sort_ws), _s()),
+                  "isect_encode_sort")
+        elif self.m > 0:
             check(self.lib.gs_isect_tile_encode_sorted_check(
                 self.C * self.N, self.m, _p(self.sort_ws), _s()), "isect_encode_sort")
 

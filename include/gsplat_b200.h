@@ -221,7 +221,32 @@ int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
                                 void* workspace, size_t workspace_bytes,
                                 gs_stream_t stream);
 
-/* The radix passes of the two calls above and below wait on one another's
+/* Binned encode and sort: the same isect_ids / flatten_ids as
+ * gs_isect_tile_encode_sorted (bit for bit the reference's sorted encode),
+ * built another way: every element lists itself once per 4x4-tile bin its
+ * tile rect touches, those entries are sorted by (bin, depth bits), and one
+ * CTA per tile keeps, in that order, the elements of its bin that cover it.
+ * With tile_offsets (the [I, rows, tile_width] slots of the call's tile
+ * rows, else NULL) it also writes what gs_isect_offset_rows would.
+ * n_isects and n_bin_entries are the two totals of
+ * gs_isect_tile_count_totals over the same rows; the workspace is sized by
+ * gs_isect_tile_encode_binned_workspace_size(p, n_bin_entries).  Tile grids
+ * wider or taller than 65535 tiles are refused (GS_ERR_INVALID).
+ * No reference counterpart. */
+int gs_isect_tile_count_totals(const gs_isect_params* p, const float* means2d,
+                               const int32_t* radii, int32_t* tiles_per_gauss,
+                               int64_t* totals_device /* [2]: intersections, bin entries */,
+                               gs_stream_t stream);
+size_t gs_isect_tile_encode_binned_workspace_size(const gs_isect_params* p,
+                                                  int64_t n_bin_entries);
+int gs_isect_tile_encode_binned(const gs_isect_params* p, const float* means2d,
+                                const int32_t* radii, const float* depths,
+                                int64_t n_isects, int64_t n_bin_entries,
+                                int64_t* isect_ids, int32_t* flatten_ids,
+                                int32_t* tile_offsets, void* workspace,
+                                size_t workspace_bytes, gs_stream_t stream);
+
+/* The radix passes of the calls above and below wait on one another's
  * tiles with bounded waits; a wait that gives up (a defect, not a workload
  * condition) raises an error word in the workspace and the kernels finish
  * with invalid output.  These read that word for the last call that used
@@ -229,6 +254,8 @@ int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
  * No reference counterpart. */
 int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_isects,
                                       const void* workspace, gs_stream_t stream);
+int gs_isect_tile_encode_binned_check(int64_t n_bin_entries, const void* workspace,
+                                      gs_stream_t stream);
 int gs_isect_sort_check(int64_t n_isects, const void* workspace, gs_stream_t stream);
 
 /* Stable ascending sort of (isect_ids, flatten_ids) by the signed 64-bit

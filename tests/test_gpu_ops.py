@@ -408,6 +408,63 @@ def test_intersect_sorted_depth_bits(gs, oracle, cuda):
     assert torch.equal(sk, g["isect_ids"]) and torch.equal(sv, g["flatten_ids"])
 
 
+def test_intersect_binned_offsets_bands_and_fallback(gs, oracle, cuda):
+    """The binned encode (the sort=True path) also writes the tile offsets;
+    over a window of tile rows it gives exactly that window's part of the
+    full sorted list and its offsets; the depth-first sorted encode (the
+    path for tile grids past 16-bit coordinates) gives the same lists."""
+    import ctypes as ct
+    from gsplat_core import _gsplat_core as G, _lib
+    from gsplat_core._lib import IsectParams
+    lib = _lib.load()
+    rng = np.random.default_rng(11)
+    I, N, ts, tw, th = 2, 40_000, 16, 37, 23
+    m2 = rng.uniform(-30, tw * ts + 30, size=(I, N, 2)).astype(np.float32)
+    rad = rng.integers(-2, 40, size=(I, N, 2)).astype(np.int32)
+    dep = rng.uniform(0.1, 20, size=(I, N)).astype(np.float32)
+    dep[:, ::5] = dep[:, 1:2]  # ties: element order decides
+    e = oracle.isect_tile(m2, rad, dep, I, ts, tw, th)
+    eo = oracle.isect_offset(e["isect_ids"], I, tw, th)
+    tpg, m, bins = G.intersect_tile_count_totals(T(m2), T(rad), I, ts, tw, th)
+    assert m == len(e["isect_ids"]) and 0 < bins <= m
+    offs = torch.full((I, th, tw), -1, dtype=torch.int32, device="cuda")
+    ids, fids = G.intersect_tile_encode_binned(T(m2), T(rad), T(dep), I, ts, tw, th, m, bins, offs)
+    assert_exact(ids, e["isect_ids"], "binned isect_ids")
+    assert_exact(fids, e["flatten_ids"], "binned flatten_ids")
+    assert_exact(offs, eo, "binned tile offsets")
+    sid, sfid = G.intersect_tile_encode_sorted(T(m2), T(rad), T(dep), tpg, I, ts, tw, th, m)
+    assert torch.equal(sid, ids) and torch.equal(sfid, fids)
+    # tile rows [y0, y1) only
+    y0, y1 = 5, 14
+    tb = gs.floor_log2_plus_one(tw * th)
+    tile = (e["isect_ids"] >> 32) & ((1 << tb) - 1)
+    keep = (tile // tw >= y0) & (tile // tw < y1)
+    bid, bfid = e["isect_ids"][keep], e["flatten_ids"][keep]
+    keys = np.array([(i << tb) | (y * tw + x) for i in range(I) for y in range(y0, y1)
+                     for x in range(tw)], np.int64)
+    bofs = np.searchsorted(bid >> 32, keys, side="left").astype(np.int32)
+    p = IsectParams(I, N, ts, tw, th, y0, y1)
+    s = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ct.c_void_p(t.data_ptr())  # noqa: E731
+    tot = torch.zeros(2, dtype=torch.int64, device="cuda")
+    tpg_b = torch.empty((I, N), dtype=torch.int32, device="cuda")
+    dm2, drad, ddep = T(m2), T(rad), T(dep)
+    assert lib.gs_isect_tile_count_totals(ct.byref(p), P(dm2), P(drad), P(tpg_b), P(tot), s) == 0
+    mb, binsb = (int(v) for v in tot.tolist())
+    assert mb == len(bid)
+    ob = torch.full((I, y1 - y0, tw), -1, dtype=torch.int32, device="cuda")
+    oid = torch.empty(mb, dtype=torch.int64, device="cuda")
+    ofid = torch.empty(mb, dtype=torch.int32, device="cuda")
+    ws = torch.empty(lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(p), binsb),
+                     dtype=torch.uint8, device="cuda")
+    assert lib.gs_isect_tile_encode_binned(ct.byref(p), P(dm2), P(drad), P(ddep), mb, binsb,
+                                           P(oid), P(ofid), P(ob), P(ws), ws.numel(), s) == 0
+    assert lib.gs_isect_tile_encode_binned_check(binsb, P(ws), s) == 0
+    assert_exact(oid, bid, "band isect_ids")
+    assert_exact(ofid, bfid, "band flatten_ids")
+    assert_exact(ob.reshape(-1), bofs, "band tile offsets")
+
+
 def test_sort_error_words_clear(gs, cuda):
     """The bounded look-back waits of a sort end normally: the error word the
     check entry points read stays clear (GS_OK) after real sorts."""
