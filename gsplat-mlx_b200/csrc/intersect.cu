@@ -897,11 +897,23 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t base = (int64_t)blockIdx.x * kScanChunk;
   int64_t block_run = sums[blockIdx.x];
+  // every round's element loads in flight before the first round's work
+  int2 rad[kScanItems];
+  float2 mu[kScanItems];
+#pragma unroll
+  for (int round = 0; round < kScanItems; ++round) {
+    const int64_t i = base + (int64_t)round * kScanThreads + threadIdx.x;
+    rad[round] = i < a.n ? __ldg(reinterpret_cast<const int2*>(a.radii) + i) : make_int2(0, 0);
+    mu[round] = i < a.n ? __ldg(reinterpret_cast<const float2*>(a.means2d) + i)
+                        : make_float2(0.0f, 0.0f);
+  }
+#pragma unroll
   for (int round = 0; round < kScanItems; ++round) {
     const int64_t i = base + (int64_t)round * kScanThreads + threadIdx.x;
     int c = 0;
     if (i < a.n) {
-      const Rect q = element_rect(a, i);
+      const Rect q = band_rect(mu[round].x, mu[round].y, rad[round].x, rad[round].y, a.ts, a.tw,
+                               a.th, a.ty0, a.ty1);
       c = rect_bins(q);
       if (c > 0) {
         const int64_t image = i / a.n_per_image;
@@ -1141,7 +1153,8 @@ __global__ void __launch_bounds__(256) slot_count_kernel(const ItemArgs a, int64
 // entries before it in this item -- as the full key and the element id.
 // Rounds of one entry per thread (consecutive entries on consecutive
 // threads) and, within a round, tile by tile: the lanes that cover a tile
-// store to consecutive places.
+// store to consecutive places.  (Staging a round's copies tile-major in
+// shared memory and storing them densely was slower: 64 KB per CTA.)
 __global__ void __launch_bounds__(kItemThreads) item_write_kernel(
     const ItemArgs a, int tile_bits, const int32_t* __restrict__ item_counts,
     const int32_t* __restrict__ offsets, const uint64_t* __restrict__ keys,
