@@ -440,8 +440,11 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
 // staged packed: a = (mean x, mean y, conic0, conic1), b = (conic2, opacity,
 // col0, col1), c = (col2, col3), in batches of one per thread.  Per-pixel
 // arithmetic is unchanged.
-constexpr int kT16Pixels = 4;                     // P
-constexpr int kT16Threads = 256 / kT16Pixels;
+// P pixels per thread (256 / P threads per tile): P = 4 when the grid has
+// enough tiles to fill every SM many times over; P = 1 for small grids,
+// where a tile's CTA must bring more warps of its own to hide latency.
+constexpr int kT16Pixels = 4;
+constexpr int kT16SmallPixels = 1;
 
 // Can the Gaussian reach alpha >= 1/255 at any pixel centre of the tile?
 // sigma(d) = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy is convex for a positive
@@ -484,7 +487,7 @@ __device__ __forceinline__ bool tile_may_hit(float mx, float my, float c0, float
 // number kept.  Entries: a = (mean x, mean y, conic0, conic1),
 // b = (conic2, opacity, col0, col1), c = (col2, col3), the intersection
 // index and the Gaussian id.
-template <int CH>
+template <int CH, int THREADS>
 __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0, float y0,
                                        float4* sa, float4* sb, float2* sc, int* sidx, int* sgid,
                                        int* swcnt) {
@@ -504,7 +507,7 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
   __syncthreads();
   int base = 0, cnt = 0;
 #pragma unroll
-  for (int w = 0; w < kT16Threads / 32; ++w) {
+  for (int w = 0; w < THREADS / 32; ++w) {
     const int c = swcnt[w];
     base += w < warp ? c : 0;
     cnt += c;
@@ -548,18 +551,18 @@ __device__ __forceinline__ void composite16(float dx, float dy, const float4& A,
 }
 
 // Both 16x16 kernels are capped at 64 registers (16 CTAs of 64 threads per
-// SM): a few bytes of spill outside the Gaussian loop, ~2% faster than the
-// 71-72 registers (14 CTAs) the compiler picks on its own.
-template <int CH>
-__global__ void __launch_bounds__(kT16Threads, 16) raster_fwd16_kernel(
+// SM at P = 4): a few bytes of spill outside the Gaussian loop, ~2% faster
+// than the 71-72 registers (14 CTAs) the compiler picks on its own.
+template <int CH, int P>
+__global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
     RArgs a, float* __restrict__ render_colors, float* __restrict__ render_alphas,
     int32_t* __restrict__ last_ids) {
-  constexpr int P = kT16Pixels, RS = 16 / P;  // pixels per thread, row stride
-  __shared__ float4 s_a[kT16Threads];
-  __shared__ float4 s_b[kT16Threads];
-  __shared__ float2 s_c[kT16Threads];
-  __shared__ int s_idx[kT16Threads];
-  __shared__ int s_wcnt[kT16Threads / 32];
+  constexpr int THREADS = 256 / P, RS = 16 / P;  // threads, row stride of a thread's pixels
+  __shared__ float4 s_a[THREADS];
+  __shared__ float4 s_b[THREADS];
+  __shared__ float2 s_c[THREADS];
+  __shared__ int s_idx[THREADS];
+  __shared__ int s_wcnt[THREADS / 32];
   const TileIdx ti = tile_of(a);
   const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x;
@@ -605,9 +608,9 @@ __global__ void __launch_bounds__(kT16Threads, 16) raster_fwd16_kernel(
     return d;
   };
 
-  for (int b0 = start; b0 < end; b0 += kT16Threads) {
+  for (int b0 = start; b0 < end; b0 += THREADS) {
     if (__syncthreads_count(!all_done()) == 0) break;
-    const int cnt = stage16<CH>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
+    const int cnt = stage16<CH, THREADS>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
                                 s_c, s_idx, nullptr, s_wcnt);
     for (int j = 0; j < cnt; ++j) {
       if (all_done()) break;
@@ -691,23 +694,23 @@ __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, co
   return true;
 }
 
-template <int CH, bool ABS>
-__global__ void __launch_bounds__(kT16Threads, 16) raster_bwd16_kernel(
+template <int CH, bool ABS, int P>
+__global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
     RArgs a, const float* __restrict__ render_alphas, const int32_t* __restrict__ last_ids,
     const float* __restrict__ v_render_colors, const float* __restrict__ v_render_alphas,
     int absgrad, float* __restrict__ v_means2d_abs, float* __restrict__ v_means2d,
     float* __restrict__ v_conics, float* __restrict__ v_colors, float* __restrict__ v_opacities,
     float* __restrict__ v_backgrounds) {
-  constexpr int P = kT16Pixels, RS = 16 / P;  // pixels per thread, row stride
+  constexpr int THREADS = 256 / P, RS = 16 / P;  // threads, row stride of a thread's pixels
   constexpr int CB = ABS ? 8 : 6;  // index of the first colour term
   constexpr int NT = CB + CH;      // gradient terms per Gaussian
-  __shared__ float4 s_a[kT16Threads];
-  __shared__ float4 s_b[kT16Threads];
-  __shared__ float2 s_c[kT16Threads];
-  __shared__ int s_idx[kT16Threads];
-  __shared__ int s_gid[kT16Threads];
-  __shared__ int s_wcnt[kT16Threads / 32];
-  __shared__ float s_acc[kT16Threads * NT];
+  __shared__ float4 s_a[THREADS];
+  __shared__ float4 s_b[THREADS];
+  __shared__ float2 s_c[THREADS];
+  __shared__ int s_idx[THREADS];
+  __shared__ int s_gid[THREADS];
+  __shared__ int s_wcnt[THREADS / 32];
+  __shared__ float s_acc[THREADS * NT];
   __shared__ int s_last;
   __shared__ float s_bg[4];
   const TileIdx ti = tile_of(a);
@@ -765,12 +768,12 @@ __global__ void __launch_bounds__(kT16Threads, 16) raster_bwd16_kernel(
     atomicAdd(v_backgrounds + image * CH + tid, s_bg[tid]);
   const int cta_last = s_last;
 
-  for (int b_end = cta_last + 1; b_end > start; b_end -= kT16Threads) {
-    const int b0 = max(start, b_end - kT16Threads);
+  for (int b_end = cta_last + 1; b_end > start; b_end -= THREADS) {
+    const int b0 = max(start, b_end - THREADS);
     __syncthreads();
-    const int cnt = stage16<CH>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
+    const int cnt = stage16<CH, THREADS>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
                                 s_c, s_idx, s_gid, s_wcnt);
-    for (int i = tid; i < cnt * NT; i += kT16Threads) s_acc[i] = 0.0f;
+    for (int i = tid; i < cnt * NT; i += THREADS) s_acc[i] = 0.0f;
     __syncthreads();
     for (int j = cnt - 1; j >= 0; --j) {
       const int idx = s_idx[j];
@@ -817,7 +820,7 @@ __global__ void __launch_bounds__(kT16Threads, 16) raster_bwd16_kernel(
       }
     }
     __syncthreads();
-    for (int i = tid; i < cnt * NT; i += kT16Threads) {
+    for (int i = tid; i < cnt * NT; i += THREADS) {
       const float v = s_acc[i];
       if (v == 0.0f) continue;
       const int j = i / NT, k = i - j * NT;
@@ -835,11 +838,21 @@ int smem_bytes(int block, int ch, bool bwd) {
   return (int)sizeof(float) * (block * (6 + ch) + (bwd ? block * (8 + ch) : 0));
 }
 
+// Fewer tiles than 8 per SM: the four-pixel kernels' two-warp CTAs would
+// leave most schedulers without a warp to switch to.
+inline bool small_grid(int64_t tiles) { return tiles < 8 * (int64_t)sm_count(); }
+
 template <int CH>
 int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cudaStream_t s) {
   if (CH > 0 && a.ts == 16) {
-    raster_fwd16_kernel<(CH > 0 ? CH : 1)><<<(unsigned)((int64_t)a.I * a.rows * a.tw), kT16Threads, 0, s>>>(
-        a, rc, ra, li);
+    constexpr int C1 = CH > 0 ? CH : 1;
+    const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
+    if (small_grid(tiles))
+      raster_fwd16_kernel<C1, kT16SmallPixels><<<(unsigned)tiles, 256 / kT16SmallPixels, 0, s>>>(
+          a, rc, ra, li);
+    else
+      raster_fwd16_kernel<C1, kT16Pixels><<<(unsigned)tiles, 256 / kT16Pixels, 0, s>>>(a, rc, ra,
+                                                                                        li);
     return launch_status("rasterize_fwd");
   }
   const int smem = smem_bytes(block, a.CH, false);
@@ -855,13 +868,21 @@ int launch_bwd(const RArgs& a, int block, const float* ra, const int32_t* li, co
                float* vop, float* vbg, cudaStream_t s) {
   if (CH > 0 && a.ts == 16) {
     constexpr int C1 = CH > 0 ? CH : 1;
-    const unsigned grid = (unsigned)((int64_t)a.I * a.rows * a.tw);
-    if (absgrad)
-      raster_bwd16_kernel<C1, true><<<grid, kT16Threads, 0, s>>>(a, ra, li, vrc, vra, absgrad,
-                                                                 vabs, vm, vc, vcol, vop, vbg);
-    else
-      raster_bwd16_kernel<C1, false><<<grid, kT16Threads, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+    const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
+    const unsigned grid = (unsigned)tiles;
+    constexpr int PS = kT16SmallPixels, PL = kT16Pixels;
+    if (small_grid(tiles) && absgrad)
+      raster_bwd16_kernel<C1, true, PS><<<grid, 256 / PS, 0, s>>>(a, ra, li, vrc, vra, absgrad,
                                                                   vabs, vm, vc, vcol, vop, vbg);
+    else if (small_grid(tiles))
+      raster_bwd16_kernel<C1, false, PS><<<grid, 256 / PS, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+                                                                   vabs, vm, vc, vcol, vop, vbg);
+    else if (absgrad)
+      raster_bwd16_kernel<C1, true, PL><<<grid, 256 / PL, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+                                                                  vabs, vm, vc, vcol, vop, vbg);
+    else
+      raster_bwd16_kernel<C1, false, PL><<<grid, 256 / PL, 0, s>>>(a, ra, li, vrc, vra, absgrad,
+                                                                   vabs, vm, vc, vcol, vop, vbg);
     return launch_status("rasterize_bwd");
   }
   const int smem = smem_bytes(block, a.CH, true);
