@@ -47,6 +47,19 @@ class SHGlueParams(ct.Structure):
                 ("use_masks", _i32), ("skip_zero_cotangents", _i32)]
 
 
+class DensifyParams(ct.Structure):
+    _fields_ = [("C", _i32), ("N", _i32), ("width", _i32), ("height", _i32), ("n_cameras", _i32)]
+
+
+class DensifyMaskParams(ct.Structure):
+    _fields_ = [("n", _i64), ("n_original", _i64), ("step", _i32), ("compute_grow", _i32),
+                ("compute_prune", _i32), ("refine_scale2d_stop_iter", _i32),
+                ("reset_every", _i32), ("pad_", _i32), ("grow_grad2d", ct.c_double),
+                ("grow_scale3d", ct.c_double), ("grow_scale2d", ct.c_double),
+                ("prune_opa", ct.c_double), ("prune_scale3d", ct.c_double),
+                ("prune_scale2d", ct.c_double), ("scene_scale", ct.c_double)]
+
+
 class AdamParams(ct.Structure):
     _fields_ = [("n", _i64), ("learning_rate", _f), ("beta1", _f), ("beta2", _f), ("eps", _f)]
 
@@ -104,6 +117,8 @@ SIGNATURES = {
     "gs_fit_activate": (ct.c_int, [_i64] + [_vp] * 9),
     "gs_l2_loss_grad": (ct.c_int, [_i64] + [_vp] * 5),
     "gs_fit_adam": (ct.c_int, [_P(AdamParams)] + [_vp] * 17),
+    "gs_densify_accumulate": (ct.c_int, [_P(DensifyParams)] + [_vp] * 6),
+    "gs_densify_masks": (ct.c_int, [_P(DensifyMaskParams)] + [_vp] * 10),
     "gs_rasterize_fwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 12),
     "gs_rasterize_bwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 19),
 }

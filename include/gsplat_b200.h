@@ -384,6 +384,54 @@ int gs_fit_adam(const gs_adam_params* p, float* means, float* quats, float* log_
                 float* quats_n, float* scales, float* colors, float* opacities,
                 gs_stream_t stream);
 
+/* ------------------------------------------------------------------ */
+/* Densification statistics of the reference trainer's default        */
+/* strategy (scripts/test/scanner_points_training_utils.py,           */
+/* ScannerDefaultStrategyRuntime) on device.                           */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int32_t C, N;             /* cameras, Gaussians                       */
+  int32_t width, height;    /* image size                               */
+  int32_t n_cameras;        /* the gradient scale's camera factor       */
+} gs_densify_params;
+
+/* update_state (:412-451): for each (camera, Gaussian) with both radii
+ * positive, grad2d[n] += |v_means2d[c,n] * (W/2, H/2) * n_cameras| and
+ * count[n] += 1, cameras in order, fp32 as the reference (bit for bit).
+ * With max_radii (the reference keeps it when refine_scale2d_stop_iter >
+ * 0): max_radii[n] = max(max_radii[n], larger radius of the last camera
+ * that sees n / max(W, H)).  v_means2d [C,N,2] (or the absgrad buffer),
+ * radii [C,N,2]; grad2d, count, max_radii [N] are accumulated in place. */
+int gs_densify_accumulate(const gs_densify_params* p, const float* v_means2d,
+                          const int32_t* radii, float* grad2d, float* count,
+                          float* max_radii, gs_stream_t stream);
+
+typedef struct {
+  int64_t n;                        /* Gaussians now                         */
+  int64_t n_original;               /* split only below this index           */
+  int32_t step;
+  int32_t compute_grow;             /* clone and split masks                 */
+  int32_t compute_prune;            /* prune mask                            */
+  int32_t refine_scale2d_stop_iter; /* > 0: max_radii terms while step < it  */
+  int32_t reset_every;              /* scale prunes only when step > it      */
+  int32_t pad_;
+  double grow_grad2d, grow_scale3d, grow_scale2d;
+  double prune_opa, prune_scale3d, prune_scale2d, scene_scale;
+} gs_densify_mask_params;
+
+/* The refine masks (uint8, one per Gaussian): clone (:556-569), split
+ * (:639-657) and prune (:706-718) -- the reference computes clone and split
+ * from the same statistics (split skips the clones it appends) and prune
+ * after both, so the caller asks for grow and prune in two calls around
+ * its clone/split.  totals_device (int64[6]): clone, split, prune, prune by
+ * opacity, by 3D scale, by 2D radius.  Decisions that need exp() can differ
+ * from numpy's only within a few ulp of their thresholds. */
+int gs_densify_masks(const gs_densify_mask_params* p, const float* grad2d,
+                     const float* count, const float* max_radii,
+                     const float* log_scales, const float* opacity_logits,
+                     uint8_t* clone, uint8_t* split, uint8_t* prune,
+                     int64_t* totals_device, gs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -238,3 +238,37 @@ def test_oracle_against_live_reference(oracle):
     assert_exact(oracle.sh_fwd(3, dirs, co), ref.sh_fwd(3, dirs, co), "sh live")
     ids = np.sort(rng.integers(0, 1 << 45, size=5000)).astype(np.int64)
     assert_exact(oracle.isect_offset(ids, 2, 64, 64), ref.isect_offset(ids, 2, 64, 64), "offsets")
+
+
+def _densify_cfg(d):
+    cfg = {k: float(d[k]) for k in ("grow_grad2d", "grow_scale3d", "grow_scale2d", "prune_opa",
+                                    "prune_scale3d", "prune_scale2d", "scene_scale")}
+    cfg["refine_scale2d_stop_iter"] = int(d["refine_scale2d_stop_iter"])
+    cfg["reset_every"] = int(d["reset_every"])
+    return cfg
+
+
+def test_densify_oracle_matches_reference(golden):
+    """oracle/densify.py against the reference trainer's own
+    ScannerDefaultStrategyRuntime (tests/golden/make_densify_golden.py):
+    statistics bit for bit, clone selection, split mask, prune keep set."""
+    from oracle import densify as D
+    d = golden("densify")
+    n = int(d["N"])
+    g, c, r = (np.zeros(n, np.float32) for _ in range(3))
+    for t in range(d["v_means2d"].shape[0]):
+        D.accumulate(d["v_means2d"][t], d["radii_in"][t], int(d["W"]), int(d["H"]), int(d["C"]),
+                     g, c, r)
+    assert_exact(g, d["grad2d"], "grad2d")
+    assert_exact(c, d["count"], "count")
+    assert_exact(r, d["radii"], "radii")
+    cfg = _densify_cfg(d)
+    m = D.masks(g, c, r, d["log_scales"], d["opacity_logits"], int(d["step"]), n, cfg,
+                grow=True, prune=False)
+    assert_exact(np.nonzero(m["clone"])[0], d["clone_selected"], "clone selection")
+    assert_exact(m["split"], d["split_mask"][:n], "split mask")
+    assert not d["split_mask"][n:].any()
+    p = D.masks(None, None, d["prune_radii"], d["prune_log_scales"], d["prune_opacity_logits"],
+                int(d["step"]), n, cfg, grow=False, prune=True)
+    assert_exact(np.nonzero(~p["prune"])[0], d["prune_keep"], "prune keep set")
+    assert_exact(p["prune_breakdown"], d["prune_breakdown"], "prune breakdown")
