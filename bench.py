@@ -42,8 +42,8 @@ LINK_GBS = 770.0
 # DRAM bytes (read + write) per launch of each stage's dominant kernel from
 # one ncu capture of this benchmark (profiles/*_config3.md); None = not
 # captured.  Valid for the config-3 workload only.
-PROFILED_TRAFFIC = {"rasterize_bwd": 44.4e6 + 0.2e6, "rasterize_fwd": 18.2e6 + 0.02e6,
-                    "sh_bwd": 118.2e6 + 147.7e6}
+PROFILED_TRAFFIC = {"rasterize_bwd": 44.4e6 + 0.2e6, "rasterize_fwd": 15.9e6 + 0.01e6,
+                    "sh_bwd": 119.9e6 + 150.2e6}
 
 
 def load_peaks():

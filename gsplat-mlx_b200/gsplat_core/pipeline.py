@@ -160,7 +160,7 @@ class TrainingStep:
             self.events.append((name, ev))
 
     def run(self, means, quats, scales, opacities, coeffs, viewmats, Ks, v_render_colors,
-            v_render_alphas, sh_backward=True, colors=None, target=None):
+            v_render_alphas, sh_backward=True, colors=None, target=None, after_raster=None):
         """Forward and backward; returns the flat gradient buffer (a view of
         self.grad_flat) and the intersection count of this step.
 
@@ -175,6 +175,11 @@ class TrainingStep:
         ``target`` [C,H,W,3] replaces the given cotangents by those of the
         L2 loss mean((render - target)^2), whose value lands in the device
         scalar ``self.loss``.
+
+        ``after_raster()`` is called once the rasterizer backward of every
+        band is queued (``self.v_colors`` complete on the stream), before the
+        projection backward: the camera-sharded step starts its colour
+        exchange there.
 
         When the step has more than ``max_isects_per_pass`` intersections
         (the int32 offsets of the operator surface cap one pass at 2^31), the
@@ -286,6 +291,8 @@ class TrainingStep:
             b += 1
         m = m_total
         self.bands = len(bands)
+        if after_raster is not None:
+            after_raster()
         if C > 1:
             torch.sum(self.v_opac_cn, dim=0, out=self.v_opacities)
         check(L.gs_projection_bwd(ct.byref(pp), _p(means), None, _p(quats), _p(scales),

@@ -63,15 +63,18 @@ def choose_exchange(n, K, cameras_per_rank, world):
     return "gather" if ga < ar else "allreduce"
 
 
-def _all_gather(out, inp, group):
-    """all-gather of equal-size contiguous shards into ``out`` (rank-major)."""
+def _all_gather(out, inp, group, async_op=False):
+    """all-gather of equal-size contiguous shards into ``out`` (rank-major);
+    with ``async_op`` the work handle (wait() before reading ``out``)."""
     if dist.get_backend(group) == "nccl":
-        dist.all_gather_into_tensor(out, inp, group=group)
-    else:  # gloo has no all_gather_into_tensor
-        dist.all_gather(list(out.chunk(dist.get_world_size(group))), inp, group=group)
+        return dist.all_gather_into_tensor(out, inp, group=group, async_op=async_op)
+    # gloo has no all_gather_into_tensor
+    return dist.all_gather(list(out.chunk(dist.get_world_size(group))), inp, group=group,
+                           async_op=async_op)
 
 
-def exchange_gradients(mode, grad_flat, n, v_colors_local, v_colors_all, sh_backward, group=None):
+def exchange_gradients(mode, grad_flat, n, v_colors_local, v_colors_all, sh_backward, group=None,
+                       gathering=None):
     """Sum the per-Gaussian gradients of all ranks into ``grad_flat``.
 
     mode "allreduce": ``grad_flat`` already holds this rank's complete
@@ -82,13 +85,18 @@ def exchange_gradients(mode, grad_flat, n, v_colors_local, v_colors_all, sh_back
     runs asynchronously while ``sh_backward(v_colors_all)`` writes v_coeffs
     (``grad_flat[11N:]``, outside the reduced range) for all cameras and
     returns the SH part of v_means, which is added once the reduction is
-    done."""
+    done.  ``gathering``: the handle of an all-gather of the colour
+    cotangents already started (the sharded step starts it before the
+    projection backward), waited for instead of gathering here."""
     if mode == "allreduce":
         dist.all_reduce(grad_flat, group=group)
         return
     if mode != "gather":
         raise ValueError(f"unknown exchange {mode!r}")
-    _all_gather(v_colors_all.view(-1), v_colors_local.reshape(-1), group)
+    if gathering is not None:
+        gathering.wait()
+    else:
+        _all_gather(v_colors_all.view(-1), v_colors_local.reshape(-1), group)
     work = dist.all_reduce(grad_flat[:11 * n], group=group, async_op=True)
     v_means_sh = sh_backward(v_colors_all)
     work.wait()
@@ -138,9 +146,17 @@ class ShardedTrainingStep:
         from .pipeline import sh_colors_backward
         st = self.step
         gather = self.exchange == "gather" and self.world > 1
+        gathering = []
+
+        def start_gather():
+            # the colour cotangents are final once the rasterizer backward
+            # ran: their all-gather overlaps the projection backward
+            gathering.append(_all_gather(self.v_colors_all.view(-1), st.v_colors.reshape(-1),
+                                         self.group, async_op=True))
+
         flat, m = st.run(means, quats, scales, opacities, coeffs, self.local(viewmats_all),
                          self.local(Ks_all), v_render_colors, v_render_alphas,
-                         sh_backward=not gather)
+                         sh_backward=not gather, after_raster=start_gather if gather else None)
         if self.world == 1:
             return flat, m
 
@@ -152,7 +168,8 @@ class ShardedTrainingStep:
             return self.v_means_sh
 
         exchange_gradients("gather" if gather else "allreduce", flat, self.N, st.v_colors,
-                           self.v_colors_all, sh_bwd, self.group)
+                           self.v_colors_all, sh_bwd, self.group,
+                           gathering=gathering[0] if gathering else None)
         return flat, m
 
     def gradients(self):

@@ -102,12 +102,13 @@ def _worker(rank, world, port, mode, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from oracle.oracle import Oracle
-        from gsplat_core.sharded import camera_shard, exchange_gradients
+        from gsplat_core.sharded import _all_gather, camera_shard, exchange_gradients
         oracle = Oracle()
         sc, vrc, vra = _scene()
         a, b = camera_shard(sc.viewmats.shape[0], world, rank)
         cams = list(range(a, b))
         flat_np, v_colors = _camera_grads(oracle, sc, cams, vrc, vra, with_sh=(mode == "allreduce"))
+        v_local = torch.from_numpy(np.ascontiguousarray(v_colors))
         flat = torch.from_numpy(flat_np)
         v_all = torch.empty((sc.viewmats.shape[0], sc.n, 3), dtype=torch.float32)
         n, K = sc.n, sc.coeffs.shape[1]
@@ -118,15 +119,20 @@ def _worker(rank, world, port, mode, out_dir):
             flat[11 * n:] = torch.from_numpy(gb["v_coeffs"].ravel())
             return torch.from_numpy(gb["v_means"])
 
-        exchange_gradients(mode, flat, n, torch.from_numpy(np.ascontiguousarray(v_colors)), v_all,
-                           sh_backward)
+        gathering = None
+        if mode == "gather_started":
+            # the sharded step starts the colour all-gather before its
+            # projection backward and hands the handle over
+            gathering = _all_gather(v_all.view(-1), v_local.reshape(-1), None, async_op=True)
+        exchange_gradients("gather" if mode == "gather_started" else mode, flat, n, v_local, v_all,
+                           sh_backward, gathering=gathering)
         np.save(os.path.join(out_dir, f"{mode}_{rank}.npy"), flat.numpy())
         assert K == 16
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["allreduce", "gather"])
+@pytest.mark.parametrize("mode", ["allreduce", "gather", "gather_started"])
 def test_two_rank_exchange_matches_single_process(oracle, tmp_path, mode):
     sc, vrc, vra = _scene()
     expect, _ = _camera_grads(oracle, sc, list(range(sc.viewmats.shape[0])), vrc, vra, True)
