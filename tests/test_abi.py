@@ -89,3 +89,32 @@ def test_invalid_arguments_rejected_before_launch(gs):
     pp = L.ProjectionParams(1, 1, 1, 8, 8, 0.3, 0.01, 1e10, 0.0, 0, 1, 0, 0)
     assert lib.gs_projection_bwd(ct.byref(pp), *([None] * 19)) == L.GS_ERR_INVALID
     assert b"pinhole only" in lib.gs_last_error()
+
+
+def test_binned_encode_and_densify_validate_before_device_work(gs):
+    """Bad arguments of the binned encode and the densify entries come back
+    as GS_ERR_INVALID with a message, before any device call (runs on a
+    machine without a GPU)."""
+    from gsplat_core import _lib as L
+    lib = gs.load()
+    p = L.IsectParams(1, 10, 16, 4, 4, 0, 0, 0)
+    # more bin entries than intersections cannot come from one count
+    rc = lib.gs_isect_tile_encode_binned(ct.byref(p), None, None, None, 5, 6, None, None, None,
+                                         None, 0, None)
+    assert rc == L.GS_ERR_INVALID and b"bin entry" in lib.gs_last_error()
+    wide = L.IsectParams(1, 10, 16, 70000, 2, 0, 0, 0)
+    rc = lib.gs_isect_tile_encode_binned(ct.byref(wide), None, None, None, 5, 5, None, None, None,
+                                         None, 0, None)
+    assert rc == L.GS_ERR_INVALID and b"65535" in lib.gs_last_error()
+    assert lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(L.IsectParams(0, 10, 16, 4, 4,
+                                                                                0, 0, 0)), 5) == 0
+    assert lib.gs_isect_tile_count_totals(ct.byref(p), None, None, None, None, None) == \
+        L.GS_ERR_INVALID
+    dp = L.DensifyParams(0, 10, 8, 8, 1)
+    assert lib.gs_densify_accumulate(ct.byref(dp), None, None, None, None, None, None) == \
+        L.GS_ERR_INVALID
+    mp = L.DensifyMaskParams()
+    mp.n = 4
+    assert lib.gs_densify_masks(ct.byref(mp), None, None, None, None, None, None, None, None,
+                                None, None) == L.GS_ERR_INVALID
+    assert b"totals" in lib.gs_last_error()
