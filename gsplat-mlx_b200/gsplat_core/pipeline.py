@@ -197,11 +197,9 @@ class TrainingStep:
                                   _p(self.conics), None, _p(self.radii), s), "projection_fwd")
         self._mark("projection_fwd")
         gp = SHGlueParams(C, N, self.K, self.deg, 0)
-        if colors is None:
-            check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
-                                   _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
+        glue_pending = colors is None
+        if glue_pending:
             colors = self.colors
-            self._mark("sh_fwd")
         else:
             sh_backward = False
         if C > 1:
@@ -221,7 +219,16 @@ class TrainingStep:
                   "isect_count")
             self.total_host.copy_(self.total, non_blocking=True)
             self._mark("isect_count")
-            torch.cuda.current_stream().synchronize()  # the reference's host read of the total
+            counted = torch.cuda.Event()
+            counted.record()
+            if glue_pending:
+                # the SH colours are first needed by the rasterizer: the
+                # device computes them while the host reads the totals
+                check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
+                                       _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
+                self._mark("sh_fwd")
+                glue_pending = False
+            counted.synchronize()  # the reference's host read of the total
             m, bins = (int(v) for v in self.total_host.tolist())
             if m > self.max_isects_per_pass and y1 == 0:
                 # too many intersections for one pass (int32 offsets, memory):
