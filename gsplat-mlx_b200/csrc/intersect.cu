@@ -71,15 +71,30 @@ __global__ void __launch_bounds__(256) count_kernel(int64_t n, const float* __re
                                                     unsigned long long* __restrict__ totals,
                                                     int bins) {
   unsigned long long sum = 0, sum_b = 0;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int2 rad = __ldg(reinterpret_cast<const int2*>(radii) + i);
-    const float2 m = __ldg(reinterpret_cast<const float2*>(means2d) + i);
-    const Rect r = band_rect(m.x, m.y, rad.x, rad.y, ts, tw, th, ty0, ty1);
-    const int c = (r.y1 - r.y0) * (r.x1 - r.x0);
-    tiles_per_gauss[i] = c;
-    sum += (unsigned long long)c;
-    if (bins) sum_b += (unsigned long long)rect_bins(r);
+  // kCountUnroll elements per round, their loads all in flight before the
+  // rect arithmetic (the kernel is bound by load latency, not bandwidth)
+  constexpr int kCountUnroll = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i0 < n;
+       i0 += kCountUnroll * stride) {
+    int2 rad[kCountUnroll];
+    float2 m[kCountUnroll];
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      rad[u] = i < n ? __ldg(reinterpret_cast<const int2*>(radii) + i) : make_int2(0, 0);
+      m[u] = i < n ? __ldg(reinterpret_cast<const float2*>(means2d) + i) : make_float2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kCountUnroll; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i >= n) break;
+      const Rect r = band_rect(m[u].x, m[u].y, rad[u].x, rad[u].y, ts, tw, th, ty0, ty1);
+      const int c = (r.y1 - r.y0) * (r.x1 - r.x0);
+      tiles_per_gauss[i] = c;
+      sum += (unsigned long long)c;
+      if (bins) sum_b += (unsigned long long)rect_bins(r);
+    }
   }
   if (totals) {  // one atomic per CTA and total
     __shared__ unsigned long long s_sum[2][8];
@@ -857,23 +872,25 @@ struct BinArgs {
   const float* depths;
 };
 
-__device__ __forceinline__ Rect element_rect(const BinArgs& a, int64_t i) {
-  const int2 rad = __ldg(reinterpret_cast<const int2*>(a.radii) + i);
-  const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + i);
-  return band_rect(m.x, m.y, rad.x, rad.y, a.ts, a.tw, a.th, a.ty0, a.ty1);
-}
-
 // Block sums of the per-element bin counts (the scan's first half).
 __global__ void __launch_bounds__(kScanThreads) bin_count_kernel(const BinArgs a,
                                                                  int64_t* __restrict__ sums) {
   __shared__ int64_t s_warp[32];
   const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int2 rad[kScanItems];
+  float2 mu[kScanItems];
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {  // all loads in flight first
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    rad[k] = i < a.n ? __ldg(reinterpret_cast<const int2*>(a.radii) + i) : make_int2(0, 0);
+    mu[k] = i < a.n ? __ldg(reinterpret_cast<const float2*>(a.means2d) + i)
+                    : make_float2(0.0f, 0.0f);
+  }
   int64_t acc = 0;
 #pragma unroll
-  for (int k = 0; k < kScanItems; ++k) {
-    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
-    if (i < a.n) acc += rect_bins(element_rect(a, i));
-  }
+  for (int k = 0; k < kScanItems; ++k)
+    acc += rect_bins(band_rect(mu[k].x, mu[k].y, rad[k].x, rad[k].y, a.ts, a.tw, a.th, a.ty0,
+                               a.ty1));
   int64_t total;
   block_exclusive_scan<kScanThreads>(acc, s_warp, &total);
   if (threadIdx.x == 0) sums[blockIdx.x] = total;
