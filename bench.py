@@ -198,9 +198,9 @@ def bin_count(cameras, tw, th):
 
 
 def bin_sort_passes(cameras, tw, th):
-    """Radix passes of the binned encode's entry sort: 32 depth bits plus
-    the bits of the bin ids."""
-    return (32 + (bin_count(cameras, tw, th) - 1).bit_length() + 7) // 8
+    """Radix passes of the binned encode's entry sort: 31 depth bits (the
+    training step's depths are positive) plus the bits of the bin ids."""
+    return (31 + (bin_count(cameras, tw, th) - 1).bit_length() + 7) // 8
 
 
 def our_kernel_launches(entry_passes, bins, slots):

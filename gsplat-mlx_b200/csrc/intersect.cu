@@ -848,7 +848,8 @@ SortedEncodeLayout sorted_encode_layout(int64_t n, int64_t m) {
 // ------------------------------------------------------------ binned encode
 // The tile grid is cut into bins of kBinTiles x kBinTiles tiles.  Every
 // element lists itself once per bin its tile rect touches, as the entry
-// (bin << 32 | depth bits, element); a stable sort of those entries groups
+// (bin << 32 | depth bits, element) -- bin << 31 when the caller promises
+// positive depths, one key bit fewer; a stable sort of those entries groups
 // them by bin, in depth-bit order and, for equal depth bits, in element
 // order.  One CTA per tile then walks its bin's list and keeps the elements
 // whose rect covers the tile: its intersections, already in the order of
@@ -867,6 +868,7 @@ struct BinArgs {
   int64_t n;  // elements I*N
   int n_per_image, ts, tw, th, ty0, ty1;
   int sw, n_bins_per_image;  // bins per row, bins per image
+  int dbits;                 // depth bits in the entry key: 32, or 31 (sign bit clear)
   const float* means2d;
   const int32_t* radii;
   const float* depths;
@@ -938,7 +940,7 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
         const int bx0 = q.x0 / kBinTiles, by0 = q.y0 / kBinTiles;
         s_bw[warp][lane] = (q.x1 - 1) / kBinTiles - bx0 + 1;
         s_bin0[warp][lane] = image * a.n_bins_per_image + (int64_t)by0 * a.sw + bx0;
-        s_low[warp][lane] = __float_as_uint(__ldg(a.depths + i));
+        s_low[warp][lane] = __float_as_uint(__ldg(a.depths + i)) & (0xFFFFFFFFu >> (32 - a.dbits));
       }
     }
     int64_t tot;
@@ -966,7 +968,7 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
         const int64_t bin = s_bin0[warp][o] + (int64_t)dy * a.sw + (k - dy * bw);
         const int64_t pos = wpos + j;
         if (pos >= 0 && pos < n_entries) {
-          keys[pos] = ((uint64_t)bin << 32) | s_low[warp][o];
+          keys[pos] = ((uint64_t)bin << a.dbits) | s_low[warp][o];
           vals[pos] = (int32_t)(base + (int64_t)round * kScanThreads + warp * 32 + o);
         }
       }
@@ -980,7 +982,7 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
 // (bins without entries point at the next one; bin_start[n_bins] =
 // n_entries), and the rect of every entry next to it (an empty rect for an
 // element id outside [0, n), which only a wrong entry total can leave).
-__global__ void __launch_bounds__(256) bin_finish_kernel(int64_t n_entries, int64_t n,
+__global__ void __launch_bounds__(256) bin_finish_kernel(int64_t n_entries, int64_t n, int dbits,
                                                          const uint64_t* __restrict__ keys,
                                                          const int32_t* __restrict__ vals,
                                                          const uint2* __restrict__ rects,
@@ -989,8 +991,8 @@ __global__ void __launch_bounds__(256) bin_finish_kernel(int64_t n_entries, int6
                                                          uint2* __restrict__ sorted_rects) {
   for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n_entries;
        p += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = (int64_t)(__ldg(keys + p) >> 32);
-    const int64_t bp = p > 0 ? (int64_t)(__ldg(keys + p - 1) >> 32) : -1;
+    const int64_t b = (int64_t)(__ldg(keys + p) >> dbits);
+    const int64_t bp = p > 0 ? (int64_t)(__ldg(keys + p - 1) >> dbits) : -1;
     for (int64_t q = bp + 1; q <= b && q <= n_bins; ++q) bin_start[q] = (int32_t)p;
     if (p == n_entries - 1)
       for (int64_t q = b + 1; q <= n_bins; ++q) bin_start[q] = (int32_t)n_entries;
@@ -1048,7 +1050,7 @@ __device__ __forceinline__ void spread16(uint32_t m, uint64_t f[4]) {
 
 struct ItemArgs {
   int64_t n_bins, per_image;
-  int sw, tw, ty0, rows;
+  int sw, tw, ty0, rows, dbits;
   const int32_t* bin_start;
   const int32_t* chunk_prefix;  // exclusive prefix of the bins' item counts
   const int64_t* n_items;       // device total of items
@@ -1207,7 +1209,7 @@ __global__ void __launch_bounds__(kItemThreads) item_write_kernel(
     spread16(m, f);
     block_scan_packed(f, pre, s_w, s_tot);  // the first also orders s_base / s_tile
     if (m) {
-      const uint64_t low = __ldg(keys + p) & 0xFFFFFFFFull;
+      const uint64_t low = __ldg(keys + p) & ((1ull << a.dbits) - 1ull);
       const int32_t e = __ldg(vals + p);
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
@@ -1626,8 +1628,11 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
   auto V = [&](size_t off) { return reinterpret_cast<int32_t*>(ws + off); };
   auto R = [&](size_t off) { return reinterpret_cast<uint2*>(ws + off); };
   cudaMemsetAsync(ws + L.sort + sort_layout(1).err, 0, sizeof(uint32_t), s);
+  // with positive depths the key's depth field drops the (clear) sign bit:
+  // 31 + bin bits, one radix pass fewer when that crosses a multiple of 8
+  const int dbits = p->positive_depths ? 31 : 32;
   BinArgs a{n, p->N, p->tile_size, p->tile_width, p->tile_height, ty0, ty1,
-            g.sw, (int)g.per_image, means2d, radii, depths};
+            g.sw, (int)g.per_image, dbits, means2d, radii, depths};
   const int64_t nb = ceil_div(n, kScanChunk);
   const size_t scan_bytes = L.total - L.scan;
   int64_t* sums = reinterpret_cast<int64_t*>(ws + L.scan);
@@ -1636,11 +1641,12 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
   bin_emit_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(a, sums, n_bin_entries, K(L.keys),
                                                         V(L.vals), R(L.rects));
   if (n_bin_entries > 0) {
-    // the depth bits are the low key word and bin ids are unsigned
-    sort_passes(n_bin_entries, 0, 32 + g.bits, kKV, kKV, K(L.keys), V(L.vals), K(L.skeys),
+    // the depth bits are the low key field and bin ids are unsigned
+    sort_passes(n_bin_entries, 0, dbits + g.bits, kKV, kKV, K(L.keys), V(L.vals), K(L.skeys),
                 V(L.svals), ws + L.sort, s, false, nullptr, nullptr, /*signed_keys=*/false);
     bin_finish_kernel<<<grid_for(n_bin_entries, 256), 256, 0, s>>>(
-        n_bin_entries, n, K(L.skeys), V(L.svals), R(L.rects), g.total, V(L.bstart), R(L.srects));
+        n_bin_entries, n, dbits, K(L.skeys), V(L.svals), R(L.rects), g.total, V(L.bstart),
+        R(L.srects));
   } else {
     cudaMemsetAsync(ws + L.bstart, 0, 4 * (size_t)(g.total + 1), s);
   }
@@ -1649,7 +1655,7 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
   int64_t* n_items = reinterpret_cast<int64_t*>(ws + L.nitems);
   if (int rc = scan_i32(g.total, V(L.chunks), V(L.cprefix), n_items, ws + L.scan, scan_bytes, s))
     return rc;
-  ItemArgs ia{g.total, g.per_image, g.sw, p->tile_width, ty0, rows,
+  ItemArgs ia{g.total, g.per_image, g.sw, p->tile_width, ty0, rows, dbits,
               V(L.bstart), V(L.cprefix), n_items, R(L.srects)};
   item_count_kernel<<<(unsigned)L.items, kItemThreads, 0, s>>>(ia, V(L.icounts));
   int32_t* offs = tile_offsets ? tile_offsets : V(L.offs);

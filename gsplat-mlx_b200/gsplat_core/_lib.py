@@ -67,7 +67,7 @@ class AdamParams(ct.Structure):
 class IsectParams(ct.Structure):
     _fields_ = [("I", _i32), ("N", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32), ("tile_y0", _i32), ("tile_y1", _i32),
-                ("reuse_depth_order", _i32)]
+                ("reuse_depth_order", _i32), ("positive_depths", _i32)]
 
 
 class RasterParams(ct.Structure):

@@ -214,6 +214,9 @@ class TrainingStep:
         while b < len(bands):
             y0, y1 = bands[b]
             ip = IsectParams(C, N, self.ts, self.tw, self.th, y0, y1)
+            # the projection culls depths below its near plane: with a
+            # positive near plane every visible depth is positive
+            ip.positive_depths = int(self.near > 0.0)
             check(L.gs_isect_tile_count_totals(ct.byref(ip), _p(self.means2d), _p(self.radii),
                                                _p(self.tiles_per_gauss), _p(self.total), s),
                   "isect_count")

@@ -175,6 +175,13 @@ typedef struct {
                                 call with the same I, N, radii and depths (the
                                 other bands of a step); its element sort is
                                 skipped */
+  int32_t positive_depths;   /* gs_isect_tile_encode_binned: 1 = the caller
+                                promises that every element with positive
+                                radii has a depth with the sign bit clear
+                                (a projection with near_plane > 0 gives
+                                that); the sort then carries 31 depth bits,
+                                one key bit fewer.  Same output; a broken
+                                promise misorders, it does not fault. */
 } gs_isect_params;
 
 /* tiles_per_gauss [I,N] int32 */

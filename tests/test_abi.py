@@ -54,7 +54,7 @@ def test_param_struct_layouts(gs):
     assert ct.sizeof(L.ProjectionParams) == 52
     assert ct.sizeof(L.SHParams) == 24
     assert ct.sizeof(L.SHGlueParams) == 24
-    assert ct.sizeof(L.IsectParams) == 32
+    assert ct.sizeof(L.IsectParams) == 36
     assert ct.sizeof(L.RasterParams) == 64
     assert ct.sizeof(L.DensifyParams) == 20
     assert ct.sizeof(L.DensifyMaskParams) == 96

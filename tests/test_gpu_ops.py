@@ -463,6 +463,19 @@ def test_intersect_binned_offsets_bands_and_fallback(gs, oracle, cuda):
     assert_exact(oid, bid, "band isect_ids")
     assert_exact(ofid, bfid, "band flatten_ids")
     assert_exact(ob.reshape(-1), bofs, "band tile offsets")
+    # the caller's promise of positive depths (31-bit depth field in the
+    # entry keys) gives the same lists
+    q = IsectParams(I, N, ts, tw, th, 0, 0, 0, 1)
+    assert lib.gs_isect_tile_count_totals(ct.byref(q), P(dm2), P(drad), P(tpg_b), P(tot), s) == 0
+    mq, binsq = (int(v) for v in tot.tolist())
+    qid = torch.empty(mq, dtype=torch.int64, device="cuda")
+    qfid = torch.empty(mq, dtype=torch.int32, device="cuda")
+    ws = torch.empty(lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(q), binsq),
+                     dtype=torch.uint8, device="cuda")
+    assert lib.gs_isect_tile_encode_binned(ct.byref(q), P(dm2), P(drad), P(ddep), mq, binsq,
+                                           P(qid), P(qfid), None, P(ws), ws.numel(), s) == 0
+    assert_exact(qid, e["isect_ids"], "positive-depth isect_ids")
+    assert_exact(qfid, e["flatten_ids"], "positive-depth flatten_ids")
 
 
 def test_sort_error_words_clear(gs, cuda):
