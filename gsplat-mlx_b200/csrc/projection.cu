@@ -351,6 +351,105 @@ __device__ __forceinline__ void qs_covar_vjp(const float q[4], const float s[3],
   vq[3] += (vn[3] - dot * z) * inv;
 }
 
+// Gradient terms of one visible (camera, Gaussian) entry: adds the
+// world-mean and world-covariance VJPs of the projection to vmw and vcw_tot
+// and, with want_view, writes the entry's 12 view-matrix terms to vR.
+__device__ __forceinline__ void entry_vjp(const BwdArgs& a, int64_t bc, int64_t idx,
+                                          const float mw[3], const M3& cw, bool want_view,
+                                          float vmw[3], M3& vcw_tot, float vR[12]) {
+    const Cam cam = load_cam(a.viewmats + bc * 16, a.Ks + bc * 9);
+    const float ci[4] = {__ldg(a.conics + idx * 3), __ldg(a.conics + idx * 3 + 1),
+                         __ldg(a.conics + idx * 3 + 1), __ldg(a.conics + idx * 3 + 2)};
+    const float vco1 = 0.5f * __ldg(a.v_conics + idx * 3 + 1);
+    const float vci[4] = {__ldg(a.v_conics + idx * 3), vco1, vco1, __ldg(a.v_conics + idx * 3 + 2)};
+    const float t0[4] = {ci[0] * vci[0] + ci[1] * vci[2], ci[0] * vci[1] + ci[1] * vci[3],
+                         ci[2] * vci[0] + ci[3] * vci[2], ci[2] * vci[1] + ci[3] * vci[3]};
+    float vc2[4] = {-(t0[0] * ci[0] + t0[1] * ci[2]), -(t0[0] * ci[1] + t0[1] * ci[3]),
+                    -(t0[2] * ci[0] + t0[3] * ci[2]), -(t0[2] * ci[1] + t0[3] * ci[3])};
+    if (a.calc_comp && a.v_comps) {
+      // gsplat_projection.cpp:277-296
+      const float comp = __ldg(a.comps + idx);
+      const float det = ci[0] * ci[3] - ci[1] * ci[2];
+      const float v_sqr = __ldg(a.v_comps + idx) * 0.5f / (comp + 1.0e-6f);
+      const float om = 1.0f - comp * comp;
+      vc2[0] += v_sqr * (om * ci[0] - a.eps2d * det);
+      vc2[1] += v_sqr * (om * ci[1]);
+      vc2[2] += v_sqr * (om * ci[2]);
+      vc2[3] += v_sqr * (om * ci[3] - a.eps2d * det);
+    }
+    const M3& R = cam.R;
+    const float mc[3] = {R.v[0] * mw[0] + R.v[1] * mw[1] + R.v[2] * mw[2] + cam.t[0],
+                         R.v[3] * mw[0] + R.v[4] * mw[1] + R.v[5] * mw[2] + cam.t[1],
+                         R.v[6] * mw[0] + R.v[7] * mw[1] + R.v[8] * mw[2] + cam.t[2]};
+    const M3 cc = mul(mul(R, cw), tr(R));
+    float vmc[3] = {0.0f, 0.0f, __ldg(a.v_depths + idx)};
+    M3 vcc;
+    persp_vjp(mc, cc, cam, a.W, a.H, vc2, __ldg(a.v_means2d + idx * 2),
+              __ldg(a.v_means2d + idx * 2 + 1), vmc, vcc);
+    // pos_w2c_vjp / covar_w2c_vjp, gsplat_projection.cpp:378-408
+    vmw[0] += R.v[0] * vmc[0] + R.v[3] * vmc[1] + R.v[6] * vmc[2];
+    vmw[1] += R.v[1] * vmc[0] + R.v[4] * vmc[1] + R.v[7] * vmc[2];
+    vmw[2] += R.v[2] * vmc[0] + R.v[5] * vmc[1] + R.v[8] * vmc[2];
+    const M3 Rt = tr(R);
+    const M3 vcw = mul(mul(Rt, vcc), R);
+#pragma unroll
+    for (int i = 0; i < 9; ++i) vcw_tot.v[i] += vcw.v[i];
+    if (want_view) {
+      const M3 term1 = mul(mul(vcc, R), tr(cw));
+      const M3 term2 = mul(mul(tr(vcc), R), cw);
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+#pragma unroll
+        for (int cc2 = 0; cc2 < 3; ++cc2)
+          vR[r * 3 + cc2] = vmc[r] * mw[cc2] + term1.v[r * 3 + cc2] + term2.v[r * 3 + cc2];
+        vR[9 + r] = vmc[r];
+      }
+    }
+}
+
+// A Gaussian's world mean and covariance (given, or from quats and scales).
+__device__ __forceinline__ void load_gauss(const BwdArgs& a, int64_t g, float mw[3], float q[4],
+                                           float s[3], M3& cw) {
+  mw[0] = __ldg(a.means + g * 3);
+  mw[1] = __ldg(a.means + g * 3 + 1);
+  mw[2] = __ldg(a.means + g * 3 + 2);
+  if (a.use_covars) {
+    cw = covar6(a.covars + g * 6);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = __ldg(a.quats + g * 4 + i);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) s[i] = __ldg(a.scales + g * 3 + i);
+    cw = covar_qs(q, s);
+  }
+}
+
+// A Gaussian's gradients, summed over its cameras: v_means and v_covars, or
+// v_quats and v_scales through the covariance VJP.
+__device__ __forceinline__ void store_gauss(const BwdArgs& a, int64_t g, const float q[4],
+                                            const float s[3], const float vmw[3],
+                                            const M3& vcw_tot) {
+  a.v_means[g * 3] = vmw[0];
+  a.v_means[g * 3 + 1] = vmw[1];
+  a.v_means[g * 3 + 2] = vmw[2];
+  if (a.use_covars) {
+    float* o = a.v_covars + g * 6;
+    o[0] = vcw_tot.v[0];
+    o[1] = vcw_tot.v[1] + vcw_tot.v[3];
+    o[2] = vcw_tot.v[2] + vcw_tot.v[6];
+    o[3] = vcw_tot.v[4];
+    o[4] = vcw_tot.v[5] + vcw_tot.v[7];
+    o[5] = vcw_tot.v[8];
+  } else {
+    float vq[4] = {0.f, 0.f, 0.f, 0.f}, vs[3] = {0.f, 0.f, 0.f};
+    qs_covar_vjp(q, s, vcw_tot, vq, vs);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a.v_quats[g * 4 + i] = vq[i];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) a.v_scales[g * 3 + i] = vs[i];
+  }
+}
+
 // Dynamic shared memory: per-camera v_viewmats partial sums [C][12].
 __global__ void __launch_bounds__(256) proj_bwd_kernel(BwdArgs a, int smem_cams) {
   extern __shared__ float s_vview[];
@@ -374,20 +473,7 @@ __global__ void __launch_bounds__(256) proj_bwd_kernel(BwdArgs a, int smem_cams)
     const int64_t g = b * a.N + n;
     float mw[3] = {0.f, 0.f, 0.f}, q[4] = {1.f, 0.f, 0.f, 0.f}, s[3] = {1.f, 1.f, 1.f};
     M3 cw = {};
-    if (live) {
-      mw[0] = __ldg(a.means + g * 3);
-      mw[1] = __ldg(a.means + g * 3 + 1);
-      mw[2] = __ldg(a.means + g * 3 + 2);
-      if (a.use_covars) {
-        cw = covar6(a.covars + g * 6);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) q[i] = __ldg(a.quats + g * 4 + i);
-#pragma unroll
-        for (int i = 0; i < 3; ++i) s[i] = __ldg(a.scales + g * 3 + i);
-        cw = covar_qs(q, s);
-      }
-    }
+    if (live) load_gauss(a, g, mw, q, s, cw);
     float vmw[3] = {0.f, 0.f, 0.f};
     M3 vcw_tot = {};
     for (int c = 0; c < a.C; ++c) {
@@ -397,56 +483,7 @@ __global__ void __launch_bounds__(256) proj_bwd_kernel(BwdArgs a, int smem_cams)
       float vR[12];
 #pragma unroll
       for (int i = 0; i < 12; ++i) vR[i] = 0.0f;
-      if (act) {
-        const Cam cam = load_cam(a.viewmats + bc * 16, a.Ks + bc * 9);
-        const float ci[4] = {__ldg(a.conics + idx * 3), __ldg(a.conics + idx * 3 + 1),
-                             __ldg(a.conics + idx * 3 + 1), __ldg(a.conics + idx * 3 + 2)};
-        const float vco1 = 0.5f * __ldg(a.v_conics + idx * 3 + 1);
-        const float vci[4] = {__ldg(a.v_conics + idx * 3), vco1, vco1, __ldg(a.v_conics + idx * 3 + 2)};
-        const float t0[4] = {ci[0] * vci[0] + ci[1] * vci[2], ci[0] * vci[1] + ci[1] * vci[3],
-                             ci[2] * vci[0] + ci[3] * vci[2], ci[2] * vci[1] + ci[3] * vci[3]};
-        float vc2[4] = {-(t0[0] * ci[0] + t0[1] * ci[2]), -(t0[0] * ci[1] + t0[1] * ci[3]),
-                        -(t0[2] * ci[0] + t0[3] * ci[2]), -(t0[2] * ci[1] + t0[3] * ci[3])};
-        if (a.calc_comp && a.v_comps) {
-          // gsplat_projection.cpp:277-296
-          const float comp = __ldg(a.comps + idx);
-          const float det = ci[0] * ci[3] - ci[1] * ci[2];
-          const float v_sqr = __ldg(a.v_comps + idx) * 0.5f / (comp + 1.0e-6f);
-          const float om = 1.0f - comp * comp;
-          vc2[0] += v_sqr * (om * ci[0] - a.eps2d * det);
-          vc2[1] += v_sqr * (om * ci[1]);
-          vc2[2] += v_sqr * (om * ci[2]);
-          vc2[3] += v_sqr * (om * ci[3] - a.eps2d * det);
-        }
-        const M3& R = cam.R;
-        const float mc[3] = {R.v[0] * mw[0] + R.v[1] * mw[1] + R.v[2] * mw[2] + cam.t[0],
-                             R.v[3] * mw[0] + R.v[4] * mw[1] + R.v[5] * mw[2] + cam.t[1],
-                             R.v[6] * mw[0] + R.v[7] * mw[1] + R.v[8] * mw[2] + cam.t[2]};
-        const M3 cc = mul(mul(R, cw), tr(R));
-        float vmc[3] = {0.0f, 0.0f, __ldg(a.v_depths + idx)};
-        M3 vcc;
-        persp_vjp(mc, cc, cam, a.W, a.H, vc2, __ldg(a.v_means2d + idx * 2),
-                  __ldg(a.v_means2d + idx * 2 + 1), vmc, vcc);
-        // pos_w2c_vjp / covar_w2c_vjp, gsplat_projection.cpp:378-408
-        vmw[0] += R.v[0] * vmc[0] + R.v[3] * vmc[1] + R.v[6] * vmc[2];
-        vmw[1] += R.v[1] * vmc[0] + R.v[4] * vmc[1] + R.v[7] * vmc[2];
-        vmw[2] += R.v[2] * vmc[0] + R.v[5] * vmc[1] + R.v[8] * vmc[2];
-        const M3 Rt = tr(R);
-        const M3 vcw = mul(mul(Rt, vcc), R);
-#pragma unroll
-        for (int i = 0; i < 9; ++i) vcw_tot.v[i] += vcw.v[i];
-        if (want_view) {
-          const M3 term1 = mul(mul(vcc, R), tr(cw));
-          const M3 term2 = mul(mul(tr(vcc), R), cw);
-#pragma unroll
-          for (int r = 0; r < 3; ++r) {
-#pragma unroll
-            for (int cc2 = 0; cc2 < 3; ++cc2)
-              vR[r * 3 + cc2] = vmc[r] * mw[cc2] + term1.v[r * 3 + cc2] + term2.v[r * 3 + cc2];
-            vR[9 + r] = vmc[r];
-          }
-        }
-      }
+      if (act) entry_vjp(a, bc, idx, mw, cw, want_view, vmw, vcw_tot, vR);
       if (want_view && a.B > 1) {
         // Lanes of one warp may belong to different batches: no warp sum.
         if (act) {
@@ -480,27 +517,7 @@ __global__ void __launch_bounds__(256) proj_bwd_kernel(BwdArgs a, int smem_cams)
         }
       }
     }
-    if (live) {
-      a.v_means[g * 3] = vmw[0];
-      a.v_means[g * 3 + 1] = vmw[1];
-      a.v_means[g * 3 + 2] = vmw[2];
-      if (a.use_covars) {
-        float* o = a.v_covars + g * 6;
-        o[0] = vcw_tot.v[0];
-        o[1] = vcw_tot.v[1] + vcw_tot.v[3];
-        o[2] = vcw_tot.v[2] + vcw_tot.v[6];
-        o[3] = vcw_tot.v[4];
-        o[4] = vcw_tot.v[5] + vcw_tot.v[7];
-        o[5] = vcw_tot.v[8];
-      } else {
-        float vq[4] = {0.f, 0.f, 0.f, 0.f}, vs[3] = {0.f, 0.f, 0.f};
-        qs_covar_vjp(q, s, vcw_tot, vq, vs);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) a.v_quats[g * 4 + i] = vq[i];
-#pragma unroll
-        for (int i = 0; i < 3; ++i) a.v_scales[g * 3 + i] = vs[i];
-      }
-    }
+    if (live) store_gauss(a, g, q, s, vmw, vcw_tot);
   }
   if (use_smem) {
     __syncthreads();
@@ -514,6 +531,74 @@ __global__ void __launch_bounds__(256) proj_bwd_kernel(BwdArgs a, int smem_cams)
       if (v != 0.0f) atomicAdd(a.v_viewmats + (int64_t)c * 16 + r * 4 + col, v);
     }
   }
+}
+
+// The form without v_viewmats (the training step's): each warp walks chunks
+// of 32 Gaussians; those no camera sees get zero gradients at once, the
+// others go to a per-warp queue in shared memory and are processed 32 at a
+// time, one per lane, so that the per-camera VJPs and the covariance VJP run
+// on full warps (about a third of the Gaussians are visible in a training
+// view).  Same arithmetic per Gaussian as proj_bwd_kernel.
+constexpr int kProjBwdWarps = 4;
+
+__device__ __forceinline__ void proj_bwd_one(const BwdArgs& a, int64_t g) {
+  const int64_t b = g / a.N, n = g - b * a.N;
+  float mw[3], q[4] = {1.f, 0.f, 0.f, 0.f}, s[3] = {1.f, 1.f, 1.f};
+  M3 cw;
+  load_gauss(a, g, mw, q, s, cw);
+  float vmw[3] = {0.f, 0.f, 0.f};
+  M3 vcw_tot = {};
+  float vR[12];
+  for (int c = 0; c < a.C; ++c) {
+    const int64_t bc = b * a.C + c;
+    const int64_t idx = bc * a.N + n;
+    if (__ldg(a.radii + idx * 2) > 0 && __ldg(a.radii + idx * 2 + 1) > 0)
+      entry_vjp(a, bc, idx, mw, cw, false, vmw, vcw_tot, vR);
+  }
+  store_gauss(a, g, q, s, vmw, vcw_tot);
+}
+
+__global__ void __launch_bounds__(32 * kProjBwdWarps) proj_bwd_queue_kernel(BwdArgs a) {
+  __shared__ int64_t s_q[kProjBwdWarps][64];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t* qu = s_q[warp];
+  int qn = 0;  // queued entries, < 32 between chunks
+  const int64_t total = (int64_t)a.B * a.N;
+  const int64_t chunks = (total + 31) / 32;
+  for (int64_t ch = (int64_t)blockIdx.x * kProjBwdWarps + warp; ch < chunks;
+       ch += (int64_t)gridDim.x * kProjBwdWarps) {
+    const int64_t g = ch * 32 + lane;
+    bool any = false;
+    if (g < total) {
+      const int64_t b = g / a.N, n = g - b * a.N;
+      for (int c = 0; c < a.C; ++c) {
+        const int64_t idx = (b * a.C + c) * a.N + n;
+        any |= __ldg(a.radii + idx * 2) > 0 && __ldg(a.radii + idx * 2 + 1) > 0;
+      }
+      if (!any) {  // no camera sees it: every gradient is zero
+        a.v_means[g * 3] = a.v_means[g * 3 + 1] = a.v_means[g * 3 + 2] = 0.0f;
+        if (a.use_covars) {
+#pragma unroll
+          for (int i = 0; i < 6; ++i) a.v_covars[g * 6 + i] = 0.0f;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a.v_quats[g * 4 + i] = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) a.v_scales[g * 3 + i] = 0.0f;
+        }
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, any);
+    if (any) qu[qn + __popc(bal & ((1u << lane) - 1u))] = g;
+    qn += __popc(bal);
+    __syncwarp();
+    if (qn >= 32) {
+      proj_bwd_one(a, qu[qn - 32 + lane]);
+      qn -= 32;
+      __syncwarp();
+    }
+  }
+  if (lane < qn) proj_bwd_one(a, qu[lane]);
 }
 
 }  // namespace
@@ -581,6 +666,11 @@ extern "C" int gs_projection_bwd(const gs_projection_params* p, const float* mea
   const size_t smem = sizeof(float) * 12 * (size_t)smem_cams;
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(proj_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }
+  if (!v_viewmats) {
+    proj_bwd_queue_kernel<<<grid_for(ceil_div(total, 32), kProjBwdWarps, 4),
+                            32 * kProjBwdWarps, 0, s>>>(a);
+    return launch_status("projection_bwd");
   }
   proj_bwd_kernel<<<grid_for(total, 256, 4), 256, smem, s>>>(a, smem_cams);
   return launch_status("projection_bwd");
