@@ -169,10 +169,13 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ helpers
 
-def algorithmic_bytes(stage, n, visible, m, pixels, K, slots):
+def algorithmic_bytes(stage, n, visible, m, pixels, K, slots, kept=None):
     """Bytes each stage must move at minimum (the roofline convention):
     what it reads once and writes once, not what an implementation's
-    intermediate passes move.  ``slots``: tile offsets written."""
+    intermediate passes move.  ``slots``: tile offsets written; ``kept``:
+    the intersections left after the encode's tile culling (the lists the
+    rasterizers walk), else m."""
+    mk = m if kept is None else kept
     return {
         # means/quats/scales in (40 B), 2D outputs out (36 B) per Gaussian
         "projection_fwd": n * (40 + 36),
@@ -182,11 +185,11 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, slots):
         "isect_count": n * (16 + 4),
         # means2d, radii, depths in; sorted keys + flatten ids and the tile
         # offsets out (the binned encode writes the offsets itself)
-        "isect_encode_sort": n * (8 + 8 + 4) + m * 12 + slots * 4,
+        "isect_encode_sort": n * (8 + 8 + 4) + mk * 12 + slots * 4,
         "isect_offset": m * 8,
         # per intersection: flatten id + Gaussian record; per pixel: outputs
-        "rasterize_fwd": m * 40 + pixels * 20,
-        "rasterize_bwd": m * (40 + 36) + pixels * 20,
+        "rasterize_fwd": mk * 40 + pixels * 20,
+        "rasterize_bwd": mk * (40 + 36) + pixels * 20,
         "projection_bwd": n * (8 + 12 + 8 + 4 + 12) + n * (40 + 40),
         "sh_bwd": n * (12 + 12 + 12) + visible * K * 12 + n * K * 12,
     }[stage]
@@ -203,15 +206,16 @@ def bin_sort_passes(cameras, tw, th):
     return (31 + (bin_count(cameras, tw, th) - 1).bit_length() + 7) // 8
 
 
-def our_kernel_launches(entry_passes, bins, slots):
+def our_kernel_launches(entry_passes, bins, slots, tile_cull=False):
     # projection fwd 1, glue fwd 1, count (+ totals) 1; binned encode: bin
     # counts 1, their scan 1, entry emit 1, digit histogram 1, entry passes,
-    # bin starts + rects 1, item counts per bin 1 and their scan, item count
-    # phase 1, slot counts 1 and their scan, item write phase 1 (a scan is
-    # one launch up to 16384 values, else 3); rasterize fwd 1, rasterize
-    # bwd 1, projection bwd 1, glue bwd 1
+    # bin starts + tile masks 1, item counts per bin 1 and their scan, item
+    # count phase 1, slot counts 1 and their scan, (tile culling: the offsets'
+    # gap 1), item write phase 1 (a scan is one launch up to 16384 values,
+    # else 3); rasterize fwd 1, rasterize bwd 1, projection bwd 1, glue bwd 1
     scan = lambda n: 1 if n <= 16384 else 3  # noqa: E731
-    binned = 3 + 1 + entry_passes + 1 + 1 + scan(bins) + 1 + 1 + scan(slots) + 1
+    binned = (3 + 1 + entry_passes + 1 + 1 + scan(bins) + 1 + 1 + scan(slots) + int(tile_cull)
+              + 1)
     return 1 + 1 + 1 + binned + 1 + 1 + 1 + 1
 
 
@@ -414,7 +418,8 @@ def run_ours(args):
     d = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in host.items()}
     pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in host.items()}
     sharded = ShardedTrainingStep(sc.n, sc.sh_degree, sc.coeffs.shape[1], C_total, sc.width,
-                                  sc.height, exchange=args.exchange, device=dev)
+                                  sc.height, exchange=args.exchange, device=dev,
+                                  tile_cull=args.tile_cull)
     step = sharded.step
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
@@ -543,7 +548,8 @@ def run_ours(args):
         # this rank's units: (camera, Gaussian) elements and pixels
         n_el, pix_local = sc.n * sharded.C, sc.width * sc.height * sharded.C
         vis_b = visible
-        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, slots)
+        kept = step.kept_isects() if step.bands == 1 else None
+        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, slots, kept)
         achieved = bytes_top / (avg[top] / 1e3) / 1e9
         stages = {}
         for k, v in avg.items():
@@ -555,7 +561,7 @@ def run_ours(args):
                              "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
                              "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
                 continue
-            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, slots)
+            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, slots, kept)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
         cpu = None
@@ -576,6 +582,8 @@ def run_ours(args):
             "data": f"synthetic (seeded, BASELINE {args.workload} distributions)",
             "config": {"workload": desc, "cameras": C_total,
                        "gaussians": sc.n, "visible": visible, "isects": m,
+                       # after the encode's opacity-aware tile culling
+                       "isects_kept": kept, "tile_cull": step.tile_cull,
                        # (per band when the step renders bands of tile rows)
                        "bwd_pixel_gaussian_pairs": (composited_pairs(step) if step.bands == 1
                                                     else None),
@@ -597,7 +605,8 @@ def run_ours(args):
                            "from pinned host memory; copies double-buffered on their own "
                            "streams, overlapping the neighbouring steps' kernels"},
             "gpu_launches": our_kernel_launches(
-                passes, bin_count(sharded.C, sc.tile_width, sc.tile_height), slots) * args.steps,
+                passes, bin_count(sharded.C, sc.tile_width, sc.tile_height), slots,
+                step.tile_cull) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(out), flush=True)
@@ -621,6 +630,9 @@ def main():
                          "per-config records)")
     ap.add_argument("--exchange", choices=["auto", "allreduce", "gather"], default="auto",
                     help="gradient exchange of the camera-sharded step (N > 1)")
+    ap.add_argument("--tile-cull", action="store_true",
+                    help="opacity-aware tile culling in the encode (the renders are the "
+                         "same either way; the reference lists every pair of the rects)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -57,4 +57,42 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Can the Gaussian reach alpha >= 1/255 at any pixel centre of the tile
+// whose first pixel centre is (x0, y0) and whose last is span pixels further
+// on each axis (15 for a 16x16 tile)?
+// sigma(d) = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy is convex for a positive
+// definite conic, so its minimum over the box of pixel-centre offsets
+// [mx - x0 - span, mx - x0] x [my - y0 - span, my - y0] is 0 when the mean lies
+// inside, else on an edge, where it is a 1-D quadratic minimised in closed
+// form and clamped.  A Gaussian is dropped only when even that minimum
+// leaves o exp(-sigma) below the threshold by a margin that covers the fp32
+// rounding of the per-pixel sigma and of __expf; such a Gaussian would be
+// skipped by every pixel of the tile (alpha < 1/255), so dropping it
+// changes no output bit.  Conics that are not positive definite are kept.
+__device__ __forceinline__ bool tile_may_hit(float mx, float my, float c0, float c1, float c2,
+                                             float o, float x0, float y0,
+                                             float span = 15.0f) {
+  if (!(c0 > 0.0f && c2 > 0.0f && c0 * c2 - c1 * c1 > 0.0f)) return true;
+  const float dxl = mx - (x0 + span), dxh = mx - x0;
+  const float dyl = my - (y0 + span), dyh = my - y0;
+  float best = 0.0f;
+  if (!(dxl <= 0.0f && dxh >= 0.0f && dyl <= 0.0f && dyh >= 0.0f)) {
+    const float ry = -c1 / c2, rx = -c1 / c0;
+    best = INFINITY;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float X = e ? dxh : dxl;
+      const float Y = fminf(fmaxf(ry * X, dyl), dyh);
+      best = fminf(best, 0.5f * (c0 * X * X + c2 * Y * Y) + c1 * X * Y);
+      const float Y2 = e ? dyh : dyl;
+      const float X2 = fminf(fmaxf(rx * Y2, dxl), dxh);
+      best = fminf(best, 0.5f * (c0 * X2 * X2 + c2 * Y2 * Y2) + c1 * X2 * Y2);
+    }
+  }
+  const float xm = fmaxf(fabsf(dxl), fabsf(dxh)), ym = fmaxf(fabsf(dyl), fabsf(dyh));
+  const float mag = 0.5f * (c0 * xm * xm + c2 * ym * ym) + fabsf(c1) * xm * ym;
+  const float margin = 1.0e-5f * mag + 1.0e-5f;
+  return o * __expf(-(best - margin)) >= (1.0f / 255.0f) * 0.998f;
+}
+
 }  // namespace gsb

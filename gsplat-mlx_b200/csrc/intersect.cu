@@ -864,6 +864,88 @@ __device__ __forceinline__ uint2 pack_rect(const Rect& r) {
   return make_uint2((uint32_t)r.x0 | ((uint32_t)r.x1 << 16), (uint32_t)r.y0 | ((uint32_t)r.y1 << 16));
 }
 
+// Tiles of a bin an entry's rect covers: bit 4j+i for tile (bx*4+i, by*4+j).
+__device__ __forceinline__ uint32_t cover_mask(uint2 r, int tx0, int ty0_) {
+  const int x0 = (int)(r.x & 0xFFFFu) - tx0, x1 = (int)(r.x >> 16) - tx0;
+  const int y0 = (int)(r.y & 0xFFFFu) - ty0_, y1 = (int)(r.y >> 16) - ty0_;
+  auto span = [](int a0, int a1) -> uint32_t {  // bits [max(a0,0), min(a1,4))
+    const int lo = a0 < 0 ? 0 : (a0 > 4 ? 4 : a0), hi = a1 < 0 ? 0 : (a1 > 4 ? 4 : a1);
+    return hi > lo ? ((1u << hi) - 1u) & ~((1u << lo) - 1u) : 0u;
+  };
+  const uint32_t xm = span(x0, x1), ym = span(y0, y1);
+  uint32_t m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if ((ym >> j) & 1u) m |= xm << (4 * j);
+  return m;
+}
+
+// The tiles of a bin mask (bit 4j+i: tile column i, row j of the bin) that
+// a Gaussian may reach with alpha >= 1/255 at some pixel centre; the others
+// are dropped.  (mx, my) is the mean relative to the bin's first pixel
+// centre; sigma(u, v) = 0.5 (c0 u^2 + c2 v^2) + c1 u v with (u, v) = pixel
+// centre - mean, as the rasterizer evaluates it.
+//
+// A pixel can pass only inside the ellipse sigma <= tau with tau =
+// ln(255 o / 0.998) plus 1e-5 (1 + mag), mag bounding the terms of sigma over
+// the bin (the rasterizer's fp32 sigma is within a few ulp of mag of the
+// exact value, and the 0.998 covers __expf).  Per row of tiles the ellipse's
+// u-range over the row's strip of v is exact: the largest u lies at the
+// clamp of the ellipse's rightmost point into the strip (u_max(v) is
+// concave), the smallest at the clamp of the leftmost; the range is widened
+// by 0.4% of the ellipse's half width + 0.01 px, four times the worst fp32
+// error of the square roots (the determinant is formed with a compensated
+// product; the hardware reciprocal and reciprocal square root, a few ulp,
+// are far inside that widening).  A tile stays when its pixel-centre span
+// meets the row's range.
+// Conics that are not positive definite and NaN opacities keep every tile.
+// sqrt(max(x, 0)) from the hardware reciprocal square root (0 at x <= 0).
+__device__ __forceinline__ float fast_sqrt(float x) {
+  x = fmaxf(x, 0.0f);
+  return x * rsqrtf(fmaxf(x, 1.0e-30f));
+}
+
+__device__ __forceinline__ uint32_t bin_hit_mask(uint32_t m, float mx, float my, float c0,
+                                                 float c1, float c2, float o, int ts) {
+  if (!(c0 > 0.0f && c2 > 0.0f) || o != o) return m;
+  const float pc = c1 * c1;
+  const float det = __fadd_rn(__fmaf_rn(c0, c2, -pc), -__fmaf_rn(c1, c1, -pc));
+  if (!(det > 0.0f)) return m;
+  const float span = (float)(kBinTiles * ts - 1), fts = (float)ts;
+  const float ul = -mx, uh = span - mx, vl = -my, vh = span - my;
+  const float U = fmaxf(fabsf(ul), fabsf(uh)), V = fmaxf(fabsf(vl), fabsf(vh));
+  const float mag = 0.5f * (c0 * U * U + c2 * V * V) + fabsf(c1) * U * V;
+  const float lvl = o * (255.0f / 0.998f);
+  if (!(lvl > 0.0f)) return 0u;  // o <= 0: alpha below the threshold everywhere
+  const float tau = __logf(lvl) + 1.0e-5f * mag + 1.0e-5f;
+  if (!(tau > 0.0f)) return 0u;  // even the centre stays below the threshold
+  const float t2 = 2.0f * tau;
+  const float inv_det = __fdividef(1.0f, det);
+  const float ur = fast_sqrt(t2 * c2 * inv_det);  // half width of the ellipse in u
+  const float ve = fast_sqrt(t2 * c0 * inv_det);  // half height in v
+  const float inv_c0 = __fdividef(1.0f, c0);
+  const float vr = -c1 * ur * __fdividef(1.0f, c2);  // v of the rightmost point
+  const float eps_u = 4.0e-3f * ur + 0.01f, ve_w = ve * 1.004f + 0.01f;
+  const float t2c0 = t2 * c0;
+  uint32_t out = 0u;
+#pragma unroll
+  for (int j = 0; j < kBinTiles; ++j) {
+    const uint32_t row = (m >> (4 * j)) & 0xFu;
+    const float v0 = vl + (float)j * fts, v1 = v0 + (fts - 1.0f);
+    if (!row || v0 > ve_w || v1 < -ve_w) continue;
+    const float lo = fmaxf(v0, -ve), hi = fminf(v1, ve);
+    const float va = fminf(fmaxf(vr, lo), hi), vb = fminf(fmaxf(-vr, lo), hi);
+    const float umax = (-c1 * va + fast_sqrt(t2c0 - det * va * va)) * inv_c0 + eps_u;
+    const float umin = (-c1 * vb - fast_sqrt(t2c0 - det * vb * vb)) * inv_c0 - eps_u;
+#pragma unroll
+    for (int i = 0; i < kBinTiles; ++i) {
+      const float u0 = ul + (float)i * fts, u1 = u0 + (fts - 1.0f);
+      if (((row >> i) & 1u) && u1 >= umin && u0 <= umax) out |= 1u << (4 * j + i);
+    }
+  }
+  return out;
+}
+
 struct BinArgs {
   int64_t n;  // elements I*N
   int n_per_image, ts, tw, th, ty0, ty1;
@@ -980,24 +1062,49 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
 
 // One pass over the sorted entries: bin_start[b] = first entry of bin b
 // (bins without entries point at the next one; bin_start[n_bins] =
-// n_entries), and the rect of every entry next to it (an empty rect for an
-// element id outside [0, n), which only a wrong entry total can leave).
-__global__ void __launch_bounds__(256) bin_finish_kernel(int64_t n_entries, int64_t n, int dbits,
-                                                         const uint64_t* __restrict__ keys,
-                                                         const int32_t* __restrict__ vals,
-                                                         const uint2* __restrict__ rects,
-                                                         int64_t n_bins,
-                                                         int32_t* __restrict__ bin_start,
-                                                         uint2* __restrict__ sorted_rects) {
-  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < n_entries;
+// n_entries), and next to every entry the mask of its bin's tiles that it
+// covers (empty for an element id outside [0, n), which only a wrong entry
+// total can leave).  With conics and opacities (the culled encode) a tile
+// leaves the mask when tile_may_hit proves that the Gaussian stays below
+// alpha 1/255 at every pixel centre of the tile -- the rasterizer would skip
+// it at each of them.
+struct FinishArgs {
+  int64_t n_entries, n, n_bins, per_image;
+  int sw, dbits, ts;
+  const uint64_t* keys;
+  const int32_t* vals;
+  const uint2* rects;
+  const float* means2d;    // culled encode only
+  const float* conics;     // null: no culling
+  const float* opacities;
+  int32_t* bin_start;
+  uint32_t* masks;
+};
+
+__global__ void __launch_bounds__(256) bin_finish_kernel(const FinishArgs a) {
+  for (int64_t p = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; p < a.n_entries;
        p += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t b = (int64_t)(__ldg(keys + p) >> dbits);
-    const int64_t bp = p > 0 ? (int64_t)(__ldg(keys + p - 1) >> dbits) : -1;
-    for (int64_t q = bp + 1; q <= b && q <= n_bins; ++q) bin_start[q] = (int32_t)p;
-    if (p == n_entries - 1)
-      for (int64_t q = b + 1; q <= n_bins; ++q) bin_start[q] = (int32_t)n_entries;
-    const int32_t e = __ldg(vals + p);
-    sorted_rects[p] = (e >= 0 && e < n) ? __ldg(rects + e) : make_uint2(0u, 0u);
+    const int64_t b = (int64_t)(__ldg(a.keys + p) >> a.dbits);
+    const int64_t bp = p > 0 ? (int64_t)(__ldg(a.keys + p - 1) >> a.dbits) : -1;
+    for (int64_t q = bp + 1; q <= b && q <= a.n_bins; ++q) a.bin_start[q] = (int32_t)p;
+    if (p == a.n_entries - 1)
+      for (int64_t q = b + 1; q <= a.n_bins; ++q) a.bin_start[q] = (int32_t)a.n_entries;
+    const int32_t e = __ldg(a.vals + p);
+    uint32_t m = 0u;
+    if (e >= 0 && e < a.n && b < a.n_bins) {
+      const int64_t image = b / a.per_image;
+      const int rem = (int)(b - image * a.per_image);
+      const int tx0 = (rem % a.sw) * kBinTiles, ty0_ = (rem / a.sw) * kBinTiles;
+      m = cover_mask(__ldg(a.rects + e), tx0, ty0_);
+      if (a.conics && m) {
+        const float2 mu = __ldg(reinterpret_cast<const float2*>(a.means2d) + e);
+        const float c0 = __ldg(a.conics + (int64_t)e * 3), c1 = __ldg(a.conics + (int64_t)e * 3 + 1);
+        const float c2 = __ldg(a.conics + (int64_t)e * 3 + 2), o = __ldg(a.opacities + e);
+        m = bin_hit_mask(m, mu.x - ((float)(tx0 * a.ts) + 0.5f),
+                         mu.y - ((float)(ty0_ * a.ts) + 0.5f), c0, c1, c2, o, a.ts);
+      }
+    }
+    a.masks[p] = m;
   }
 }
 
@@ -1020,22 +1127,6 @@ __global__ void __launch_bounds__(256) bin_chunks_kernel(int64_t n_bins,
   }
 }
 
-// Tiles of a bin an entry's rect covers: bit 4j+i for tile (bx*4+i, by*4+j).
-__device__ __forceinline__ uint32_t cover_mask(uint2 r, int tx0, int ty0_) {
-  const int x0 = (int)(r.x & 0xFFFFu) - tx0, x1 = (int)(r.x >> 16) - tx0;
-  const int y0 = (int)(r.y & 0xFFFFu) - ty0_, y1 = (int)(r.y >> 16) - ty0_;
-  auto span = [](int a0, int a1) -> uint32_t {  // bits [max(a0,0), min(a1,4))
-    const int lo = a0 < 0 ? 0 : (a0 > 4 ? 4 : a0), hi = a1 < 0 ? 0 : (a1 > 4 ? 4 : a1);
-    return hi > lo ? ((1u << hi) - 1u) & ~((1u << lo) - 1u) : 0u;
-  };
-  const uint32_t xm = span(x0, x1), ym = span(y0, y1);
-  uint32_t m = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if ((ym >> j) & 1u) m |= xm << (4 * j);
-  return m;
-}
-
 // Bit t of a 16-bit mask to 16-bit field t of four words (tiles 4w..4w+3
 // in word w).
 __device__ __forceinline__ void spread16(uint32_t m, uint64_t f[4]) {
@@ -1054,7 +1145,7 @@ struct ItemArgs {
   const int32_t* bin_start;
   const int32_t* chunk_prefix;  // exclusive prefix of the bins' item counts
   const int64_t* n_items;       // device total of items
-  const uint2* sorted_rects;
+  const uint32_t* masks;  // per sorted entry: the tiles of its bin it lands in
 };
 
 // The item of this CTA: its bin and its entries [lo, hi).  False past the
@@ -1125,9 +1216,6 @@ __global__ void __launch_bounds__(kItemThreads) item_count_kernel(const ItemArgs
   int64_t bin;
   int lo, hi;
   if (!item_of(a, blockIdx.x, bin, lo, hi)) return;
-  int64_t image;
-  int tx0, ty0_;
-  bin_origin(a, bin, image, tx0, ty0_);
   const int p0 = lo + threadIdx.x * kItemPer;
   uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -1135,7 +1223,7 @@ __global__ void __launch_bounds__(kItemThreads) item_count_kernel(const ItemArgs
     const int p = p0 + k;
     if (p < hi) {
       uint64_t f[4];
-      spread16(cover_mask(__ldg(a.sorted_rects + p), tx0, ty0_), f);
+      spread16(__ldg(a.masks + p), f);
 #pragma unroll
       for (int w = 0; w < 4; ++w) acc[w] += f[w];
     }
@@ -1204,7 +1292,7 @@ __global__ void __launch_bounds__(kItemThreads) item_write_kernel(
   uint64_t run[4] = {0, 0, 0, 0};  // covering entries of earlier rounds, per tile
   for (int r = 0; r < kItemPer; ++r) {
     const int p = lo + r * kItemThreads + threadIdx.x;
-    const uint32_t m = p < hi ? cover_mask(__ldg(a.sorted_rects + p), tx0, ty0_) : 0u;
+    const uint32_t m = p < hi ? __ldg(a.masks + p) : 0u;
     uint64_t f[4], pre[4];
     spread16(m, f);
     block_scan_packed(f, pre, s_w, s_tot);  // the first also orders s_base / s_tile
@@ -1535,7 +1623,7 @@ static BinGeom bin_geom(const gs_isect_params* p) {
 // Workspace of the binned encode; the sort scratch comes first, so that its
 // error word sits at offset 0.
 struct BinnedLayout {
-  size_t sort, nent, nitems, keys, vals, skeys, svals, rects, srects, bstart, chunks, cprefix,
+  size_t sort, nent, nitems, nkept, keys, vals, skeys, svals, rects, masks, bstart, chunks, cprefix,
       icounts, counts, offs, scan, total;
   int64_t items;  // bound on the work items
 };
@@ -1551,12 +1639,13 @@ static BinnedLayout binned_layout(const gs_isect_params* p, int64_t n_entries) {
   size_t o = 0;
   L.sort = o; o += sort_layout(e1).total;
   L.nent = o; o += 256;
+  L.nkept = o; o += 256;
   L.keys = o; o += align256(8 * (size_t)e1);
   L.vals = o; o += align256(4 * (size_t)e1);
   L.skeys = o; o += align256(8 * (size_t)e1);
   L.svals = o; o += align256(4 * (size_t)e1);
   L.rects = o; o += align256(8 * (size_t)n1);
-  L.srects = o; o += align256(8 * (size_t)e1);
+  L.masks = o; o += align256(4 * (size_t)e1);
   L.items = ceil_div(e1, kItemEntries) + g.total;
   L.nitems = o; o += 256;
   L.bstart = o; o += align256(4 * (size_t)(g.total + 1));
@@ -1578,16 +1667,26 @@ extern "C" size_t gs_isect_tile_encode_binned_workspace_size(const gs_isect_para
   return binned_layout(p, n_bin_entries).total;
 }
 
+// offsets[s] += n_isects - kept: the culled lists end at n_isects.
+__global__ void __launch_bounds__(256) offsets_gap_kernel(int64_t slots, int64_t n_isects,
+                                                          const int64_t* __restrict__ kept,
+                                                          int32_t* __restrict__ offsets) {
+  const int32_t gap = (int32_t)(n_isects - *kept);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < slots;
+       i += (int64_t)gridDim.x * blockDim.x)
+    offsets[i] += gap;
+}
+
 // Binned sorted encode (see the kernels above): the same isect_ids /
 // flatten_ids as the encode followed by the stable 64-bit key sort, plus
 // the tile offsets of the call's tile rows when tile_offsets is given.
-// n_bin_entries is the second total of gs_isect_tile_count_totals.
-extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float* means2d,
-                                           const int32_t* radii, const float* depths,
-                                           int64_t n_isects, int64_t n_bin_entries,
-                                           int64_t* isect_ids, int32_t* flatten_ids,
-                                           int32_t* tile_offsets, void* workspace,
-                                           size_t workspace_bytes, gs_stream_t stream) {
+// n_bin_entries is the second total of gs_isect_tile_count_totals.  With
+// conics the tile-culled form (gs_isect_tile_encode_binned_culled).
+static int encode_binned(const gs_isect_params* p, const float* means2d, const int32_t* radii,
+                         const float* depths, const float* conics, const float* opacities,
+                         int64_t n_isects, int64_t n_bin_entries, int64_t* isect_ids,
+                         int32_t* flatten_ids, int32_t* tile_offsets, int64_t* n_kept,
+                         void* workspace, size_t workspace_bytes, gs_stream_t stream) {
   if (int rc = check_isect(p)) return rc;
   if (n_isects < 0 || n_bin_entries < 0 || n_bin_entries > n_isects)
     return invalid("intersect_tile_encode_binned: bad intersection / bin entry totals");
@@ -1612,6 +1711,8 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
   if (n == 0 || n_isects == 0) {
     if (tile_offsets && slots > 0 &&
         cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t) * (size_t)slots, s) != cudaSuccess)
+      return launch_status("intersect_tile_encode_binned");
+    if (n_kept && cudaMemsetAsync(n_kept, 0, sizeof(int64_t), s) != cudaSuccess)
       return launch_status("intersect_tile_encode_binned");
     return GS_OK;
   }
@@ -1644,9 +1745,10 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
     // the depth bits are the low key field and bin ids are unsigned
     sort_passes(n_bin_entries, 0, dbits + g.bits, kKV, kKV, K(L.keys), V(L.vals), K(L.skeys),
                 V(L.svals), ws + L.sort, s, false, nullptr, nullptr, /*signed_keys=*/false);
-    bin_finish_kernel<<<grid_for(n_bin_entries, 256), 256, 0, s>>>(
-        n_bin_entries, n, dbits, K(L.skeys), V(L.svals), R(L.rects), g.total, V(L.bstart),
-        R(L.srects));
+    const FinishArgs fa{n_bin_entries, n, g.total, g.per_image, g.sw, dbits, p->tile_size,
+                        K(L.skeys), V(L.svals), R(L.rects), means2d, conics, opacities,
+                        V(L.bstart), reinterpret_cast<uint32_t*>(ws + L.masks)};
+    bin_finish_kernel<<<grid_for(n_bin_entries, 256), 256, 0, s>>>(fa);
   } else {
     cudaMemsetAsync(ws + L.bstart, 0, 4 * (size_t)(g.total + 1), s);
   }
@@ -1656,16 +1758,47 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
   if (int rc = scan_i32(g.total, V(L.chunks), V(L.cprefix), n_items, ws + L.scan, scan_bytes, s))
     return rc;
   ItemArgs ia{g.total, g.per_image, g.sw, p->tile_width, ty0, rows, dbits,
-              V(L.bstart), V(L.cprefix), n_items, R(L.srects)};
+              V(L.bstart), V(L.cprefix), n_items, reinterpret_cast<const uint32_t*>(ws + L.masks)};
   item_count_kernel<<<(unsigned)L.items, kItemThreads, 0, s>>>(ia, V(L.icounts));
   int32_t* offs = tile_offsets ? tile_offsets : V(L.offs);
+  int64_t* kept = n_kept ? n_kept : reinterpret_cast<int64_t*>(ws + L.nkept);
   if (slots > 0) {
     slot_count_kernel<<<grid_for(slots, 256), 256, 0, s>>>(ia, slots, V(L.icounts), V(L.counts));
-    if (int rc = scan_i32(slots, V(L.counts), offs, nullptr, ws + L.scan, scan_bytes, s)) return rc;
+    if (int rc = scan_i32(slots, V(L.counts), offs, conics ? kept : nullptr, ws + L.scan,
+                          scan_bytes, s))
+      return rc;
+    if (conics)  // the culled lists take the last `kept` places
+      offsets_gap_kernel<<<grid_for(slots, 256), 256, 0, s>>>(slots, n_isects, kept, offs);
+  } else if (conics && cudaMemsetAsync(kept, 0, sizeof(int64_t), s) != cudaSuccess) {
+    return launch_status("intersect_tile_encode_binned");
   }
+
   item_write_kernel<<<(unsigned)L.items, kItemThreads, 0, s>>>(
       ia, tile_bits, V(L.icounts), offs, K(L.skeys), V(L.svals), n_isects, isect_ids, flatten_ids);
   return launch_status("intersect_tile_encode_binned");
+}
+
+extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float* means2d,
+                                           const int32_t* radii, const float* depths,
+                                           int64_t n_isects, int64_t n_bin_entries,
+                                           int64_t* isect_ids, int32_t* flatten_ids,
+                                           int32_t* tile_offsets, void* workspace,
+                                           size_t workspace_bytes, gs_stream_t stream) {
+  return encode_binned(p, means2d, radii, depths, nullptr, nullptr, n_isects, n_bin_entries,
+                       isect_ids, flatten_ids, tile_offsets, nullptr, workspace, workspace_bytes,
+                       stream);
+}
+
+extern "C" int gs_isect_tile_encode_binned_culled(
+    const gs_isect_params* p, const float* means2d, const int32_t* radii, const float* depths,
+    const float* conics, const float* opacities, int64_t n_isects, int64_t n_bin_entries,
+    int64_t* isect_ids, int32_t* flatten_ids, int32_t* tile_offsets, int64_t* n_kept,
+    void* workspace, size_t workspace_bytes, gs_stream_t stream) {
+  if (!conics || !opacities)
+    return invalid("intersect_tile_encode_binned_culled: conics and opacities are required");
+  return encode_binned(p, means2d, radii, depths, conics, opacities, n_isects, n_bin_entries,
+                       isect_ids, flatten_ids, tile_offsets, n_kept, workspace, workspace_bytes,
+                       stream);
 }
 
 extern "C" int gs_isect_tile_encode_binned_check(int64_t n_bin_entries, const void* workspace,

@@ -11,5 +11,6 @@ fused training step), ``synthetic`` (seeded benchmark scenes).
 """
 from ._gsplat_core import *  # noqa: F401,F403
 from ._gsplat_core import (floor_log2_plus_one, intersect_tile_count,  # noqa: F401
-                           intersect_tile_encode, intersect_tile_offsets, intersect_tile_sort)
+                           intersect_tile_culled_forward, intersect_tile_encode,
+                           intersect_tile_offsets, intersect_tile_sort)
 from ._lib import GsplatError, LIB_PATH, load  # noqa: F401

@@ -403,6 +403,60 @@ def intersect_tile_encode_binned(means2d, radii, depths, I, tile_size, tile_widt
     return isect_ids, flatten_ids
 
 
+def intersect_tile_culled_forward(inputs, I, tile_size, tile_width, tile_height):
+    """Sorted intersections with opacity-aware tile culling: what
+    ``intersect_tile_forward(..., sort=True)`` returns, minus every
+    (tile, Gaussian) pair whose Gaussian -- conics [I,N,3] and opacities
+    [I,N], the rasterizer's inputs -- stays below alpha 1/255 at every pixel
+    centre of the tile.  The reference's intersect_tile_forward refuses
+    conics / opacities (gsplat_intersect.cpp:115-126); the rasterizer skips
+    such pairs at every pixel, so rendering these lists gives the same
+    colours and alphas bit for bit.  Returns {"isect_ids", "flatten_ids",
+    "tile_offsets"} (the kept pairs, in the unculled order; tile_offsets
+    [I, tile_height, tile_width] into them)."""
+    means2d = _req(inputs, "means2d")
+    radii = _req(inputs, "radii")
+    depths = _req(inputs, "depths")
+    conics = _req(inputs, "conics")
+    opacities = _req(inputs, "opacities")
+    _validate_intersect(means2d, radii, depths, None, None, None, None, False)
+    means2d, radii, depths = _cuda(means2d, radii, depths)
+    if conics.dtype != torch.float32 or opacities.dtype != torch.float32:
+        raise RuntimeError("intersect_tile_culled_forward expects float32 conics / opacities.")
+    conics, opacities = _cuda(conics, opacities)
+    N = means2d.shape[-2]
+    if conics.numel() != int(I) * N * 3 or opacities.numel() != int(I) * N:
+        raise RuntimeError("intersect_tile_culled_forward expects conics [I,N,3] and "
+                           "opacities [I,N].")
+    if max(tile_width, tile_height) > 65535:
+        raise RuntimeError("intersect_tile_culled_forward: more than 65535 tiles per row or column.")
+    if floor_log2_plus_one(I) + floor_log2_plus_one(tile_width * tile_height) > 32:
+        raise RuntimeError("intersect_tile_encode image id and tile id require more than 32 bits.")
+    _, m, bins = intersect_tile_count_totals(means2d, radii, I, tile_size, tile_width, tile_height)
+    if m >= 2 ** 31:
+        raise RuntimeError(
+            f"intersect_tile_encode: {m} intersections exceed the int32 index range")
+    isect_ids = _empty((m,), torch.int64)
+    flatten_ids = _empty((m,), torch.int32)
+    offsets = _empty((int(I), int(tile_height), int(tile_width)), torch.int32)
+    kept = torch.zeros((1,), dtype=torch.int64, device=means2d.device)
+    lib = _lib.load()
+    p = IsectParams(int(I), int(N), int(tile_size), int(tile_width), int(tile_height))
+    ws = _empty((max(1, lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(p), bins)),),
+                torch.uint8)
+    check(lib.gs_isect_tile_encode_binned_culled(
+        ct.byref(p), _ptr(means2d), _ptr(radii), _ptr(depths), _ptr(conics),
+        _ptr(opacities), int(m), int(bins), _ptr(isect_ids), _ptr(flatten_ids),
+        _ptr(offsets), _ptr(kept), _ptr(ws), ws.numel(), _stream()),
+        "intersect_tile_culled_forward")
+    if bins > 0:
+        check(lib.gs_isect_tile_encode_binned_check(bins, _ptr(ws), _stream()),
+              "intersect_tile_culled_forward")
+    gap = m - int(kept.item())  # the kept lists fill the last places
+    return {"isect_ids": isect_ids[gap:], "flatten_ids": flatten_ids[gap:],
+            "tile_offsets": offsets - gap}
+
+
 def intersect_tile_sort(isect_ids, flatten_ids, key_bits=64):
     """Stable sort by key (gsplat_intersect.cpp:266-286: argsort + take)."""
     if isect_ids.dtype != torch.int64:

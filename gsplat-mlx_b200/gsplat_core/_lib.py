@@ -107,6 +107,9 @@ SIGNATURES = {
     "gs_isect_tile_encode_binned_workspace_size": (_sz, [_P(IsectParams), _i64]),
     "gs_isect_tile_encode_binned": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _i64, _i64, _vp,
                                                _vp, _vp, _vp, _sz, _vp]),
+    "gs_isect_tile_encode_binned_culled": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _vp,
+                                                      _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz,
+                                                      _vp]),
     "gs_isect_tile_encode_binned_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),

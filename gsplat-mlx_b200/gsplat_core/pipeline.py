@@ -78,7 +78,7 @@ class TrainingStep:
 
     def __init__(self, n, sh_degree, K, cameras, width, height, tile_size=16, eps2d=0.3,
                  near_plane=0.01, far_plane=1e10, device=None, use_background=True,
-                 max_isects_per_pass=1 << 30):
+                 max_isects_per_pass=1 << 30, tile_cull=False):
         self.dev = device or torch.device("cuda", torch.cuda.current_device())
         self.N, self.deg, self.K, self.C = int(n), int(sh_degree), int(K), int(cameras)
         self.W, self.H, self.ts = int(width), int(height), int(tile_size)
@@ -109,6 +109,14 @@ class TrainingStep:
         # intersections (grown on demand); the binned encode needs 16-bit
         # tile coordinates, else the depth-first sorted encode runs
         self.binned = max(self.tw, self.th) <= 65535
+        # opacity-aware tile culling in the binned encode (opt-in): (tile,
+        # Gaussian) pairs below alpha 1/255 at every pixel centre of the tile
+        # are not listed (the rasterizer would skip them at each pixel; the
+        # renders are the same bit for bit, the lists shorter).  The 16x16
+        # rasterizers drop such pairs themselves when they stage a batch, so
+        # the step gains little from it.  Kept totals per band.
+        self.tile_cull = bool(tile_cull) and self.binned
+        self.kept = torch.zeros((64,), dtype=torch.int64, device=self.dev)
         self.capacity = 0
         self.sort_ws = torch.empty((0,), dtype=torch.uint8, device=self.dev)
         self.m = 0
@@ -248,7 +256,19 @@ class TrainingStep:
             grew = self._ensure_capacity(m, bins)
             self.m, self.bins = m, bins
             m_total += m
-            if self.binned:
+            if self.binned and self.tile_cull:
+                # sorted, tile-culled intersections (the last places of the
+                # lists) and the band's tile offsets in one call
+                if b >= self.kept.numel():
+                    self.kept = torch.zeros((2 * len(bands),), dtype=torch.int64, device=self.dev)
+                check(L.gs_isect_tile_encode_binned_culled(
+                    ct.byref(ip), _p(self.means2d), _p(self.radii), _p(self.depths),
+                    _p(self.conics), _p(opac), m, bins, _p(self.sorted_ids),
+                    _p(self.sorted_flatten), _p(self.tile_offsets),
+                    ct.c_void_p(self.kept.data_ptr() + 8 * b), _p(self.sort_ws),
+                    self.sort_ws.numel(), s), "isect_encode_sort")
+                self._mark("isect_encode_sort")
+            elif self.binned:
                 # sorted intersections and the band's tile offsets in one call
                 check(L.gs_isect_tile_encode_binned(ct.byref(ip), _p(self.means2d),
                                                     _p(self.radii), _p(self.depths), m, bins,
@@ -300,6 +320,7 @@ class TrainingStep:
             self._mark("rasterize_bwd")
             b += 1
         m = m_total
+        self.m_total = m_total
         self.bands = len(bands)
         if after_raster is not None:
             after_raster()
@@ -328,6 +349,14 @@ class TrainingStep:
         elif self.m > 0:
             check(self.lib.gs_isect_tile_encode_sorted_check(
                 self.C * self.N, self.m, _p(self.sort_ws), _s()), "isect_encode_sort")
+
+    def kept_isects(self) -> int:
+        """Intersections the last step's rasterizer passes walked: the
+        tile-culled totals of its bands (a host read), else the counted
+        total."""
+        if not self.tile_cull:
+            return self.m_total
+        return int(self.kept[:self.bands].sum().item())
 
     def gradients(self):
         return {"v_means": self.v_means, "v_quats": self.v_quats, "v_scales": self.v_scales,

@@ -253,6 +253,30 @@ int gs_isect_tile_encode_binned(const gs_isect_params* p, const float* means2d,
                                 int32_t* tile_offsets, void* workspace,
                                 size_t workspace_bytes, gs_stream_t stream);
 
+/* Opacity-aware tile culling on top of the binned encode: the tile lists
+ * of gs_isect_tile_encode_binned with every (tile, element) pair removed
+ * for which the element's opacity-weighted Gaussian (conics [I,N,3],
+ * opacities [I,N], the rasterizer's inputs) stays below alpha 1/255 at
+ * every pixel centre of the tile, by a margin that covers fp32 rounding.
+ * The rasterizer skips such a pair at every pixel, so rendering the culled
+ * lists gives the same colours and alphas bit for bit; only the list
+ * positions (and so last_ids) change.  The kept lists keep their order and
+ * fill the LAST n_kept places of isect_ids / flatten_ids [n_isects]:
+ * tile_offsets point there, so that the last tile still ends at n_isects
+ * and a rasterizer call with the same n_isects needs no host read.
+ * *n_kept (device int64, may be NULL) receives the kept total.  Same
+ * workspace as gs_isect_tile_encode_binned.
+ * Replaces the conics / opacities arguments of intersect_tile_forward,
+ * which the reference accepts and refuses (gsplat_intersect.cpp:115-126). */
+int gs_isect_tile_encode_binned_culled(const gs_isect_params* p, const float* means2d,
+                                       const int32_t* radii, const float* depths,
+                                       const float* conics, const float* opacities,
+                                       int64_t n_isects, int64_t n_bin_entries,
+                                       int64_t* isect_ids, int32_t* flatten_ids,
+                                       int32_t* tile_offsets, int64_t* n_kept,
+                                       void* workspace, size_t workspace_bytes,
+                                       gs_stream_t stream);
+
 /* The radix passes of the calls above and below wait on one another's
  * tiles with bounded waits; a wait that gives up (a defect, not a workload
  * condition) raises an error word in the workspace and the kernels finish

@@ -106,6 +106,10 @@ def test_binned_encode_and_densify_validate_before_device_work(gs):
     rc = lib.gs_isect_tile_encode_binned(ct.byref(wide), None, None, None, 5, 5, None, None, None,
                                          None, 0, None)
     assert rc == L.GS_ERR_INVALID and b"65535" in lib.gs_last_error()
+    # the tile-culled encode needs the rasterizer's conics and opacities
+    rc = lib.gs_isect_tile_encode_binned_culled(ct.byref(p), None, None, None, None, None, 5, 5,
+                                                None, None, None, None, None, 0, None)
+    assert rc == L.GS_ERR_INVALID and b"conics and opacities" in lib.gs_last_error()
     assert lib.gs_isect_tile_encode_binned_workspace_size(ct.byref(L.IsectParams(0, 10, 16, 4, 4,
                                                                                 0, 0, 0)), 5) == 0
     assert lib.gs_isect_tile_count_totals(ct.byref(p), None, None, None, None, None) == \

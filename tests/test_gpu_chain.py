@@ -67,7 +67,8 @@ def test_training_step_matches_oracle(gs, oracle, cuda, n, cams):
     idx = np.sort(rng.choice(sc.n, size=n, replace=False))
     vrc, vra = S.cotangents(3, cams, sc.height, sc.width)
     rf, it, offs, eg, vrc, vra, near = oracle_step(oracle, sc, idx, vrc, vra)
-    step = pipeline.TrainingStep(n, 3, 16, cams, sc.width, sc.height)
+    # the reference's full lists (the tile-culled ones are pinned in test_gpu_tile_cull)
+    step = pipeline.TrainingStep(n, 3, 16, cams, sc.width, sc.height, tile_cull=False)
     flat, m = step.run(T(sc.means[idx]), T(sc.quats[idx]), T(sc.scales[idx]),
                        T(sc.opacities[idx]), T(sc.coeffs[idx]), T(sc.viewmats), T(sc.Ks),
                        T(vrc), T(vra))
@@ -90,7 +91,7 @@ def test_full_size_config3_properties(gs, oracle, cuda):
     from gsplat_core import pipeline, synthetic as S
     sc = S.config3(seed=0)
     vrc, vra = S.cotangents(0, 1, sc.height, sc.width)
-    step = pipeline.TrainingStep(sc.n, 3, 16, 1, sc.width, sc.height)
+    step = pipeline.TrainingStep(sc.n, 3, 16, 1, sc.width, sc.height, tile_cull=False)
     args = [T(sc.means), T(sc.quats), T(sc.scales), T(sc.opacities), T(sc.coeffs),
             T(sc.viewmats), T(sc.Ks), T(vrc), T(vra)]
     flat, m = step.run(*args)
@@ -124,7 +125,8 @@ def test_full_size_config3_properties(gs, oracle, cuda):
 
 
 
-def test_banded_passes_match_one_pass(gs, cuda):
+@pytest.mark.parametrize("tile_cull", [False, True])
+def test_banded_passes_match_one_pass(gs, cuda, tile_cull):
     """Past max_isects_per_pass the step renders bands of tile rows, each
     with its own intersection pass: the same image bit for bit, and the
     same gradients up to the order of the atomic additions."""
@@ -138,10 +140,11 @@ def test_banded_passes_match_one_pass(gs, cuda):
     vrc, vra = S.cotangents(8, 2, H, W)
     args = [T(sc.means[idx]), T(sc.quats[idx]), T(sc.scales[idx]), T(sc.opacities[idx]),
             T(sc.coeffs[idx]), T(views), T(Ks), T(vrc), T(vra)]
-    one = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H)
+    one = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H, tile_cull=tile_cull)
     flat1, m1 = one.run(*args)
     flat1 = flat1.clone()
-    banded = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H, max_isects_per_pass=m1 // 3)
+    banded = pipeline.TrainingStep(idx.size, 3, 16, 2, W, H, max_isects_per_pass=m1 // 3,
+                                   tile_cull=tile_cull)
     flat2, m2 = banded.run(*args)
     torch.cuda.synchronize()
     banded.check()
