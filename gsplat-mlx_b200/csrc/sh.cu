@@ -692,12 +692,18 @@ __global__ void __launch_bounds__(32 * kGlueBwdWarps, ACC ? 3 : 4) glue_bwd_vec_
     if (n < N) {
       for (int c = 0; c < C; ++c)
         any |= bwd_visible(masks, radii, v_colors, skip_zero, (int64_t)c * N + n);
-      if (!any) {
-        float4* out = reinterpret_cast<float4*>(v_coeffs + n * (int64_t)K * 3);
-        for (int v = 0; v < K * 3 / 4; ++v) out[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
     }
     const unsigned bal = __ballot_sync(0xffffffffu, any);
+    {
+      // zero rows of the chunk's Gaussians that no camera sees: the chunk's
+      // rows are contiguous, so the warp stores them together (512 B per
+      // store instruction) rather than one row per lane
+      const int per = K * 3 / 4;  // float4 per row
+      const int rows = (int)min((int64_t)32, (int64_t)N - ch * 32);
+      float4* base = reinterpret_cast<float4*>(v_coeffs + ch * 32 * (int64_t)K * 3);
+      for (int f = lane; f < rows * per; f += 32)
+        if (!((bal >> (f / per)) & 1u)) base[f] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
     if (any) q[qn + __popc(bal & ((1u << lane) - 1u))] = (int)n;
     qn += __popc(bal);
     __syncwarp();
