@@ -520,7 +520,9 @@ def run_ours(args):
             if k >= 2:
                 comp.wait_event(d2h_done[b])    # staging buffer b downloaded
             one(bufs[b])
-            stage[b].copy_(step.grad_flat)
+            # staged by a kernel (an elementwise copy), not a memcpy that a
+            # copy engine busy with the previous download would hold back
+            torch.mul(step.grad_flat, 1.0, out=stage[b])
             comp_done[b].record(comp)
             d2h_s.wait_event(comp_done[b])
             with torch.cuda.stream(d2h_s):

@@ -1582,6 +1582,35 @@ extern "C" int gs_isect_tile_encode_sorted_check(int64_t n_elements, int64_t n_i
                          as_stream(stream));
 }
 
+// n int64 values from device memory to pinned host memory by one warp's
+// stores through the host mapping (no copy engine).
+__global__ void store_i64_kernel(const int64_t* __restrict__ src, int64_t* __restrict__ dst, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+}
+
+// A small device-to-host read that must not queue behind large transfers:
+// a cudaMemcpyAsync to host runs on a copy engine, where it can wait for
+// another stream's download of hundreds of MB; a kernel storing into the
+// pinned buffer's device mapping does not.  Falls back to cudaMemcpyAsync
+// when host_dst has no device mapping.
+extern "C" int gs_store_to_host_i64(const int64_t* src, int64_t* host_dst, int32_t n,
+                                    gs_stream_t stream) {
+  if (n < 0 || n > 1024 || (n > 0 && (!src || !host_dst)))
+    return invalid("store_to_host_i64: bad arguments");
+  if (n == 0) return GS_OK;
+  cudaStream_t s = as_stream(stream);
+  void* mapped = nullptr;
+  if (cudaHostGetDevicePointer(&mapped, host_dst, 0) != cudaSuccess || !mapped) {
+    cudaGetLastError();  // clear the lookup's error: not a mapped host buffer
+    if (cudaMemcpyAsync(host_dst, src, sizeof(int64_t) * (size_t)n, cudaMemcpyDeviceToHost, s) !=
+        cudaSuccess)
+      return launch_status("store_to_host_i64");
+    return GS_OK;
+  }
+  store_i64_kernel<<<1, 32, 0, s>>>(src, static_cast<int64_t*>(mapped), n);
+  return launch_status("store_to_host_i64");
+}
+
 extern "C" int gs_isect_tile_count_totals(const gs_isect_params* p, const float* means2d,
                                           const int32_t* radii, int32_t* tiles_per_gauss,
                                           int64_t* totals_device, gs_stream_t stream) {

@@ -111,6 +111,7 @@ SIGNATURES = {
                                                       _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz,
                                                       _vp]),
     "gs_isect_tile_encode_binned_check": (ct.c_int, [_i64, _vp, _vp]),
+    "gs_store_to_host_i64": (ct.c_int, [_vp, _vp, _i32, _vp]),
     "gs_isect_sort_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

@@ -228,7 +228,10 @@ class TrainingStep:
             check(L.gs_isect_tile_count_totals(ct.byref(ip), _p(self.means2d), _p(self.radii),
                                                _p(self.tiles_per_gauss), _p(self.total), s),
                   "isect_count")
-            self.total_host.copy_(self.total, non_blocking=True)
+            # the host read of the totals: kernel stores into the pinned
+            # buffer, not a copy that could queue behind a download
+            check(L.gs_store_to_host_i64(_p(self.total), _p(self.total_host), 2, s),
+                  "isect_count")
             self._mark("isect_count")
             counted = torch.cuda.Event()
             counted.record()

@@ -240,6 +240,15 @@ int gs_isect_tile_encode_sorted(const gs_isect_params* p, const float* means2d,
  * gs_isect_tile_encode_binned_workspace_size(p, n_bin_entries).  Tile grids
  * wider or taller than 65535 tiles are refused (GS_ERR_INVALID).
  * No reference counterpart. */
+/* Copies n (<= 1024) int64 from device memory into pinned host memory with a
+ * kernel's stores through the buffer's device mapping, so that a host read of
+ * a few totals (the intersection count of a step) does not wait on the copy
+ * engines behind another stream's large download; without a mapping it is a
+ * cudaMemcpyAsync.  The values are on the host once `stream` has passed this
+ * point.  No reference counterpart (the reference reads its total with
+ * MLX's item()). */
+int gs_store_to_host_i64(const int64_t* src, int64_t* host_dst, int32_t n,
+                         gs_stream_t stream);
 int gs_isect_tile_count_totals(const gs_isect_params* p, const float* means2d,
                                const int32_t* radii, int32_t* tiles_per_gauss,
                                int64_t* totals_device /* [2]: intersections, bin entries */,
