@@ -60,6 +60,11 @@ class DensifyMaskParams(ct.Structure):
                 ("prune_scale2d", ct.c_double), ("scene_scale", ct.c_double)]
 
 
+class SpzParams(ct.Structure):
+    _fields_ = [("n", _i64), ("scale_mode", _i32), ("rotation_mode", _i32), ("quat_order", _i32),
+                ("color_mode", _i32), ("source", _i32), ("sh_rest", _i32), ("rest_stride", _i32)]
+
+
 class AdamParams(ct.Structure):
     _fields_ = [("n", _i64), ("learning_rate", _f), ("beta1", _f), ("beta2", _f), ("eps", _f)]
 
@@ -123,6 +128,7 @@ SIGNATURES = {
     "gs_fit_adam": (ct.c_int, [_P(AdamParams)] + [_vp] * 17),
     "gs_densify_accumulate": (ct.c_int, [_P(DensifyParams)] + [_vp] * 6),
     "gs_densify_masks": (ct.c_int, [_P(DensifyMaskParams)] + [_vp] * 10),
+    "gs_spz_attributes": (ct.c_int, [_P(SpzParams)] + [_vp] * 13),
     "gs_rasterize_fwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 12),
     "gs_rasterize_bwd": (ct.c_int, [_P(RasterParams)] + [_vp] * 19),
 }

@@ -472,6 +472,42 @@ int gs_densify_masks(const gs_densify_mask_params* p, const float* grad2d,
                      uint8_t* clone, uint8_t* split, uint8_t* prune,
                      int64_t* totals_device, gs_stream_t stream);
 
+/* ------------------------------------------------------------------ */
+/* SPZ export attributes                                               */
+/* Replaces the numpy conversions of export_trained_spz               */
+/* (scripts/test/scanner_points_training_utils.py:1424-1493, with     */
+/* positions_to_spz :1361, scales_to_spz :1380, quats_to_spz :1392,   */
+/* quats_to_spz_storage :1415): the arrays the reference hands to the */
+/* spz package's GaussianCloud.  Packing them into a .spz file is that */
+/* package's job (spz.save_spz), not this library's.                  */
+/* ------------------------------------------------------------------ */
+typedef struct {
+  int64_t n;             /* Gaussians                                      */
+  int32_t scale_mode;    /* 0 direct, 1 scanner_axis (y and z swapped)     */
+  int32_t rotation_mode; /* 0 direct, 1 position_axis, 2 fastgs_conjugate,
+                            3 position_conjugate                           */
+  int32_t quat_order;    /* 0 wxyz, 1 xyzw                                 */
+  int32_t color_mode;    /* 0 sh, 1 raw_rgb                                */
+  int32_t source;        /* 0 SH model (colors_or_dc = features_dc [n,3]),
+                            1 RGB model (colors_or_dc = its colours [n,3]) */
+  int32_t sh_rest;       /* rest coefficients written per Gaussian:
+                            (degree+1)^2 - 1 for an SH model in sh mode,
+                            else 0                                         */
+  int32_t rest_stride;   /* rest coefficients per row of features_rest     */
+} gs_spz_params;
+
+/* means [n,3], quats [n,4] (wxyz), log_scales [n,3], opacity_logits [n],
+ * colors_or_dc [n,3], features_rest [n,rest_stride,3] -> positions [n,3],
+ * scales [n,3], rotations [n,4], alphas [n], colors [n,3],
+ * sh [n,sh_rest,3] (NULL when sh_rest is 0).  fp32 in the reference's
+ * operation order. */
+int gs_spz_attributes(const gs_spz_params* p, const float* means,
+                      const float* quats, const float* log_scales,
+                      const float* opacity_logits, const float* colors_or_dc,
+                      const float* features_rest, float* positions,
+                      float* scales, float* rotations, float* alphas,
+                      float* colors, float* sh, gs_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -106,6 +106,14 @@ def test_binned_encode_and_densify_validate_before_device_work(gs):
     rc = lib.gs_isect_tile_encode_binned(ct.byref(wide), None, None, None, 5, 5, None, None, None,
                                          None, 0, None)
     assert rc == L.GS_ERR_INVALID and b"65535" in lib.gs_last_error()
+    # SPZ attributes: unknown modes, and SH rest terms with RGB colours
+    sp = L.SpzParams(4, 0, 4, 0, 0, 0, 0, 0)
+    assert lib.gs_spz_attributes(ct.byref(sp), *([None] * 13)) == L.GS_ERR_INVALID
+    sp = L.SpzParams(4, 0, 0, 0, 0, 1, 3, 15)
+    assert lib.gs_spz_attributes(ct.byref(sp), *([None] * 13)) == L.GS_ERR_INVALID
+    sp = L.SpzParams(4, 0, 0, 0, 0, 0, 0, 0)
+    assert lib.gs_spz_attributes(ct.byref(sp), *([None] * 13)) == L.GS_ERR_INVALID
+    assert b"missing buffer" in lib.gs_last_error()
     # the host store of a few totals is bounded and needs both buffers
     assert lib.gs_store_to_host_i64(None, None, 2000, None) == L.GS_ERR_INVALID
     assert lib.gs_store_to_host_i64(None, None, 2, None) == L.GS_ERR_INVALID
