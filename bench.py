@@ -43,7 +43,7 @@ LINK_GBS = 770.0
 # one ncu capture of this benchmark (profiles/*_config3.md); None = not
 # captured.  Valid for the config-3 workload only.
 PROFILED_TRAFFIC = {"rasterize_bwd": 44.4e6 + 0.2e6, "rasterize_fwd": 15.9e6 + 0.01e6,
-                    "sh_bwd": 119.9e6 + 150.2e6}
+                    "sh_bwd": 120.0e6 + 151.8e6, "projection_bwd": 86.4e6 + 13.7e6}
 
 
 def load_peaks():
