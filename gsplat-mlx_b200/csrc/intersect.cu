@@ -455,6 +455,53 @@ __global__ void __launch_bounds__(kScanThreads) visible_depth_keys_kernel(
   }
 }
 
+// With the scanned block counts of visible_count_kernel: the visible
+// elements' projection outputs as packed rows, in element (image, Gaussian)
+// order -- image and Gaussian ids, radii, means2d, depths, conics and, when
+// given, compensations.  Rows past `capacity` are dropped.
+struct PackArgs {
+  int64_t n, capacity;
+  int N;
+  const int32_t* radii;
+  const float *means2d, *depths, *conics, *comps;
+  int32_t *image_ids, *gaussian_ids, *p_radii;
+  float *p_means2d, *p_depths, *p_conics, *p_comps;
+};
+
+__global__ void __launch_bounds__(kScanThreads) pack_rows_kernel(const PackArgs a,
+                                                                 const int64_t* __restrict__ sums) {
+  __shared__ int64_t s_warp[32];
+  const int64_t base = (int64_t)blockIdx.x * kScanChunk;
+  int f[kScanItems];
+  int64_t acc = 0;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    f[k] = i < a.n ? visible_at(a.radii, i) : 0;
+    acc += f[k];
+  }
+  int64_t total;
+  int64_t run = block_exclusive_scan<kScanThreads>(acc, s_warp, &total) + sums[blockIdx.x];
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    if (!f[k]) continue;
+    const int64_t i = base + (int64_t)threadIdx.x * kScanItems + k;
+    if (run < a.capacity) {
+      const int64_t r = run;
+      a.image_ids[r] = (int32_t)(i / a.N);
+      a.gaussian_ids[r] = (int32_t)(i % a.N);
+      reinterpret_cast<int2*>(a.p_radii)[r] = __ldg(reinterpret_cast<const int2*>(a.radii) + i);
+      reinterpret_cast<float2*>(a.p_means2d)[r] =
+          __ldg(reinterpret_cast<const float2*>(a.means2d) + i);
+      a.p_depths[r] = __ldg(a.depths + i);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) a.p_conics[r * 3 + c] = __ldg(a.conics + i * 3 + c);
+      if (a.comps) a.p_comps[r] = __ldg(a.comps + i);
+    }
+    ++run;
+  }
+}
+
 // ------------------------------------------------------------ radix sort
 // LSD radix sort, 8-bit digits, one kernel per digit ("onesweep": Adinets &
 // Merrill, 2022).  A histogram kernel counts the digits of every pass in
@@ -954,6 +1001,7 @@ struct BinArgs {
   const float* means2d;
   const int32_t* radii;
   const float* depths;
+  const int32_t* image_ids;  // packed rows: each row's image (else i / n_per_image)
 };
 
 // Block sums of the per-element bin counts (the scan's first half).
@@ -1017,7 +1065,7 @@ __global__ void __launch_bounds__(kScanThreads) bin_emit_kernel(
                                a.th, a.ty0, a.ty1);
       c = rect_bins(q);
       if (c > 0) {
-        const int64_t image = i / a.n_per_image;
+        const int64_t image = a.image_ids ? (int64_t)__ldg(a.image_ids + i) : i / a.n_per_image;
         rects[i] = pack_rect(q);
         const int bx0 = q.x0 / kBinTiles, by0 = q.y0 / kBinTiles;
         s_bw[warp][lane] = (q.x1 - 1) / kBinTiles - bx0 + 1;
@@ -1657,11 +1705,14 @@ struct BinnedLayout {
   int64_t items;  // bound on the work items
 };
 
-static BinnedLayout binned_layout(const gs_isect_params* p, int64_t n_entries) {
+// packed: the elements are N packed rows (with their own image ids), not
+// I * N.
+static BinnedLayout binned_layout(const gs_isect_params* p, int64_t n_entries,
+                                  bool packed = false) {
   int ty0, ty1;
   tile_rows(p, ty0, ty1);
   const BinGeom g = bin_geom(p);
-  const int64_t n = (int64_t)p->I * p->N;
+  const int64_t n = packed ? (int64_t)p->N : (int64_t)p->I * p->N;
   const int64_t slots = (int64_t)p->I * (ty1 - ty0) * p->tile_width;
   const int64_t e1 = n_entries < 1 ? 1 : n_entries, n1 = n < 1 ? 1 : n;
   BinnedLayout L;
@@ -1711,7 +1762,8 @@ __global__ void __launch_bounds__(256) offsets_gap_kernel(int64_t slots, int64_t
 // the tile offsets of the call's tile rows when tile_offsets is given.
 // n_bin_entries is the second total of gs_isect_tile_count_totals.  With
 // conics the tile-culled form (gs_isect_tile_encode_binned_culled).
-static int encode_binned(const gs_isect_params* p, const float* means2d, const int32_t* radii,
+static int encode_binned(const gs_isect_params* p, const int32_t* image_ids,
+                         const float* means2d, const int32_t* radii,
                          const float* depths, const float* conics, const float* opacities,
                          int64_t n_isects, int64_t n_bin_entries, int64_t* isect_ids,
                          int32_t* flatten_ids, int32_t* tile_offsets, int64_t* n_kept,
@@ -1736,7 +1788,7 @@ static int encode_binned(const gs_isect_params* p, const float* means2d, const i
   const int rows = ty1 - ty0;
   const int64_t slots = (int64_t)p->I * rows * p->tile_width;
   cudaStream_t s = as_stream(stream);
-  const int64_t n = (int64_t)p->I * p->N;
+  const int64_t n = image_ids ? (int64_t)p->N : (int64_t)p->I * p->N;
   if (n == 0 || n_isects == 0) {
     if (tile_offsets && slots > 0 &&
         cudaMemsetAsync(tile_offsets, 0, sizeof(int32_t) * (size_t)slots, s) != cudaSuccess)
@@ -1747,7 +1799,7 @@ static int encode_binned(const gs_isect_params* p, const float* means2d, const i
   }
   if (!means2d || !radii || !depths || !isect_ids || !flatten_ids)
     return invalid("intersect_tile_encode_binned: missing buffer");
-  const BinnedLayout L = binned_layout(p, n_bin_entries);
+  const BinnedLayout L = binned_layout(p, n_bin_entries, image_ids != nullptr);
   if (!workspace || workspace_bytes < L.total) {
     set_error("intersect_tile_encode_binned: workspace of %zu bytes needed", L.total);
     return GS_ERR_WORKSPACE;
@@ -1762,7 +1814,7 @@ static int encode_binned(const gs_isect_params* p, const float* means2d, const i
   // 31 + bin bits, one radix pass fewer when that crosses a multiple of 8
   const int dbits = p->positive_depths ? 31 : 32;
   BinArgs a{n, p->N, p->tile_size, p->tile_width, p->tile_height, ty0, ty1,
-            g.sw, (int)g.per_image, dbits, means2d, radii, depths};
+            g.sw, (int)g.per_image, dbits, means2d, radii, depths, image_ids};
   const int64_t nb = ceil_div(n, kScanChunk);
   const size_t scan_bytes = L.total - L.scan;
   int64_t* sums = reinterpret_cast<int64_t*>(ws + L.scan);
@@ -1813,7 +1865,8 @@ extern "C" int gs_isect_tile_encode_binned(const gs_isect_params* p, const float
                                            int64_t* isect_ids, int32_t* flatten_ids,
                                            int32_t* tile_offsets, void* workspace,
                                            size_t workspace_bytes, gs_stream_t stream) {
-  return encode_binned(p, means2d, radii, depths, nullptr, nullptr, n_isects, n_bin_entries,
+  return encode_binned(p, nullptr, means2d, radii, depths, nullptr, nullptr, n_isects,
+                       n_bin_entries,
                        isect_ids, flatten_ids, tile_offsets, nullptr, workspace, workspace_bytes,
                        stream);
 }
@@ -1825,9 +1878,68 @@ extern "C" int gs_isect_tile_encode_binned_culled(
     void* workspace, size_t workspace_bytes, gs_stream_t stream) {
   if (!conics || !opacities)
     return invalid("intersect_tile_encode_binned_culled: conics and opacities are required");
-  return encode_binned(p, means2d, radii, depths, conics, opacities, n_isects, n_bin_entries,
+  return encode_binned(p, nullptr, means2d, radii, depths, conics, opacities, n_isects,
+                       n_bin_entries,
                        isect_ids, flatten_ids, tile_offsets, n_kept, workspace, workspace_bytes,
                        stream);
+}
+
+extern "C" size_t gs_isect_tile_encode_binned_packed_workspace_size(const gs_isect_params* p,
+                                                                   int64_t n_bin_entries) {
+  if (!p || check_isect(p) != GS_OK) return 0;
+  return binned_layout(p, n_bin_entries, true).total;
+}
+
+extern "C" int gs_isect_tile_encode_binned_packed(
+    const gs_isect_params* p, const int32_t* image_ids, const float* means2d,
+    const int32_t* radii, const float* depths, int64_t n_isects, int64_t n_bin_entries,
+    int64_t* isect_ids, int32_t* flatten_ids, int32_t* tile_offsets, void* workspace,
+    size_t workspace_bytes, gs_stream_t stream) {
+  if (p && p->N > 0 && !image_ids)
+    return invalid("intersect_tile_encode_binned_packed: image_ids required");
+  // (no rows: image_ids may be null; the plain element count I * 0 is 0 too)
+  return encode_binned(p, image_ids, means2d,
+                       radii, depths, nullptr, nullptr, n_isects, n_bin_entries, isect_ids,
+                       flatten_ids, tile_offsets, nullptr, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t gs_pack_visible_workspace_size(int64_t n_elements) {
+  return n_elements <= 0 ? 256 : align256(8 * (size_t)ceil_div(n_elements, kScanChunk)) + 256;
+}
+
+extern "C" int gs_pack_visible(int64_t n_elements, int32_t N, const int32_t* radii,
+                               const float* means2d, const float* depths, const float* conics,
+                               const float* compensations, int64_t capacity, int32_t* image_ids,
+                               int32_t* gaussian_ids, int32_t* p_radii, float* p_means2d,
+                               float* p_depths, float* p_conics, float* p_compensations,
+                               int64_t* nnz_device, void* workspace, size_t workspace_bytes,
+                               gs_stream_t stream) {
+  if (n_elements < 0 || N <= 0 || (n_elements % N) != 0 || capacity < 0 || !nnz_device)
+    return invalid("pack_visible: bad sizes");
+  cudaStream_t s = as_stream(stream);
+  if (n_elements == 0) {
+    if (cudaMemsetAsync(nnz_device, 0, sizeof(int64_t), s) != cudaSuccess)
+      return launch_status("pack_visible");
+    return GS_OK;
+  }
+  if (!radii || !means2d || !depths || !conics ||
+      (capacity > 0 && (!image_ids || !gaussian_ids || !p_radii || !p_means2d || !p_depths ||
+                        !p_conics || (compensations && !p_compensations))))
+    return invalid("pack_visible: missing buffer");
+  if (!workspace || workspace_bytes < gs_pack_visible_workspace_size(n_elements)) {
+    set_error("pack_visible: workspace of %zu bytes needed",
+              gs_pack_visible_workspace_size(n_elements));
+    return GS_ERR_WORKSPACE;
+  }
+  const int64_t nb = ceil_div(n_elements, kScanChunk);
+  int64_t* sums = static_cast<int64_t*>(workspace);
+  visible_count_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(n_elements, radii, sums);
+  scan_sums_kernel<<<1, 1024, 0, s>>>(nb, sums, nnz_device);
+  const PackArgs a{n_elements, capacity, N, radii, means2d, depths, conics,
+                   compensations, image_ids, gaussian_ids, p_radii, p_means2d, p_depths,
+                   p_conics, compensations ? p_compensations : nullptr};
+  pack_rows_kernel<<<(unsigned)nb, kScanThreads, 0, s>>>(a, sums);
+  return launch_status("pack_visible");
 }
 
 extern "C" int gs_isect_tile_encode_binned_check(int64_t n_bin_entries, const void* workspace,

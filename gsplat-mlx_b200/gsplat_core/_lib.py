@@ -117,6 +117,11 @@ SIGNATURES = {
                                                       _vp]),
     "gs_isect_tile_encode_binned_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_store_to_host_i64": (ct.c_int, [_vp, _vp, _i32, _vp]),
+    "gs_pack_visible_workspace_size": (_sz, [_i64]),
+    "gs_pack_visible": (ct.c_int, [_i64, _i32] + [_vp] * 5 + [_i64] + [_vp] * 9 + [_sz, _vp]),
+    "gs_isect_tile_encode_binned_packed_workspace_size": (_sz, [_P(IsectParams), _i64]),
+    "gs_isect_tile_encode_binned_packed": (ct.c_int, [_P(IsectParams), _vp, _vp, _vp, _vp, _i64,
+                                                      _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "gs_isect_sort_check": (ct.c_int, [_i64, _vp, _vp]),
     "gs_isect_sort_workspace_size": (_sz, [_i64]),
     "gs_isect_sort": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),

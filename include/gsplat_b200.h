@@ -286,6 +286,46 @@ int gs_isect_tile_encode_binned_culled(const gs_isect_params* p, const float* me
                                        void* workspace, size_t workspace_bytes,
                                        gs_stream_t stream);
 
+/* Packed [nnz] layout -- the upstream-gsplat form the reference refuses
+ * ("intersect_tile packed path is not implemented yet",
+ * gsplat_intersect.cpp:115-118, image_ids / gaussian_ids inputs of
+ * intersect_tile_forward).
+ *
+ * gs_pack_visible: the visible (both radii > 0) entries of a dense
+ * projection output [n_elements = I*N] as rows in (image, Gaussian) order:
+ * image_ids, gaussian_ids [nnz], radii [nnz,2], means2d [nnz,2], depths
+ * [nnz], conics [nnz,3], compensations [nnz] (when given).  *nnz_device gets
+ * the row count; rows past `capacity` are not written (size the outputs
+ * with a first call of capacity 0, or with an upper bound).  Workspace:
+ * gs_pack_visible_workspace_size(n_elements) bytes.
+ *
+ * gs_isect_tile_encode_binned_packed: the binned encode over nnz packed
+ * rows (p->N = nnz, p->I = images): element i's image is image_ids[i],
+ * which must lie in [0, I); flatten_ids are row indices.  n_isects /
+ * n_bin_entries come from gs_isect_tile_count_totals over the rows (I = 1,
+ * N = nnz: the counts do not depend on the image).  The rasterizer entries
+ * render packed rows as they are (pass N = 0 so that they do not size
+ * anything by I * N, and zero the gradient buffers first). */
+size_t gs_pack_visible_workspace_size(int64_t n_elements);
+int gs_pack_visible(int64_t n_elements, int32_t N, const int32_t* radii,
+                    const float* means2d, const float* depths,
+                    const float* conics, const float* compensations,
+                    int64_t capacity, int32_t* image_ids, int32_t* gaussian_ids,
+                    int32_t* p_radii, float* p_means2d, float* p_depths,
+                    float* p_conics, float* p_compensations,
+                    int64_t* nnz_device, void* workspace, size_t workspace_bytes,
+                    gs_stream_t stream);
+size_t gs_isect_tile_encode_binned_packed_workspace_size(const gs_isect_params* p,
+                                                         int64_t n_bin_entries);
+int gs_isect_tile_encode_binned_packed(const gs_isect_params* p,
+                                       const int32_t* image_ids,
+                                       const float* means2d, const int32_t* radii,
+                                       const float* depths, int64_t n_isects,
+                                       int64_t n_bin_entries, int64_t* isect_ids,
+                                       int32_t* flatten_ids, int32_t* tile_offsets,
+                                       void* workspace, size_t workspace_bytes,
+                                       gs_stream_t stream);
+
 /* The radix passes of the calls above and below wait on one another's
  * tiles with bounded waits; a wait that gives up (a defect, not a workload
  * condition) raises an error word in the workspace and the kernels finish

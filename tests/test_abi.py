@@ -114,6 +114,13 @@ def test_binned_encode_and_densify_validate_before_device_work(gs):
     sp = L.SpzParams(4, 0, 0, 0, 0, 0, 0, 0)
     assert lib.gs_spz_attributes(ct.byref(sp), *([None] * 13)) == L.GS_ERR_INVALID
     assert b"missing buffer" in lib.gs_last_error()
+    # packed rows: sizes must split into whole images; the encode needs image ids
+    assert lib.gs_pack_visible(10, 3, *([None] * 5), 0, *([None] * 7), None, None, 0,
+                               None) == L.GS_ERR_INVALID
+    assert lib.gs_isect_tile_encode_binned_packed(ct.byref(p), None, None, None, None, 5, 5,
+                                                  None, None, None, None, 0, None) == \
+        L.GS_ERR_INVALID
+    assert b"image_ids" in lib.gs_last_error()
     # the host store of a few totals is bounded and needs both buffers
     assert lib.gs_store_to_host_i64(None, None, 2000, None) == L.GS_ERR_INVALID
     assert lib.gs_store_to_host_i64(None, None, 2, None) == L.GS_ERR_INVALID
