@@ -187,6 +187,8 @@ def algorithmic_bytes(stage, n, visible, m, pixels, K, slots, kept=None):
         # offsets out (the binned encode writes the offsets itself)
         "isect_encode_sort": n * (8 + 8 + 4) + mk * 12 + slots * 4,
         "isect_offset": m * 8,
+        # opacity in, its two sigma bounds out
+        "sigma_bounds": n * (4 + 8),
         # per intersection: flatten id + Gaussian record; per pixel: outputs
         "rasterize_fwd": mk * 40 + pixels * 20,
         "rasterize_bwd": mk * (40 + 36) + pixels * 20,
@@ -216,7 +218,8 @@ def our_kernel_launches(entry_passes, bins, slots, tile_cull=False):
     scan = lambda n: 1 if n <= 16384 else 3  # noqa: E731
     binned = (3 + 1 + entry_passes + 1 + 1 + scan(bins) + 1 + 1 + scan(slots) + int(tile_cull)
               + 1)
-    return 1 + 1 + 1 + binned + 1 + 1 + 1 + 1
+    # + the sigma bounds of the opacities 1
+    return 1 + 1 + 1 + 1 + binned + 1 + 1 + 1 + 1
 
 
 # ------------------------------------------------------------------ CPU arms

@@ -594,6 +594,7 @@ struct PassArgs {
   uint64_t* state;
   uint32_t* error_word;
   const int64_t* n_dev;  // when set, the length is *n_dev (the grid covers n)
+  uint32_t spin_limit;   // polls of one look-back wait before it gives up
 };
 
 __device__ __forceinline__ uint64_t load_state(const uint64_t* p) {
@@ -715,7 +716,7 @@ __global__ void __launch_bounds__(kSortThreads, 3) radix_onesweep_kernel(const P
         uint64_t v = w[i];
         uint32_t spins = 0;
         while ((v & ~0xFFFFFFFFull) != tag_agg && (v & ~0xFFFFFFFFull) != tag_inc) {
-          if (++spins > kSpinLimit) {
+          if (++spins > a.spin_limit) {
             atomicOr(a.error_word, 1u);
             v = tag_inc;  // give up: count 0, stop walking
             break;
@@ -845,6 +846,7 @@ void sort_passes(int64_t n, int begin_bit, int end_bit, int in, int out, const u
   a.state = reinterpret_cast<uint64_t*>(ws + L.state);
   a.error_word = reinterpret_cast<uint32_t*>(ws + L.err);
   a.n_dev = n_dev;
+  a.spin_limit = kSpinLimit;
   int src = in;
   for (int pass = 0; pass < passes; ++pass) {
     const bool last = pass == passes - 1;
@@ -1125,6 +1127,7 @@ struct FinishArgs {
   const float* means2d;    // culled encode only
   const float* conics;     // null: no culling
   const float* opacities;
+  int32_t opac_n;          // > 0: opacities are [opac_n], element e reads e mod opac_n
   int32_t* bin_start;
   uint32_t* masks;
 };
@@ -1147,7 +1150,7 @@ __global__ void __launch_bounds__(256) bin_finish_kernel(const FinishArgs a) {
       if (a.conics && m) {
         const float2 mu = __ldg(reinterpret_cast<const float2*>(a.means2d) + e);
         const float c0 = __ldg(a.conics + (int64_t)e * 3), c1 = __ldg(a.conics + (int64_t)e * 3 + 1);
-        const float c2 = __ldg(a.conics + (int64_t)e * 3 + 2), o = __ldg(a.opacities + e);
+        const float c2 = __ldg(a.conics + (int64_t)e * 3 + 2), o = __ldg(a.opacities + (a.opac_n > 0 ? e % a.opac_n : e));
         m = bin_hit_mask(m, mu.x - ((float)(tx0 * a.ts) + 0.5f),
                          mu.y - ((float)(ty0_ * a.ts) + 0.5f), c0, c1, c2, o, a.ts);
       }
@@ -1828,7 +1831,8 @@ static int encode_binned(const gs_isect_params* p, const int32_t* image_ids,
                 V(L.svals), ws + L.sort, s, false, nullptr, nullptr, /*signed_keys=*/false);
     const FinishArgs fa{n_bin_entries, n, g.total, g.per_image, g.sw, dbits, p->tile_size,
                         K(L.skeys), V(L.svals), R(L.rects), means2d, conics, opacities,
-                        V(L.bstart), reinterpret_cast<uint32_t*>(ws + L.masks)};
+                        p->shared_opacities ? p->N : 0, V(L.bstart),
+                        reinterpret_cast<uint32_t*>(ws + L.masks)};
     bin_finish_kernel<<<grid_for(n_bin_entries, 256), 256, 0, s>>>(fa);
   } else {
     cudaMemsetAsync(ws + L.bstart, 0, 4 * (size_t)(g.total + 1), s);
@@ -2029,8 +2033,79 @@ extern "C" int gs_isect_sort_noalloc(int64_t n_isects, int32_t key_bits,
     scratch = g_noalloc_scratch_ptr[dev];
   }
   // Every scratch byte the sort reads is written earlier in the same call
+  // (the error word and the per-call region are cleared by gs_isect_sort)
   // (per-tile digit counts, scan block sums, ping-pong key/value buffers), so
   // nothing needs clearing between calls.
   return gs_isect_sort(n_isects, key_bits, isect_ids, flatten_ids, sorted_isect_ids,
                        sorted_flatten_ids, scratch, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int gs_isect_sort_noalloc_check(int64_t n_isects, gs_stream_t stream) {
+  if (n_isects <= 0) return GS_OK;
+  if (n_isects > kNoAllocMaxIsects)
+    return invalid("intersect_tile_sort_noalloc_check: more intersections than the sort takes");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return invalid("intersect_tile_sort_noalloc_check: no usable current device");
+  }
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  if (!scratch) return GS_OK;  // no sort ran on this device yet
+  return read_sort_error(n_isects, static_cast<const char*>(scratch), as_stream(stream));
+}
+
+namespace gsb {
+namespace {
+__global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
+}  // namespace
+}  // namespace gsb
+
+extern "C" int gs_isect_sort_wait_selftest(int64_t n_isects, const int64_t* isect_ids,
+                                           const int32_t* flatten_ids, int64_t* sorted_isect_ids,
+                                           int32_t* sorted_flatten_ids, void* workspace,
+                                           size_t workspace_bytes, uint32_t spin_limit,
+                                           gs_stream_t stream) {
+  if (n_isects <= kSortTile || n_isects > 2 * kSortTile)
+    return invalid("intersect_sort_wait_selftest: n_isects must be in (4096, 8192]");
+  if (spin_limit < 1 || spin_limit > 1024)
+    return invalid("intersect_sort_wait_selftest: spin_limit must be in 1..1024");
+  if (!isect_ids || !flatten_ids || !sorted_isect_ids || !sorted_flatten_ids)
+    return invalid("intersect_sort_wait_selftest: missing buffer");
+  const SortLayout L = sort_layout(n_isects);
+  if (!workspace || workspace_bytes < L.total) {
+    set_error("intersect_sort_wait_selftest: workspace of %zu bytes needed", L.total);
+    return GS_ERR_WORKSPACE;
+  }
+  cudaStream_t s = as_stream(stream);
+  char* ws = static_cast<char*>(workspace);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(ws + L.hist);
+  cudaMemsetAsync(ws + L.err, 0, sizeof(uint32_t), s);
+  cudaMemsetAsync(ws + L.hist, 0, L.total - L.hist, s);
+  const uint64_t* keys = reinterpret_cast<const uint64_t*>(isect_ids);
+  const uint64_t flip = 0ull;
+  radix_hist_kernel<<<grid_for(ceil_div(n_isects, 4), 256, 2), 256, 0, s>>>(
+      n_isects, keys, 0, 1, flip, nullptr, hist);
+  uint32_t* counter = reinterpret_cast<uint32_t*>(ws + L.ctrl);
+  // the one CTA claims tile 1: tile 0 never runs, so its state stays unpublished
+  set_u32_kernel<<<1, 1, 0, s>>>(counter, 1u);
+  PassArgs a{};
+  a.n = n_isects;
+  a.keys_in = keys;
+  a.vals_in = flatten_ids;
+  a.keys_out = reinterpret_cast<uint64_t*>(sorted_isect_ids);
+  a.vals_out = sorted_flatten_ids;
+  a.shift = 0;
+  a.flip = flip;
+  a.pass = 0;
+  a.pass_hist = hist;
+  a.tile_counter = counter;
+  a.state = reinterpret_cast<uint64_t*>(ws + L.state);
+  a.error_word = reinterpret_cast<uint32_t*>(ws + L.err);
+  a.spin_limit = spin_limit;
+  launch_pass(kKV, kKV, 1, a, s);
+  return launch_status("intersect_sort_wait_selftest");
 }

@@ -27,11 +27,126 @@ constexpr float kMaxAlpha = 0.99f;
 constexpr float kTransmittanceThreshold = 1.0e-4f;
 constexpr float kMinOneMinusAlpha = 1.0e-6f;
 constexpr int kMaxChannels = 64;
+// last_ids mark of a pixel the forward kernels leave to raster_fix_kernel
+// (a real last id is >= 0).
+constexpr int32_t kUndecided = -1;
 
-// sigma = 0.5 (c0 dx^2 + c2 dy^2) + c1 dx dy with one fixed rounding
-// sequence (explicit intrinsics, which the compiler does not re-contract):
-// every forward and backward kernel then makes the same alpha decision for
-// the same pixel and Gaussian.  c0 dx and c2 dy are returned for reuse.
+// Exact decisions.  The reference decides with std::exp (glibc expf) on its
+// own fp32 sigma: skip when sigma < 0 or o e^-sigma < 1/255, clamp alpha at
+// 0.99, stop when T (1 - alpha) <= 1e-4.  Here:
+//
+// * sigma is the reference's float (gauss_sigma below).
+// * The skip and clamp decisions compare sigma with two bounds that depend on
+//   the opacity alone (sigma_bounds below): f(sigma) = o (x) e^-sigma, with the
+//   exponential correctly rounded and (x) a float multiply, is non-increasing
+//   in sigma, so "f >= 1/255" is "sigma <= keep" and "f <= 0.99" is
+//   "sigma >= clamp" for two floats found once per Gaussian.  No exponential
+//   is evaluated for a decision inside the pixel loops.
+// * The stop test sees the fast T (alpha from __expf, T - T alpha with one
+//   rounding).  Each pixel carries a bound E on |T_fast - T_reference|: per
+//   composited step E becomes E (1 - alpha) + T_prev alpha d + T_next kStepErr,
+//   with d = kAlphaErr0 + kAlphaErrS max(keep, 0) bounding the relative alpha
+//   error of the Gaussian's pairs, whose sigma is at most its keep bound
+//   (__expf is within 2 + floor(1.173 |x|) ulp; the correctly rounded e
+//   within half an ulp; the product rounds once; zero for a clamped alpha,
+//   which is exact) and kStepErr the three roundings between the two
+//   recurrences.  A pixel
+//   whose next T lies within E of 1e-4 is marked and recomputed exactly by
+//   one warp at the end of the tile (exact_walk).
+constexpr float kAlphaErrS = 1.4e-7f;  // per unit of sigma: 1.173 ulp
+constexpr float kAlphaErr0 = 4.2e-7f;  // 2 ulp of __expf, 0.5 of the rounded e, 1 of the product
+constexpr float kStepErr = 2.0e-7f;    // three roundings of 2^-24
+
+// e^x correctly rounded to float: CUDA's double exponential (under one
+// double ulp of error) rounded once.  glibc's expf, which the reference
+// calls, returns the same float on all but 7.7e-5 of the floats in
+// [-16, 0] (exhaustive comparison), and there by one ulp, which moves a
+// decision only when the product o e^-sigma itself sits on a threshold.
+__device__ __noinline__ float exp_cr(float x) { return __double2float_rn(exp((double)x)); }
+
+__device__ __forceinline__ float next_up(float x) { return nextafterf(x, INFINITY); }
+__device__ __forceinline__ float next_down(float x) { return nextafterf(x, -INFINITY); }
+
+// The decision bounds of opacity o: keep = the largest float sigma with
+// o (x) CR(e^-sigma) >= 1/255 (-inf when none: the Gaussian is never
+// composited), clamp = the smallest float sigma with o (x) CR(e^-sigma) <= 0.99
+// (-inf when every sigma >= 0 qualifies: never clamped).  A pair at sigma
+// (with sigma >= 0, or -0) is composited iff !(sigma > keep) and has
+// alpha = 0.99 iff sigma < clamp, exactly as the reference decides it with
+// CR(exp).  NaN or +inf opacities: the reference's std::min(0.99f, NaN)
+// yields 0.99, so every pair is composited and clamped (both bounds +inf).
+//
+// With e_min the smallest float e with o (x) e >= 1/255 and m the midpoint
+// between e_min and the float below it, CR(e^-sigma) >= e_min exactly when
+// e^-sigma > m (a tie is impossible for the exponential of a float), i.e.
+// sigma < -ln m: keep is -ln m rounded down to a float.  The double
+// logarithm gives -ln m rounded to nearest; one double exponential tells
+// whether that float lies above the root (then the float below is keep).
+// The clamp bound is the mirror image with the midpoint above e_max.
+__device__ __forceinline__ float root_down(double m) {  // largest float s with e^-s > m
+  float s = __double2float_rn(-log(m));
+  if (!(exp(-(double)s) > m)) s = next_down(s);
+  return s;
+}
+__device__ __forceinline__ float root_up(double m) {  // smallest float s with e^-s < m
+  float s = __double2float_rn(-log(m));
+  if (!(exp(-(double)s) < m)) s = next_up(s);
+  return s;
+}
+
+__device__ __noinline__ float2 sigma_bounds(float o) {
+  if (!(o < INFINITY)) return make_float2(INFINITY, INFINITY);
+  float2 b = make_float2(-INFINITY, -INFINITY);
+  if (!(o > 0.0f)) return b;
+  // smallest e with o (x) e >= 1/255
+  float e = __fdiv_rn(kAlphaThreshold, o);
+  for (int i = 0; i < 8 && __fmul_rn(o, e) < kAlphaThreshold; ++i) e = next_up(e);
+  for (int i = 0; i < 8 && e > 0.0f && __fmul_rn(o, next_down(e)) >= kAlphaThreshold; ++i)
+    e = next_down(e);
+  if (e <= 1.0f) b.x = fmaxf(root_down(0.5 * ((double)e + (double)next_down(e))), 0.0f);
+  // largest e with o (x) e <= 0.99
+  if (o > kMaxAlpha) {
+    e = __fdiv_rn(kMaxAlpha, o);
+    for (int i = 0; i < 8 && __fmul_rn(o, e) > kMaxAlpha; ++i) e = next_down(e);
+    for (int i = 0; i < 8 && __fmul_rn(o, next_up(e)) <= kMaxAlpha; ++i) e = next_up(e);
+    if (e < 1.0f) b.y = fmaxf(root_up(0.5 * ((double)e + (double)next_up(e))), 0.0f);
+  }
+  return b;
+}
+
+// The stop decision of the fast path for a pixel whose fast T after this
+// step is next_T, E its error bound: 0 continue, 1 stop, 2 undecided
+// (within E of 1e-4: recompute the pixel exactly).
+__device__ __forceinline__ int stop_decision(float next_T, float E) {
+  if (next_T > fmaf(E, 1.0625f, kTransmittanceThreshold + 1.0e-12f)) return 0;
+  return next_T > fmaf(E, -1.0625f, kTransmittanceThreshold - 1.0e-12f) ? 2 : 1;
+}
+
+// E after a step from Tr with alpha (vis = alpha Tr, oma = 1 - alpha); a
+// clamped alpha (exactly 0.99) adds no alpha error.
+// d: the relative alpha error bound of the Gaussian, alpha_err(keep) (its
+// composited pairs have sigma <= keep).
+__device__ __forceinline__ float step_bound(float E, float vis, float oma, float next_T,
+                                            float d, bool clamped) {
+  return fmaf(E, oma, fmaf(vis, clamped ? 0.0f : d, next_T * kStepErr));
+}
+
+// The relative error bound of the fast alpha of a Gaussian with keep bound sk.
+__device__ __forceinline__ float alpha_err(float sk) {
+  return fmaf(fmaxf(sk, 0.0f), kAlphaErrS, kAlphaErr0);
+}
+
+// The fast path's alpha of a composited pair: exactly 0.99 when clamped,
+// else o __expf(-sigma) (within the alpha error of step_bound).
+__device__ __forceinline__ float fast_alpha(float sigma, float o, bool clamped) {
+  return clamped ? kMaxAlpha : fminf(kMaxAlpha, __fmul_rn(o, __expf(-sigma)));
+}
+
+// The reference's sigma = 0.5f * (c0 * dx * dx + c2 * dy * dy) + c1 * dx * dy
+// (gsplat_rasterize.cpp:333-334, 474-475), evaluated in its order with one
+// IEEE rounding per operation (explicit intrinsics, which the compiler does
+// not contract), so that every kernel here gets the reference's float.
+// c0 dx and c2 dy are returned for reuse by the backward.
 struct Sigma {
   float cdx, cdy, s;
 };
@@ -40,14 +155,20 @@ __device__ __forceinline__ Sigma gauss_sigma(float dx, float dy, float c0, float
   Sigma r;
   r.cdx = __fmul_rn(c0, dx);
   r.cdy = __fmul_rn(c2, dy);
-  const float q = __fmaf_rn(r.cdx, dx, __fmul_rn(r.cdy, dy));
-  r.s = __fmaf_rn(__fmul_rn(c1, dx), dy, __fmul_rn(0.5f, q));
+  const float q = __fadd_rn(__fmul_rn(r.cdx, dx), __fmul_rn(r.cdy, dy));
+  r.s = __fadd_rn(__fmul_rn(0.5f, q), __fmul_rn(__fmul_rn(c1, dx), dy));
   return r;
+}
+
+// Composited (reference: !(sigma < 0 || alpha < 1/255)) for keep bound sk.
+__device__ __forceinline__ bool composited(float sigma, float sk) {
+  return !(sigma < 0.0f) && !(sigma > sk);
 }
 
 struct RArgs {
   int I, N, CH, W, H, ts, tw, th;
   int ty0, rows;  // tile rows [ty0, ty0 + rows) are rendered (all: 0, th)
+  int opac_shared;  // opacities / v_opacities are [N]: entry g reads g mod N
   int64_t n_isects;
   const float* means2d;
   const float* conics;
@@ -57,7 +178,18 @@ struct RArgs {
   const uint8_t* masks;
   const int32_t* tile_offsets;
   const int32_t* flatten_ids;
+  const float2* sbounds;  // per opacity entry: (keep, clamp) of sigma_bounds; null: computed
 };
+
+// Index of entry g's opacity (and opacity gradient).
+__device__ __forceinline__ int64_t opac_index(const RArgs& a, int64_t g) {
+  return a.opac_shared ? g % a.N : g;
+}
+
+// (keep, clamp) sigma bounds of entry g with opacity o.
+__device__ __forceinline__ float2 entry_bounds(const RArgs& a, int64_t g, float o) {
+  return a.sbounds ? __ldg(a.sbounds + opac_index(a, g)) : sigma_bounds(o);
+}
 
 // The CTA's tile: `slot` indexes tile_offsets ([I, rows, tw]), `mask` the
 // masks ([I, th, tw]).
@@ -85,6 +217,145 @@ __device__ __forceinline__ void tile_range(const RArgs& a, int64_t slot, int& st
   end = (slot + 1 == n_slots) ? (int)a.n_isects : __ldg(a.tile_offsets + slot + 1);
 }
 
+// The CTA recomputes the pixel `pix` of `image`, centred at (px, py), whose
+// tile list is [start, end), exactly as the reference does
+// (gsplat_rasterize.cpp:320-357), and writes its outputs: the reference's
+// sigma, its decisions (sigma bounds), alpha from the correctly rounded
+// exponential, and T (1 - alpha), alpha T and the colour sums with one
+// rounding per operation in list order.  Per chunk of kWalk entries (one
+// per thread; the next chunk's loads are issued before this one is folded)
+// the composited entries are compacted in list order into shared memory
+// with their colours, thread 0 folds them into T in order (stopping where
+// the reference stops), and thread c sums channel c (and c + kWalk) over
+// the folded entries in order.  The longest walk bounds the fix-up
+// kernel's time, so a walk gets every thread of the CTA.
+constexpr int kWalk = 256;
+
+struct WalkSmem {
+  float al[kWalk];       // alpha of the kept entries, in list order
+  int g[kWalk];          // their Gaussian
+  int ix[kWalk];         // their list index
+  float vis[kWalk];      // alpha T of the folded ones
+  float col[kWalk][4];   // their colours (CH in 1..4)
+  int wcnt[kWalk / 32];  // kept entries per warp
+  float T;
+  int cur, nfold, stop;
+};
+
+template <int CH>
+__device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int image, int64_t pix,
+                                        float px, float py, WalkSmem& w, float* render_colors,
+                                        float* render_alphas, int32_t* last_ids) {
+  const int ch = CH > 0 ? CH : a.CH;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    w.T = 1.0f;
+    w.cur = 0;
+    w.stop = 0;
+  }
+  float acc0 = 0.0f, acc1 = 0.0f;  // channels tid and tid + kWalk (<= 64)
+  int g = 0;
+  float2 m = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
+  float c0 = 0.f, c1 = 0.f, c2 = 0.f, o = 0.f;
+  auto load = [&](int cb) {
+    const int idx = cb + tid;
+    if (idx < end) {
+      g = __ldg(a.flatten_ids + idx);
+      m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+      const float* con = a.conics + (int64_t)g * 3;
+      c0 = __ldg(con);
+      c1 = __ldg(con + 1);
+      c2 = __ldg(con + 2);
+      o = __ldg(a.opacities + opac_index(a, g));
+      if (a.sbounds) sb = __ldg(a.sbounds + opac_index(a, g));
+    }
+  };
+  load(start);
+  for (int cb = start; cb < end; cb += kWalk) {
+    const int idx = cb + tid;
+    bool take = false;
+    float al = 0.0f;
+    const int gk = g;
+    if (idx < end) {
+      const float sigma = gauss_sigma(__fsub_rn(m.x, px), __fsub_rn(m.y, py), c0, c1, c2).s;
+      if (!a.sbounds) sb = sigma_bounds(o);
+      take = composited(sigma, sb.x);
+      if (take) al = sigma < sb.y ? kMaxAlpha : fminf(kMaxAlpha, __fmul_rn(o, exp_cr(-sigma)));
+    }
+    if (cb + kWalk < end) load(cb + kWalk);  // in flight during the fold
+    const unsigned bal = __ballot_sync(0xffffffffu, take);
+    if (lane == 0) w.wcnt[warp] = __popc(bal);
+    __syncthreads();
+    int base = 0, cnt = 0;
+#pragma unroll
+    for (int i = 0; i < kWalk / 32; ++i) {
+      const int c = w.wcnt[i];
+      base += i < warp ? c : 0;
+      cnt += c;
+    }
+    if (take) {
+      const int slot = base + __popc(bal & ((1u << lane) - 1u));
+      w.al[slot] = al;
+      w.g[slot] = gk;
+      w.ix[slot] = idx;
+      if (CH > 0) {
+#pragma unroll
+        for (int c = 0; c < (CH > 0 ? CH : 1); ++c)
+          w.col[slot][c] = __ldg(a.colors + (int64_t)gk * ch + c);
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float T = w.T;
+      int k = 0, cur = w.cur;
+      for (; k < cnt; ++k) {
+        const float ak = w.al[k];
+        const float nT = __fmul_rn(T, __fsub_rn(1.0f, ak));
+        if (nT <= kTransmittanceThreshold) {
+          w.stop = 1;
+          break;
+        }
+        w.vis[k] = __fmul_rn(ak, T);
+        cur = w.ix[k];
+        T = nT;
+      }
+      w.T = T;
+      w.cur = cur;
+      w.nfold = k;
+    }
+    __syncthreads();
+    const int nf = w.nfold;
+    if (CH > 0) {
+      if (tid < CH)
+        for (int k = 0; k < nf; ++k) acc0 = __fadd_rn(acc0, __fmul_rn(w.col[k][tid], w.vis[k]));
+    } else {
+      for (int k = 0; k < nf; ++k) {
+        const float vis = w.vis[k];
+        const int64_t gq = w.g[k];
+        if (tid < ch) acc0 = __fadd_rn(acc0, __fmul_rn(__ldg(a.colors + gq * ch + tid), vis));
+        if (tid + kWalk < ch)
+          acc1 = __fadd_rn(acc1, __fmul_rn(__ldg(a.colors + gq * ch + tid + kWalk), vis));
+      }
+    }
+    const bool stop = w.stop != 0;
+    __syncthreads();  // the arrays are refilled by the next chunk
+    if (stop) break;
+  }
+  const float T = w.T;
+  for (int j = 0; j < 2; ++j) {
+    const int c = tid + j * kWalk;
+    if (c < ch) {
+      const float bg = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
+      render_colors[pix * ch + c] = __fadd_rn(j ? acc1 : acc0, __fmul_rn(T, bg));
+    }
+  }
+  if (tid == 0) {
+    render_alphas[pix] = __fsub_rn(1.0f, T);
+    last_ids[pix] = w.cur;
+  }
+  __syncthreads();  // w serves the next pixel
+}
+
 // ------------------------------------------------------------------ forward
 // CH > 0: channel count known at compile time (colours staged in smem and
 // accumulated in registers); CH == 0: runtime channel count up to 64.
@@ -97,7 +368,8 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   const int ch = CH > 0 ? CH : a.CH;
   float2* s_xy = reinterpret_cast<float2*>(smem);
   float4* s_co = reinterpret_cast<float4*>(smem + 2 * BLOCK);  // conic xyz, opacity
-  float* s_col = smem + 6 * BLOCK;                              // [BLOCK][ch]
+  float2* s_sb = reinterpret_cast<float2*>(smem + 6 * BLOCK);  // sigma bounds
+  float* s_col = smem + 8 * BLOCK;                              // [BLOCK][ch]
 
   const TileIdx ti = tile_of(a);
   const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
@@ -121,7 +393,8 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   const float px = (float)x + 0.5f, py = (float)y + 0.5f;
   float Tr = 1.0f;
   int cur = 0;
-  bool done = !inside;
+  bool done = !inside, unsure = false;
+  float E = 0.0f;  // bound on |Tr - the reference's T|
   float acc[CH > 0 ? CH : 1];
 #pragma unroll
   for (int c = 0; c < (CH > 0 ? CH : 1); ++c) acc[c] = 0.0f;
@@ -133,9 +406,11 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
     const int idx = b0 + tid;
     if (idx < end) {
       const int g = __ldg(a.flatten_ids + idx);
+      const float o = __ldg(a.opacities + opac_index(a, g));
       s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
       s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
-                              __ldg(a.conics + (int64_t)g * 3 + 2), __ldg(a.opacities + g));
+                              __ldg(a.conics + (int64_t)g * 3 + 2), o);
+      s_sb[tid] = entry_bounds(a, g, o);
       for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
     }
     __syncthreads();
@@ -143,16 +418,21 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
     for (int j = 0; j < cnt && !done; ++j) {
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
+      const float2 sb = s_sb[j];
       const float dx = m.x - px, dy = m.y - py;
       const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
-      const float alpha = fminf(kMaxAlpha, __fmul_rn(co.w, __expf(-sigma)));
-      if (sigma < 0.0f || alpha < kAlphaThreshold) continue;
-      const float next_T = Tr * (1.0f - alpha);
-      if (next_T <= kTransmittanceThreshold) {
+      if (!composited(sigma, sb.x)) continue;
+      const bool clamped = !(sigma >= sb.y);  // o e^-sigma > 0.99 (or NaN)
+      const float alpha = fast_alpha(sigma, co.w, clamped);
+      const float vis = alpha * Tr;
+      const float next_T = __fmaf_rn(-alpha, Tr, Tr);
+      const float nE = step_bound(E, vis, 1.0f - alpha, next_T, alpha_err(sb.x), clamped);
+      if (const int st = stop_decision(next_T, nE)) {
+        unsure = st == 2;
         done = true;
         break;
       }
-      const float vis = alpha * Tr;
+      E = nE;
       if (CH > 0) {
 #pragma unroll
         for (int c = 0; c < (CH > 0 ? CH : 1); ++c) acc[c] += s_col[j * (CH > 0 ? CH : 1) + c] * vis;
@@ -163,7 +443,7 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
       Tr = next_T;
     }
   }
-  if (inside) {
+  if (inside && !unsure) {
     render_alphas[pix] = 1.0f - Tr;
     if (CH > 0) {
 #pragma unroll
@@ -179,6 +459,63 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
     }
     last_ids[pix] = cur;
   }
+  // a pixel whose stop decision fell within the error bound is left to
+  // raster_fix_kernel
+  if (inside && unsure) last_ids[pix] = kUndecided;
+}
+
+// Recomputes exactly the pixels that the forward kernel left undecided
+// (last_ids == kUndecided).  The CTAs scan the rendered rows in row-major
+// order, kFixPixels pixels per CTA (one wave covers an image of millions of
+// pixels), and walk each undecided pixel they find with all their threads
+// (exact_walk).  Kept out of the forward kernels: the walk code there took
+// registers from the compositing loop.
+constexpr int kFixPixels = 4 * kWalk;
+
+template <int CH>
+__global__ void __launch_bounds__(kWalk) raster_fix_kernel(RArgs a,
+                                                           float* __restrict__ render_colors,
+                                                           float* __restrict__ render_alphas,
+                                                           int32_t* __restrict__ last_ids) {
+  __shared__ WalkSmem w;
+  __shared__ int64_t s_list[kFixPixels];
+  __shared__ int s_n;
+  const int tid = threadIdx.x;
+  // the rendered rows: those of tile rows [ty0, ty0 + rows)
+  const int y0 = a.ty0 * a.ts, y1 = min(a.H, (a.ty0 + a.rows) * a.ts);
+  const int64_t per_image = (int64_t)(y1 - y0) * a.W;
+  const int64_t total = (int64_t)a.I * per_image;
+  if (tid == 0) s_n = 0;
+  __syncthreads();
+  const int64_t p0 = (int64_t)blockIdx.x * kFixPixels;
+  for (int k = tid; k < kFixPixels; k += kWalk) {
+    const int64_t p = p0 + k;
+    if (p >= total) break;
+    const int64_t image = p / per_image, r = p - image * per_image;
+    const int64_t pix = (image * a.H + y0) * a.W + r;
+    if (__ldg(last_ids + pix) == kUndecided) s_list[atomicAdd(&s_n, 1)] = pix;
+  }
+  __syncthreads();
+  const int n = s_n;
+  for (int u = 0; u < n; ++u) {
+    const int64_t pix = s_list[u];
+    const int64_t image = pix / ((int64_t)a.H * a.W);
+    const int rem = (int)(pix - image * a.H * a.W);
+    const int y = rem / a.W, x = rem - y * a.W;
+    const int tx = x / a.ts, ty = y / a.ts;
+    const int64_t slot = ((int64_t)image * a.rows + (ty - a.ty0)) * a.tw + tx;
+    int start, end;
+    tile_range(a, slot, start, end);
+    exact_walk<CH>(a, start, end, (int)image, pix, (float)x + 0.5f, (float)y + 0.5f, w,
+                   render_colors, render_alphas, last_ids);
+  }
+}
+
+// CTAs of raster_fix_kernel.
+inline unsigned fix_grid(const RArgs& a) {
+  const int y0 = a.ty0 * a.ts, y1 = a.H < (a.ty0 + a.rows) * a.ts ? a.H : (a.ty0 + a.rows) * a.ts;
+  const int64_t total = (int64_t)a.I * (y1 - y0) * a.W;
+  return (unsigned)(total > 0 ? ceil_div(total, kFixPixels) : 1);
 }
 
 // ------------------------------------------------------------------ backward
@@ -275,7 +612,8 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
   const int NT = 8 + ch;  // gradient terms per Gaussian
   float2* s_xy = reinterpret_cast<float2*>(smem);
   float4* s_co = reinterpret_cast<float4*>(smem + 2 * BLOCK);
-  float* s_col = smem + 6 * BLOCK;         // [BLOCK][ch]
+  float2* s_sb = reinterpret_cast<float2*>(smem + 6 * BLOCK);  // sigma bounds
+  float* s_col = smem + 8 * BLOCK;         // [BLOCK][ch]
   float* s_acc = s_col + BLOCK * ch;       // [BLOCK][NT]
   __shared__ int s_last;
   __shared__ float s_bg[kMaxChannels];
@@ -341,9 +679,11 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
     __syncthreads();
     if (tid < cnt) {
       const int g = __ldg(a.flatten_ids + b0 + tid);
+      const float o = __ldg(a.opacities + opac_index(a, g));
       s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
       s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
-                              __ldg(a.conics + (int64_t)g * 3 + 2), __ldg(a.opacities + g));
+                              __ldg(a.conics + (int64_t)g * 3 + 2), o);
+      s_sb[tid] = entry_bounds(a, g, o);
       for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
     }
     for (int i = tid; i < cnt * NT; i += BLOCK) s_acc[i] = 0.0f;
@@ -352,15 +692,18 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
       const int idx = b0 + j;
       bool valid = idx <= my_last;
       float vis = 0.0f, alpha = 0.0f, dx = 0.0f, dy = 0.0f;
+      bool clamped = false;
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
       if (valid) {
+        const float2 sb = s_sb[j];
         dx = m.x - px;
         dy = m.y - py;
         const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
+        valid = composited(sigma, sb.x);
+        clamped = !(sigma >= sb.y);  // the reference's !(o * vis <= 0.99)
         vis = __expf(-sigma);
-        alpha = fminf(kMaxAlpha, __fmul_rn(co.w, vis));
-        valid = !(sigma < 0.0f || alpha < kAlphaThreshold);
+        alpha = clamped ? kMaxAlpha : fminf(kMaxAlpha, __fmul_rn(co.w, vis));
       }
       if (!__any_sync(0xffffffffu, valid)) continue;
       float g[16];
@@ -390,7 +733,7 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
         }
         v_alpha += T_final * ra * v_ra;
         if (a.backgrounds) v_alpha += -T_final * ra * bg_dot;
-        if (__fmul_rn(co.w, vis) <= kMaxAlpha) {
+        if (!clamped) {
           const float v_sigma = -co.w * vis * v_alpha;
           const float vx = v_sigma * (co.x * dx + co.y * dy);
           const float vy = v_sigma * (co.y * dx + co.z * dy);
@@ -424,7 +767,7 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
       const int64_t gg = __ldg(a.flatten_ids + b0 + j);
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
       else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
-      else if (k == 5) atomicAdd(v_opacities + gg, v);
+      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg), v);
       else if (k < 8) {
         if (absgrad) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);
       } else atomicAdd(v_colors + gg * ch + (k - 8), v);
@@ -454,8 +797,8 @@ constexpr int kT16SmallPixels = 1;
 // index and the Gaussian id.
 template <int CH, int THREADS>
 __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0, float y0,
-                                       float4* sa, float4* sb, float2* sc, int* sidx, int* sgid,
-                                       int* swcnt) {
+                                       float4* sa, float4* sb, float2* sc, float2* sd, int* sidx,
+                                       int* sgid, int* swcnt) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int idx = b0 + tid;
   bool keep = false;
@@ -465,7 +808,7 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
     const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
     const float* con = a.conics + (int64_t)g * 3;
     keep = tile_may_hit(m.x, m.y, __ldg(con), __ldg(con + 1), __ldg(con + 2),
-                        __ldg(a.opacities + g), x0, y0);
+                        __ldg(a.opacities + opac_index(a, g)), x0, y0);
   }
   const unsigned bal = __ballot_sync(0xffffffffu, keep);
   if (lane == 0) swcnt[warp] = __popc(bal);
@@ -486,9 +829,11 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
     float cc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int c = 0; c < CH; ++c) cc[c] = __ldg(col + c);
+    const float o = __ldg(a.opacities + opac_index(a, g));
     sa[slot] = make_float4(m.x, m.y, __ldg(con), __ldg(con + 1));
-    sb[slot] = make_float4(__ldg(con + 2), __ldg(a.opacities + g), cc[0], cc[1]);
+    sb[slot] = make_float4(__ldg(con + 2), o, cc[0], cc[1]);
     sc[slot] = make_float2(cc[2], cc[3]);
+    sd[slot] = entry_bounds(a, g, o);
     sidx[slot] = idx;
     if (sgid) sgid[slot] = g;
   }
@@ -496,23 +841,26 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
   return cnt;
 }
 
+// Returns 0 while the pixel goes on, 1 once it stopped, 2 when its stop
+// decision is left to the exact walk.
 template <int CH>
-__device__ __forceinline__ void composite16(float dx, float dy, const float4& A, const float4& B,
-                                            const float* col, float& Tr, float* acc, int& cur,
-                                            bool& done, int idx) {
+__device__ __forceinline__ int composite16(float dx, float dy, const float4& A, const float4& B,
+                                           float2 sb, float dg, const float* col, float& Tr,
+                                           float& E, float* acc, int& cur, int idx) {
   const float sigma = gauss_sigma(dx, dy, A.z, A.w, B.x).s;
-  const float alpha = fminf(kMaxAlpha, __fmul_rn(B.y, __expf(-sigma)));
-  if (sigma < 0.0f || alpha < kAlphaThreshold) return;
-  const float next_T = Tr * (1.0f - alpha);
-  if (next_T <= kTransmittanceThreshold) {
-    done = true;
-    return;
-  }
+  if (!composited(sigma, sb.x)) return 0;
+  const bool clamped = !(sigma >= sb.y);  // o e^-sigma > 0.99 (or NaN)
+  const float alpha = fast_alpha(sigma, B.y, clamped);
   const float vis = alpha * Tr;
+  const float next_T = __fmaf_rn(-alpha, Tr, Tr);
+  const float nE = step_bound(E, vis, 1.0f - alpha, next_T, dg, clamped);
+  if (const int st = stop_decision(next_T, nE)) return st;
+  E = nE;
 #pragma unroll
   for (int c = 0; c < CH; ++c) acc[c] += col[c] * vis;
   cur = idx;
   Tr = next_T;
+  return 0;
 }
 
 // Both 16x16 kernels are capped at 64 registers (16 CTAs of 64 threads per
@@ -526,6 +874,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   __shared__ float4 s_a[THREADS];
   __shared__ float4 s_b[THREADS];
   __shared__ float2 s_c[THREADS];
+  __shared__ float2 s_d[THREADS];
   __shared__ int s_idx[THREADS];
   __shared__ int s_wcnt[THREADS / 32];
   const TileIdx ti = tile_of(a);
@@ -554,33 +903,30 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   int start, end;
   tile_range(a, ti.slot, start, end);
   const float px = (float)x + 0.5f;
-  float py[P], Tr[P], acc[P][CH];
+  float py[P], Tr[P], tb[P], acc[P][CH];
   int cur[P];
-  bool dn[P];
+  unsigned dn = 0u, uns = 0u;  // bit q: pixel q stopped / left to the exact walk
 #pragma unroll
   for (int q = 0; q < P; ++q) {
     py[q] = (float)(ybase + q * RS) + 0.5f;
     Tr[q] = 1.0f;
+    tb[q] = 0.0f;
     cur[q] = 0;
-    dn[q] = !in[q];
+    dn |= in[q] ? 0u : 1u << q;
 #pragma unroll
     for (int c = 0; c < CH; ++c) acc[q][c] = 0.0f;
   }
-  auto all_done = [&]() {
-    bool d = true;
-#pragma unroll
-    for (int q = 0; q < P; ++q) d = d && dn[q];
-    return d;
-  };
+  auto all_done = [&]() { return dn == (1u << P) - 1u; };
 
   for (int b0 = start; b0 < end; b0 += THREADS) {
     if (__syncthreads_count(!all_done()) == 0) break;
-    const int cnt = stage16<CH, THREADS>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
-                                s_c, s_idx, nullptr, s_wcnt);
+    const int cnt = stage16<CH, THREADS>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a,
+                                         s_b, s_c, s_d, s_idx, nullptr, s_wcnt);
     for (int j = 0; j < cnt; ++j) {
       if (all_done()) break;
       const float4 A = s_a[j];
       const float4 B = s_b[j];
+      const float2 sb = s_d[j];
       float col[4] = {B.z, B.w, 0.0f, 0.0f};
       if (CH > 2) {
         const float2 C = s_c[j];
@@ -589,14 +935,22 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
       }
       const float dx = A.x - px;
       const int idx = s_idx[j];
+      const float dg = alpha_err(sb.x);
 #pragma unroll
       for (int q = 0; q < P; ++q)
-        if (!dn[q]) composite16<CH>(dx, A.y - py[q], A, B, col, Tr[q], acc[q], cur[q], dn[q], idx);
+        if (!(dn >> q & 1u)) {
+          const int st = composite16<CH>(dx, A.y - py[q], A, B, sb, dg, col, Tr[q], tb[q],
+                                         acc[q], cur[q], idx);
+          if (st) {
+            dn |= 1u << q;
+            if (st == 2) uns |= 1u << q;
+          }
+        }
     }
   }
 #pragma unroll
   for (int q = 0; q < P; ++q) {
-    if (!in[q]) continue;
+    if (!in[q] || (uns >> q & 1u)) continue;
     const int64_t pix = pix0 + (int64_t)q * RS * a.W;
     render_alphas[pix] = 1.0f - Tr[q];
 #pragma unroll
@@ -606,6 +960,11 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
     }
     last_ids[pix] = cur[q];
   }
+  // pixels whose stop decision fell within the error bound are left to
+  // raster_fix_kernel
+#pragma unroll
+  for (int q = 0; q < P; ++q)
+    if (uns >> q & 1u) last_ids[pix0 + (int64_t)q * RS * a.W] = kUndecided;
 }
 
 // Reverse step of one pixel for one Gaussian (gsplat_rasterize.cpp:503-562);
@@ -622,14 +981,16 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
 // argument in [0.01, 1]).
 template <int CH, bool ABS>
 __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, const float4& A,
-                                           const float4& B, const float* col, float& Tr,
-                                           float& bufdot, float K, const float* v_rc, float* g) {
+                                           const float4& B, float2 sb, const float* col,
+                                           float& Tr, float& bufdot, float K, const float* v_rc,
+                                           float* g) {
   if (!in_range) return false;
   const Sigma sg = gauss_sigma(dx, dy, A.z, A.w, B.x);
+  if (!composited(sg.s, sb.x)) return false;
+  const bool clamped = !(sg.s >= sb.y);  // the reference's !(o * vis <= 0.99)
   const float vis = __expf(-sg.s);
   const float ov = __fmul_rn(B.y, vis);
-  const float alpha = fminf(kMaxAlpha, ov);
-  if (sg.s < 0.0f || alpha < kAlphaThreshold) return false;
+  const float alpha = clamped ? kMaxAlpha : fminf(kMaxAlpha, ov);
   const float ra = __fdividef(1.0f, fmaxf(kMinOneMinusAlpha, 1.0f - alpha));
   Tr *= ra;
   const float fac = alpha * Tr;
@@ -640,7 +1001,7 @@ __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, co
   for (int c = 0; c < CH; ++c) g[(ABS ? 8 : 6) + c] = fmaf(fac, v_rc[c], g[(ABS ? 8 : 6) + c]);
   const float v_alpha = fmaf(Tr, cdot, ra * (K - bufdot));
   bufdot = fmaf(fac, cdot, bufdot);
-  if (ov <= kMaxAlpha) {
+  if (!clamped) {
     const float v_sigma = -ov * v_alpha;
     const float vsdx = v_sigma * dx, vsdy = v_sigma * dy;
     const float vx = fmaf(A.w, vsdy, v_sigma * sg.cdx);   // v_sigma (c0 dx + c1 dy)
@@ -672,6 +1033,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
   __shared__ float4 s_a[THREADS];
   __shared__ float4 s_b[THREADS];
   __shared__ float2 s_c[THREADS];
+  __shared__ float2 s_d[THREADS];
   __shared__ int s_idx[THREADS];
   __shared__ int s_gid[THREADS];
   __shared__ int s_wcnt[THREADS / 32];
@@ -736,8 +1098,8 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
   for (int b_end = cta_last + 1; b_end > start; b_end -= THREADS) {
     const int b0 = max(start, b_end - THREADS);
     __syncthreads();
-    const int cnt = stage16<CH, THREADS>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a, s_b,
-                                s_c, s_idx, s_gid, s_wcnt);
+    const int cnt = stage16<CH, THREADS>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f,
+                                         s_a, s_b, s_c, s_d, s_idx, s_gid, s_wcnt);
     for (int i = tid; i < cnt * NT; i += THREADS) s_acc[i] = 0.0f;
     __syncthreads();
     for (int j = cnt - 1; j >= 0; --j) {
@@ -754,11 +1116,12 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
 #pragma unroll
       for (int i = 0; i < 16; ++i) g[i] = 0.0f;
       const float dx = A.x - px;
+      const float2 sb = s_d[j];
       bool any = false;
 #pragma unroll
       for (int q = 0; q < P; ++q)
-        any |= backward16<CH, ABS>(idx <= last[q], dx, A.y - py[q], A, B, col, Tr[q], bufdot[q],
-                                   K[q], vrc[q], g);
+        any |= backward16<CH, ABS>(idx <= last[q], dx, A.y - py[q], A, B, sb, col, Tr[q],
+                                   bufdot[q], K[q], vrc[q], g);
       const unsigned active = __ballot_sync(0xffffffffu, any);
       if (!active) continue;
       if (__popc(active) <= 2) {
@@ -792,15 +1155,34 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
       const int64_t gg = s_gid[j];
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
       else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
-      else if (k == 5) atomicAdd(v_opacities + gg, v);
+      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg), v);
       else if (k < CB) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);  // ABS only
       else atomicAdd(v_colors + gg * CH + (k - CB), v);
     }
   }
 }
 
+// Bounds of every opacity; with radii ([cameras, n, 2]) only of the
+// Gaussians some camera sees (no intersection lists the others).
+__global__ void sigma_bounds_kernel(int64_t n, const float* __restrict__ opacities,
+                                    const int2* __restrict__ radii, int cameras,
+                                    float2* __restrict__ bounds) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (radii) {
+      bool seen = false;
+      for (int c = 0; c < cameras && !seen; ++c) {
+        const int2 r = __ldg(radii + (int64_t)c * n + i);
+        seen = r.x > 0 && r.y > 0;
+      }
+      if (!seen) continue;
+    }
+    bounds[i] = sigma_bounds(__ldg(opacities + i));
+  }
+}
+
 int smem_bytes(int block, int ch, bool bwd) {
-  return (int)sizeof(float) * (block * (6 + ch) + (bwd ? block * (8 + ch) : 0));
+  return (int)sizeof(float) * (block * (8 + ch) + (bwd ? block * (8 + ch) : 0));
 }
 
 // Fewer tiles than 8 per SM: the four-pixel kernels' two-warp CTAs would
@@ -818,12 +1200,14 @@ int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cud
     else
       raster_fwd16_kernel<C1, kT16Pixels><<<(unsigned)tiles, 256 / kT16Pixels, 0, s>>>(a, rc, ra,
                                                                                         li);
+    raster_fix_kernel<C1><<<fix_grid(a), kWalk, 0, s>>>(a, rc, ra, li);
     return launch_status("rasterize_fwd");
   }
   const int smem = smem_bytes(block, a.CH, false);
   cudaFuncSetAttribute(raster_fwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
   raster_fwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, rc, ra, li);
+  raster_fix_kernel<CH><<<fix_grid(a), kWalk, 0, s>>>(a, rc, ra, li);
   return launch_status("rasterize_fwd");
 }
 
@@ -889,10 +1273,12 @@ RArgs make_args(const gs_raster_params* p, const float* means2d, const float* co
     rows = p->tile_y1 - p->tile_y0;
   }
   return RArgs{p->I, p->N, p->channels, p->image_width, p->image_height, p->tile_size,
-               p->tile_width, p->tile_height, ty0, rows, p->n_isects, means2d, conics, colors,
+               p->tile_width, p->tile_height, ty0, rows, p->shared_opacities ? 1 : 0,
+               p->n_isects, means2d, conics, colors,
                opacities,
                p->use_backgrounds ? backgrounds : nullptr, p->use_masks ? masks : nullptr,
-               tile_offsets, flatten_ids};
+               tile_offsets, flatten_ids,
+               reinterpret_cast<const float2*>(p->sigma_bounds)};
 }
 
 }  // namespace
@@ -916,6 +1302,8 @@ extern "C" int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,
   if ((p->use_backgrounds && !backgrounds) || (p->use_masks && !masks))
     return invalid("rasterize_fwd: missing backgrounds/masks");
   if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_fwd: means2d must be 8-byte aligned");
+  if (reinterpret_cast<uintptr_t>(p->sigma_bounds) % 8)
+    return invalid("rasterize_fwd: sigma_bounds must be 8-byte aligned");
   const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
                             flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
@@ -951,7 +1339,7 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
   if (nG > 0 && !p->accumulate) {
     if (cudaMemsetAsync(v_means2d, 0, f * 2 * nG, s) || cudaMemsetAsync(v_conics, 0, f * 3 * nG, s) ||
         cudaMemsetAsync(v_colors, 0, f * p->channels * nG, s) ||
-        cudaMemsetAsync(v_opacities, 0, f * nG, s) ||
+        cudaMemsetAsync(v_opacities, 0, f * (p->shared_opacities ? (int64_t)p->N : nG), s) ||
         (p->absgrad && cudaMemsetAsync(v_means2d_abs, 0, f * 2 * nG, s)))
       return launch_status("rasterize_bwd: zero gradients");
   }
@@ -964,6 +1352,8 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
   if (p->n_isects > 0 && (!means2d || !conics || !colors || !opacities || !flatten_ids))
     return invalid("rasterize_bwd: missing input buffer");
   if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_bwd: means2d must be 8-byte aligned");
+  if (reinterpret_cast<uintptr_t>(p->sigma_bounds) % 8)
+    return invalid("rasterize_bwd: sigma_bounds must be 8-byte aligned");
   const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
                             flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
@@ -975,4 +1365,18 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
     case 4: return launch_bwd<4>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
     default: return launch_bwd<0>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
   }
+}
+
+extern "C" int gs_rasterize_sigma_bounds(int64_t n, const float* opacities,
+                                         const int32_t* radii, int32_t cameras, float* bounds,
+                                         gs_stream_t stream) {
+  if (n < 0 || (radii && cameras <= 0)) return invalid("rasterize_sigma_bounds: bad sizes");
+  if (n == 0) return GS_OK;
+  if (!opacities || !bounds) return invalid("rasterize_sigma_bounds: missing buffer");
+  if (reinterpret_cast<uintptr_t>(bounds) % 8 || reinterpret_cast<uintptr_t>(radii) % 8)
+    return invalid("rasterize_sigma_bounds: bounds and radii must be 8-byte aligned");
+  sigma_bounds_kernel<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+      n, opacities, reinterpret_cast<const int2*>(radii), cameras,
+      reinterpret_cast<float2*>(bounds));
+  return launch_status("rasterize_sigma_bounds");
 }

@@ -596,12 +596,26 @@ def rasterize_to_pixels_3dgs_forward(inputs, image_width, image_height, tile_siz
     }
     p = RasterParams(I, N, ch, W, H, int(tile_size), tw, th, flatten_ids.numel(),
                      int(backgrounds is not None), int(masks is not None), 0)
+    bounds = sigma_bounds(opacities)
+    p.sigma_bounds = _ptr(bounds)
     check(_lib.load().gs_rasterize_fwd(ct.byref(p), _ptr(means2d), _ptr(conics), _ptr(colors),
                                        _ptr(opacities), _ptr(backgrounds), _ptr(masks),
                                        _ptr(tile_offsets), _ptr(flatten_ids),
                                        _ptr(out["render_colors"]), _ptr(out["render_alphas"]),
                                        _ptr(out["last_ids"]), _stream()),
           "rasterize_to_pixels_3dgs_forward")
+    return out
+
+
+def sigma_bounds(opacities):
+    """The rasterizer's exact alpha decisions as two sigma bounds per opacity
+    entry ([n, 2] float32; gs_rasterize_sigma_bounds), computed once and read
+    by every tile instead of being derived per staged entry."""
+    o = opacities.contiguous()
+    out = torch.empty((o.numel(), 2), dtype=torch.float32, device=o.device)
+    check(_lib.load().gs_rasterize_sigma_bounds(o.numel(), _ptr(o), None, 0, _ptr(out),
+                                                _stream()),
+          "rasterize_sigma_bounds")
     return out
 
 
@@ -651,6 +665,8 @@ def rasterize_to_pixels_3dgs_backward(inputs, forward_outputs, cotangents, image
         out["v_backgrounds"] = _empty(tuple(backgrounds.shape))
     p = RasterParams(I, N, ch, W, H, int(tile_size), tw, th, flatten_ids.numel(),
                      int(backgrounds is not None), int(masks is not None), int(bool(absgrad)))
+    bounds = sigma_bounds(opacities)
+    p.sigma_bounds = _ptr(bounds)
     check(_lib.load().gs_rasterize_bwd(ct.byref(p), _ptr(means2d), _ptr(conics), _ptr(colors),
                                        _ptr(opacities), _ptr(backgrounds), _ptr(masks),
                                        _ptr(tile_offsets), _ptr(flatten_ids), _ptr(render_alphas),

@@ -72,7 +72,8 @@ class AdamParams(ct.Structure):
 class IsectParams(ct.Structure):
     _fields_ = [("I", _i32), ("N", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32), ("tile_y0", _i32), ("tile_y1", _i32),
-                ("reuse_depth_order", _i32), ("positive_depths", _i32)]
+                ("reuse_depth_order", _i32), ("positive_depths", _i32),
+                ("shared_opacities", _i32)]
 
 
 class RasterParams(ct.Structure):
@@ -80,7 +81,7 @@ class RasterParams(ct.Structure):
                 ("image_height", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32), ("n_isects", _i64), ("use_backgrounds", _i32),
                 ("use_masks", _i32), ("absgrad", _i32), ("tile_y0", _i32), ("tile_y1", _i32),
-                ("accumulate", _i32)]
+                ("accumulate", _i32), ("shared_opacities", _i32), ("sigma_bounds", _vp)]
 
 
 _P = ct.POINTER
@@ -128,6 +129,10 @@ SIGNATURES = {
     "gs_isect_offset": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _vp, _vp]),
     "gs_isect_offset_rows": (ct.c_int, [_i64, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "gs_isect_sort_noalloc": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gs_isect_sort_noalloc_check": (ct.c_int, [_i64, _vp]),
+    "gs_rasterize_sigma_bounds": (ct.c_int, [_i64, _vp, _vp, _i32, _vp, _vp]),
+    "gs_isect_sort_wait_selftest": (ct.c_int, [_i64, _vp, _vp, _vp, _vp, _vp, _sz,
+                                               ct.c_uint32, _vp]),
     "gs_fit_activate": (ct.c_int, [_i64] + [_vp] * 9),
     "gs_l2_loss_grad": (ct.c_int, [_i64] + [_vp] * 5),
     "gs_fit_adam": (ct.c_int, [_P(AdamParams)] + [_vp] * 17),

@@ -95,7 +95,7 @@ class TrainingStep:
         self.means2d, self.depths = e((C, N, 2)), e((C, N))
         self.conics, self.radii = e((C, N, 3)), e((C, N, 2), i32)
         self.colors = e((C, N, 3))
-        self.opac_cn = e((C, N)) if C > 1 else None
+        self.sbounds = e((N, 2))  # exact alpha decisions per opacity (sigma bounds)
         self.tiles_per_gauss = e((C, N), i32)
         # [intersections, bin entries of the binned encode]
         self.total = torch.zeros((2,), dtype=torch.int64, device=self.dev)
@@ -123,7 +123,7 @@ class TrainingStep:
         self.bins = 0
         # backward state
         self.v_means2d, self.v_conics = e((C, N, 2)), e((C, N, 3))
-        self.v_colors, self.v_opac_cn = e((C, N, 3)), e((C, N))
+        self.v_colors = e((C, N, 3))
         self.v_depths = torch.zeros((C, N), dtype=f32, device=self.dev)
         sizes = [3 * N, 4 * N, 3 * N, N, self.K * 3 * N]
         self.grad_flat = e((sum(sizes),))
@@ -210,12 +210,9 @@ class TrainingStep:
             colors = self.colors
         else:
             sh_backward = False
-        if C > 1:
-            self.opac_cn.copy_(opacities.view(1, N).expand(C, N))
-            opac = self.opac_cn
-        else:
-            opac = opacities
-        v_opac = self.v_opacities if C == 1 else self.v_opac_cn
+        # the rasterizer and the culled encode read the [N] opacities of
+        # every camera in place and sum their gradient over the cameras
+        opac, v_opac = opacities, self.v_opacities
         m_total = 0
         bands = [(0, 0)]  # (0, 0): every tile row in one pass
         b = 0
@@ -225,6 +222,7 @@ class TrainingStep:
             # the projection culls depths below its near plane: with a
             # positive near plane every visible depth is positive
             ip.positive_depths = int(self.near > 0.0)
+            ip.shared_opacities = 1
             check(L.gs_isect_tile_count_totals(ct.byref(ip), _p(self.means2d), _p(self.radii),
                                                _p(self.tiles_per_gauss), _p(self.total), s),
                   "isect_count")
@@ -242,6 +240,11 @@ class TrainingStep:
                                        _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
                 self._mark("sh_fwd")
                 glue_pending = False
+            if b == 0:
+                check(L.gs_rasterize_sigma_bounds(N, _p(opac), _p(self.radii), C,
+                                                  _p(self.sbounds), s),
+                      "rasterize_sigma_bounds")
+                self._mark("sigma_bounds")
             counted.synchronize()  # the reference's host read of the total
             m, bins = (int(v) for v in self.total_host.tolist())
             if m > self.max_isects_per_pass and y1 == 0:
@@ -296,7 +299,8 @@ class TrainingStep:
                                              _p(self.tile_offsets), s), "isect_offset")
                 self._mark("isect_offset")
             rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
-                              int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0))
+                              int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0), 1,
+                              _p(self.sbounds))
             check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics),
                                      _p(colors), _p(opac), _p(self.backgrounds), None,
                                      _p(self.tile_offsets), _p(self.sorted_flatten),
@@ -327,8 +331,6 @@ class TrainingStep:
         self.bands = len(bands)
         if after_raster is not None:
             after_raster()
-        if C > 1:
-            torch.sum(self.v_opac_cn, dim=0, out=self.v_opacities)
         check(L.gs_projection_bwd(ct.byref(pp), _p(means), None, _p(quats), _p(scales),
                                   _p(viewmats), _p(Ks), _p(self.radii), _p(self.conics), None,
                                   _p(self.v_means2d), _p(self.v_depths), _p(self.v_conics), None,

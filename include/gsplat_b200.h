@@ -182,6 +182,9 @@ typedef struct {
                                 that); the sort then carries 31 depth bits,
                                 one key bit fewer.  Same output; a broken
                                 promise misorders, it does not fault. */
+  int32_t shared_opacities;  /* gs_isect_tile_encode_binned_culled: 1 =
+                                opacities are [N], shared by the I images
+                                (element e reads e mod N); else [I, N] */
 } gs_isect_params;
 
 /* tiles_per_gauss [I,N] int32 */
@@ -364,6 +367,27 @@ int gs_isect_sort_noalloc(int64_t n_isects, int32_t key_bits,
                           const int64_t* isect_ids, const int32_t* flatten_ids,
                           int64_t* sorted_isect_ids, int32_t* sorted_flatten_ids,
                           gs_stream_t stream);
+/* The error word of the last gs_isect_sort_noalloc call on the current
+ * device (n_isects as passed to it), read from the library's fixed array:
+ * waits for `stream`, then GS_OK, or GS_ERR_DEVICE when a bounded wait of
+ * that sort gave up.  GS_OK before the first call.  The array's cached
+ * device address does not survive cudaDeviceReset: calls after a reset of
+ * the device are not supported.  No reference counterpart. */
+int gs_isect_sort_noalloc_check(int64_t n_isects, gs_stream_t stream);
+
+/* Diagnostic of the bounded look-back wait, no reference counterpart: runs
+ * the second 4096-key tile of one radix pass over n_isects keys (4096 <
+ * n_isects <= 8192) alone, so that its wait on the first tile, which never
+ * publishes, gives up after spin_limit polls (1..1024).  The pass then
+ * raises the error word in `workspace` (gs_isect_sort_workspace_size bytes)
+ * and finishes; gs_isect_sort_check reports GS_ERR_DEVICE.  The outputs get
+ * the second tile's keys at in-range places, the rest is left untouched.
+ * Lets a test run the give-up path without holding the GPU. */
+int gs_isect_sort_wait_selftest(int64_t n_isects, const int64_t* isect_ids,
+                                const int32_t* flatten_ids, int64_t* sorted_isect_ids,
+                                int32_t* sorted_flatten_ids, void* workspace,
+                                size_t workspace_bytes, uint32_t spin_limit,
+                                gs_stream_t stream);
 
 /* tile_offsets [I, tile_height, tile_width] int32 from sorted isect_ids:
  * lower bound of (image << tile_bits | tile) in isect_ids >> 32. */
@@ -400,7 +424,35 @@ typedef struct {
                                flatten_ids / n_isects the band's); else all */
   int32_t accumulate; /* bwd: add into the gradient outputs instead of
                          zeroing them first (bands after the first) */
+  int32_t shared_opacities; /* when set, opacities and v_opacities are [N],
+                               shared by the I images (entry g of the
+                               flattened [I, N] index reads g mod N): the
+                               per-Gaussian opacity of a multi-camera batch
+                               without an [I, N] copy, and its gradient
+                               summed over the images in place.  No
+                               reference counterpart (the reference takes
+                               [I, N]). */
+  const float* sigma_bounds; /* optional, 8-byte aligned: the (keep, clamp)
+                                sigma bounds of every opacity entry, laid out
+                                like opacities ([I, N] or [N]) with two floats
+                                each, from gs_rasterize_sigma_bounds.  Null:
+                                the kernels derive them per staged entry
+                                (same results, slower).  No reference
+                                counterpart. */
 } gs_raster_params;
+
+/* The exact alpha decisions of the rasterizer as two sigma bounds per
+ * opacity: bounds[2i] = the largest sigma at which o = opacities[i] still
+ * reaches alpha >= 1/255, bounds[2i+1] = the smallest sigma at which
+ * o e^-sigma <= 0.99 (alpha not clamped), both with the correctly rounded
+ * exponential and the reference's float multiply (-inf: never composited /
+ * never clamped; NaN or +inf opacity: +inf, +inf).  Pass them through
+ * gs_raster_params.sigma_bounds.  With radii ([cameras, n, 2], 8-byte
+ * aligned) only the entries some camera sees (both radii > 0) are written:
+ * the others have no intersections, so no rasterizer reads them.  No
+ * reference counterpart. */
+int gs_rasterize_sigma_bounds(int64_t n, const float* opacities, const int32_t* radii,
+                              int32_t cameras, float* bounds, gs_stream_t stream);
 
 /* render_colors [I,H,W,ch], render_alphas [I,H,W,1], last_ids [I,H,W] */
 int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,

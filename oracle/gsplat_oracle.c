@@ -14,6 +14,7 @@
 #include "gsplat_oracle.h"
 
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -1015,13 +1016,291 @@ int orc_isect_offset(int64_t n_isects, const int64_t* isect_ids, int I,
 #define K_T_EPS 1.0e-4f
 #define K_MIN_1MA 1.0e-6f
 
-/* True when a float decision of the compositing loop is within rounding of
- * its threshold, so that a different (but correct) exp() can flip it. */
-static int near_rel(float v, float thr, float rel) {
-  return fabsf(v - thr) <= rel * thr;
+/* One rasterization call: its inputs and outputs. */
+typedef struct {
+  int I, N, channels, width, height, tile_size, tile_width, tile_height;
+  const float *means2d, *conics, *colors, *opacities, *backgrounds;
+  const uint8_t* masks;
+  const int32_t* tile_offsets;
+  int64_t n_isects;
+  const int32_t* flatten_ids;
+  /* forward outputs */
+  float *render_colors, *render_alphas;
+  int32_t* last_ids;
+  /* backward inputs */
+  const float *render_alphas_in, *v_render_colors, *v_render_alphas;
+  const int32_t* last_ids_in;
+} RasterCall;
+
+/* Gradient outputs of one backward worker. */
+typedef struct {
+  float *v_means2d_abs, *v_means2d, *v_conics, *v_colors, *v_opacities, *v_backgrounds;
+} RasterGrads;
+
+static void tile_range(const RasterCall* a, int64_t oi, int64_t* start, int64_t* end) {
+  const int64_t per = (int64_t)a->tile_width * a->tile_height;
+  *start = a->tile_offsets[oi];
+  *end = (oi / per == a->I - 1 && oi % per == per - 1) ? a->n_isects : a->tile_offsets[oi + 1];
 }
 
-/* gsplat_rasterize.cpp:249-369 (CPU) == metal/gsplat_rasterize.metal:31-120. */
+/* Forward of the pixels of tile `oi` (image-major tile index):
+ * gsplat_rasterize.cpp:292-366 (CPU) == metal/gsplat_rasterize.metal:31-120. */
+static void raster_fwd_tile(const RasterCall* a, int64_t oi) {
+  const int per = a->tile_width * a->tile_height;
+  const int im = (int)(oi / per), tid = (int)(oi % per);
+  const int ty = tid / a->tile_width, tx = tid % a->tile_width;
+  int64_t start, end;
+  tile_range(a, oi, &start, &end);
+  const int skip = a->masks && !a->masks[oi];
+  const int ch_n = a->channels;
+  for (int ly = 0; ly < a->tile_size; ++ly) {
+    const int y = ty * a->tile_size + ly;
+    if (y >= a->height) continue;
+    for (int lx = 0; lx < a->tile_size; ++lx) {
+      const int x = tx * a->tile_size + lx;
+      if (x >= a->width) continue;
+      const int64_t pix = ((int64_t)im * a->height + y) * a->width + x;
+      const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+      float T = 1.0f;
+      int32_t cur = 0;
+      float* rc = a->render_colors + pix * ch_n;
+      for (int ch = 0; ch < ch_n; ++ch) rc[ch] = 0.0f;
+      for (int64_t idx = start; !skip && idx < end; ++idx) {
+        const int g = a->flatten_ids[idx];
+        const float dx = a->means2d[g * 2] - px, dy = a->means2d[g * 2 + 1] - py;
+        const float c0 = a->conics[g * 3], c1 = a->conics[g * 3 + 1], c2 = a->conics[g * 3 + 2];
+        const float sigma = 0.5f * (c0 * dx * dx + c2 * dy * dy) + c1 * dx * dy;
+        const float alpha = fminf(K_MAX_ALPHA, a->opacities[g] * expf(-sigma));
+        if (sigma < 0.0f || alpha < K_ALPHA_T) continue;
+        const float next_T = T * (1.0f - alpha);
+        if (next_T <= K_T_EPS) break;
+        const float vis = alpha * T;
+        for (int ch = 0; ch < ch_n; ++ch) rc[ch] += a->colors[(int64_t)g * ch_n + ch] * vis;
+        cur = (int32_t)idx;
+        T = next_T;
+      }
+      a->render_alphas[pix] = 1.0f - T;
+      for (int ch = 0; ch < ch_n; ++ch) {
+        const float bg = a->backgrounds ? a->backgrounds[im * ch_n + ch] : 0.0f;
+        rc[ch] += T * bg;
+      }
+      a->last_ids[pix] = cur;
+    }
+  }
+}
+
+/* Per-worker scratch of the backward: the composited entries of a pixel. */
+typedef struct {
+  float* buf;
+  int64_t cap;
+  int64_t* ids;
+  float *al, *vi;
+} BwdScratch;
+
+static int scratch_grow(BwdScratch* s) {
+  const int64_t cap = s->cap ? s->cap * 2 : 1024;
+  int64_t* ni = (int64_t*)realloc(s->ids, sizeof(int64_t) * (size_t)cap);
+  if (ni) s->ids = ni;
+  float* na = (float*)realloc(s->al, sizeof(float) * (size_t)cap);
+  if (na) s->al = na;
+  float* nv = (float*)realloc(s->vi, sizeof(float) * (size_t)cap);
+  if (nv) s->vi = nv;
+  if (!ni || !na || !nv) return ORC_ERR_NOMEM;
+  s->cap = cap;
+  return 0;
+}
+
+/* Backward of the pixels of tile `oi`, accumulated into `o`:
+ * gsplat_rasterize.cpp:437-566 (CPU) == metal/gsplat_rasterize.metal:122-251. */
+static int raster_bwd_tile(const RasterCall* a, int64_t oi, const RasterGrads* o, BwdScratch* s) {
+  if (a->masks && !a->masks[oi]) return 0;
+  const int per = a->tile_width * a->tile_height;
+  const int im = (int)(oi / per), tid = (int)(oi % per);
+  const int ty = tid / a->tile_width, tx = tid % a->tile_width;
+  const int ch_n = a->channels;
+  int64_t start, end;
+  tile_range(a, oi, &start, &end);
+  for (int ly = 0; ly < a->tile_size; ++ly) {
+    const int y = ty * a->tile_size + ly;
+    if (y >= a->height) continue;
+    for (int lx = 0; lx < a->tile_size; ++lx) {
+      const int x = tx * a->tile_size + lx;
+      if (x >= a->width) continue;
+      const int64_t pix = ((int64_t)im * a->height + y) * a->width + x;
+      const int32_t bin_final = a->last_ids_in[pix];
+      const float px = (float)x + 0.5f, py = (float)y + 0.5f;
+      int64_t nv = 0;
+      for (int64_t idx = start; idx < end && idx <= bin_final; ++idx) {
+        const int g = a->flatten_ids[idx];
+        const float dx = a->means2d[g * 2] - px, dy = a->means2d[g * 2 + 1] - py;
+        const float c0 = a->conics[g * 3], c1 = a->conics[g * 3 + 1], c2 = a->conics[g * 3 + 2];
+        const float sigma = 0.5f * (c0 * dx * dx + c2 * dy * dy) + c1 * dx * dy;
+        const float vis = expf(-sigma);
+        const float alpha = fminf(K_MAX_ALPHA, a->opacities[g] * vis);
+        if (sigma < 0.0f || alpha < K_ALPHA_T) continue;
+        if (nv == s->cap && scratch_grow(s)) return ORC_ERR_NOMEM;
+        s->ids[nv] = idx;
+        s->al[nv] = alpha;
+        s->vi[nv] = vis;
+        ++nv;
+      }
+      const float T_final = 1.0f - a->render_alphas_in[pix];
+      float T = T_final;
+      float* buf = s->buf;
+      for (int ch = 0; ch < ch_n; ++ch) buf[ch] = 0.0f;
+      const float v_a = a->v_render_alphas[pix];
+      const float* v_c = a->v_render_colors + pix * ch_n;
+      if (o->v_backgrounds)
+        for (int ch = 0; ch < ch_n; ++ch) o->v_backgrounds[im * ch_n + ch] += T_final * v_c[ch];
+      for (int64_t l = nv - 1; l >= 0; --l) {
+        const int g = a->flatten_ids[s->ids[l]];
+        const float alpha = s->al[l], vis = s->vi[l];
+        const float ra = 1.0f / fmaxf(K_MIN_1MA, 1.0f - alpha);
+        T *= ra;
+        const float fac = alpha * T;
+        for (int ch = 0; ch < ch_n; ++ch) o->v_colors[(int64_t)g * ch_n + ch] += fac * v_c[ch];
+        float v_alpha = 0.0f;
+        for (int ch = 0; ch < ch_n; ++ch)
+          v_alpha += (a->colors[(int64_t)g * ch_n + ch] * T - buf[ch] * ra) * v_c[ch];
+        v_alpha += T_final * ra * v_a;
+        if (a->backgrounds) {
+          float acc = 0.0f;
+          for (int ch = 0; ch < ch_n; ++ch) acc += a->backgrounds[im * ch_n + ch] * v_c[ch];
+          v_alpha += -T_final * ra * acc;
+        }
+        if (a->opacities[g] * vis <= K_MAX_ALPHA) {
+          const float dx = a->means2d[g * 2] - px, dy = a->means2d[g * 2 + 1] - py;
+          const float c0 = a->conics[g * 3], c1 = a->conics[g * 3 + 1], c2 = a->conics[g * 3 + 2];
+          const float v_sigma = -a->opacities[g] * vis * v_alpha;
+          const float vx = v_sigma * (c0 * dx + c1 * dy);
+          const float vy = v_sigma * (c1 * dx + c2 * dy);
+          o->v_conics[g * 3] += 0.5f * v_sigma * dx * dx;
+          o->v_conics[g * 3 + 1] += v_sigma * dx * dy;
+          o->v_conics[g * 3 + 2] += 0.5f * v_sigma * dy * dy;
+          o->v_means2d[g * 2] += vx;
+          o->v_means2d[g * 2 + 1] += vy;
+          if (o->v_means2d_abs) {
+            o->v_means2d_abs[g * 2] += fabsf(vx);
+            o->v_means2d_abs[g * 2 + 1] += fabsf(vy);
+          }
+          o->v_opacities[g] += vis * v_alpha;
+        }
+        for (int ch = 0; ch < ch_n; ++ch) buf[ch] += a->colors[(int64_t)g * ch_n + ch] * fac;
+      }
+    }
+  }
+  return 0;
+}
+
+/* Workers take the tiles k, k + nthreads, k + 2 nthreads, ... of the
+ * image-major tile order.  The forward writes disjoint pixels; backward
+ * worker 0 accumulates into the outputs and every other worker into its own
+ * zeroed copy, added to the outputs in worker order afterwards (so the
+ * result depends on nthreads only through the order of the float sums). */
+typedef struct {
+  const RasterCall* a;
+  RasterGrads g;
+  int k, nthreads, bwd, rc;
+} RasterWork;
+
+static void* raster_worker(void* p) {
+  RasterWork* w = (RasterWork*)p;
+  const RasterCall* a = w->a;
+  const int64_t n_tiles = (int64_t)a->I * a->tile_width * a->tile_height;
+  BwdScratch s = {0};
+  if (w->bwd) {
+    s.buf = (float*)malloc(sizeof(float) * (size_t)a->channels);
+    if (!s.buf || scratch_grow(&s)) w->rc = ORC_ERR_NOMEM;
+  }
+  for (int64_t oi = w->k; oi < n_tiles && !w->rc; oi += w->nthreads) {
+    if (w->bwd) w->rc = raster_bwd_tile(a, oi, &w->g, &s);
+    else raster_fwd_tile(a, oi);
+  }
+  free(s.buf);
+  free(s.ids);
+  free(s.al);
+  free(s.vi);
+  return NULL;
+}
+
+static size_t grad_floats(const RasterCall* a, int absgrad, int bg) {
+  const size_t nG = (size_t)a->I * (size_t)a->N;
+  return nG * (2 + 3 + (size_t)a->channels + 1 + (absgrad ? 2 : 0)) +
+         (bg ? (size_t)a->I * a->channels : 0);
+}
+
+static RasterGrads grads_in(float* base, const RasterCall* a, int absgrad, int bg) {
+  const size_t nG = (size_t)a->I * (size_t)a->N;
+  RasterGrads g;
+  g.v_means2d = base;
+  g.v_conics = g.v_means2d + 2 * nG;
+  g.v_colors = g.v_conics + 3 * nG;
+  g.v_opacities = g.v_colors + (size_t)a->channels * nG;
+  g.v_means2d_abs = absgrad ? g.v_opacities + nG : NULL;
+  g.v_backgrounds = bg ? g.v_opacities + nG + (absgrad ? 2 * nG : 0) : NULL;
+  return g;
+}
+
+static void add_into(float* dst, const float* src, size_t n) {
+  if (!dst) return;
+  for (size_t i = 0; i < n; ++i) dst[i] += src[i];
+}
+
+static int raster_run(const RasterCall* a, const RasterGrads* out, int bwd, int nthreads) {
+  const int64_t n_tiles = (int64_t)a->I * a->tile_width * a->tile_height;
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > n_tiles) nthreads = n_tiles > 0 ? (int)n_tiles : 1;
+  if (nthreads > 256) nthreads = 256;
+  const int absgrad = bwd && out->v_means2d_abs != NULL;
+  const int bg = bwd && out->v_backgrounds != NULL;
+  RasterWork w[256];
+  pthread_t th[256];
+  float* priv[256] = {0};
+  const size_t nf = bwd ? grad_floats(a, absgrad, bg) : 0;
+  int rc = 0;
+  for (int k = 0; k < nthreads; ++k) {
+    w[k].a = a;
+    w[k].k = k;
+    w[k].nthreads = nthreads;
+    w[k].bwd = bwd;
+    w[k].rc = 0;
+    if (bwd) {
+      if (k == 0) {
+        w[k].g = *out;
+      } else {
+        priv[k] = (float*)calloc(nf, sizeof(float));
+        if (!priv[k]) { rc = ORC_ERR_NOMEM; nthreads = k; break; }
+        w[k].g = grads_in(priv[k], a, absgrad, bg);
+      }
+    }
+  }
+  int started = 0;
+  for (int k = 1; k < nthreads && !rc; ++k) {
+    if (pthread_create(&th[k], NULL, raster_worker, &w[k]) != 0) break;
+    started = k;
+  }
+  if (!rc) {
+    /* tiles of workers that could not start run here, after worker 0's */
+    raster_worker(&w[0]);
+    for (int k = started + 1; k < nthreads; ++k) raster_worker(&w[k]);
+  }
+  for (int k = 1; k <= started; ++k) pthread_join(th[k], NULL);
+  for (int k = 0; k < nthreads; ++k)
+    if (w[k].rc) rc = w[k].rc;
+  const size_t nG = (size_t)a->I * (size_t)a->N;
+  for (int k = 1; k < nthreads && bwd && !rc; ++k) {
+    const RasterGrads* g = &w[k].g;
+    add_into(out->v_means2d, g->v_means2d, 2 * nG);
+    add_into(out->v_conics, g->v_conics, 3 * nG);
+    add_into(out->v_colors, g->v_colors, (size_t)a->channels * nG);
+    add_into(out->v_opacities, g->v_opacities, nG);
+    if (absgrad) add_into(out->v_means2d_abs, g->v_means2d_abs, 2 * nG);
+    if (bg) add_into(out->v_backgrounds, g->v_backgrounds, (size_t)a->I * a->channels);
+  }
+  for (int k = 1; k < 256; ++k) free(priv[k]);
+  return rc;
+}
+
 int orc_raster_fwd(int I, int N, int channels, const float* means2d,
                    const float* conics, const float* colors,
                    const float* opacities, const float* backgrounds,
@@ -1029,69 +1308,20 @@ int orc_raster_fwd(int I, int N, int channels, const float* means2d,
                    int tile_width, int tile_height, const int32_t* tile_offsets,
                    int64_t n_isects, const int32_t* flatten_ids,
                    float* render_colors, float* render_alphas,
-                   int32_t* last_ids, uint8_t* near_threshold) {
-  (void)N;
+                   int32_t* last_ids, int nthreads) {
   if (I <= 0 || channels <= 0 || tile_size <= 0) return ORC_ERR_ARG;
   const int64_t n_pix = (int64_t)I * height * width;
   memset(render_colors, 0, sizeof(float) * (size_t)n_pix * channels);
   memset(render_alphas, 0, sizeof(float) * (size_t)n_pix);
   memset(last_ids, 0, sizeof(int32_t) * (size_t)n_pix);
-  if (near_threshold) memset(near_threshold, 0, (size_t)n_pix);
-  for (int im = 0; im < I; ++im)
-    for (int ty = 0; ty < tile_height; ++ty)
-      for (int tx = 0; tx < tile_width; ++tx) {
-        const int tid = ty * tile_width + tx;
-        const int64_t oi = (int64_t)im * tile_height * tile_width + tid;
-        const int64_t start = tile_offsets[oi];
-        const int64_t end = (im == I - 1 && tid == tile_width * tile_height - 1)
-                                ? n_isects
-                                : tile_offsets[oi + 1];
-        const int skip = masks && !masks[oi];
-        for (int ly = 0; ly < tile_size; ++ly) {
-          const int y = ty * tile_size + ly;
-          if (y >= height) continue;
-          for (int lx = 0; lx < tile_size; ++lx) {
-            const int x = tx * tile_size + lx;
-            if (x >= width) continue;
-            const int64_t pix = ((int64_t)im * height + y) * width + x;
-            const float px = (float)x + 0.5f, py = (float)y + 0.5f;
-            float T = 1.0f;
-            int32_t cur = 0;
-            int near = 0;
-            for (int64_t idx = start; !skip && idx < end; ++idx) {
-              const int g = flatten_ids[idx];
-              const float dx = means2d[g * 2] - px, dy = means2d[g * 2 + 1] - py;
-              const float c0 = conics[g * 3], c1 = conics[g * 3 + 1], c2 = conics[g * 3 + 2];
-              const float sigma = 0.5f * (c0 * dx * dx + c2 * dy * dy) + c1 * dx * dy;
-              const float oe = opacities[g] * expf(-sigma);
-              const float alpha = fminf(K_MAX_ALPHA, oe);
-              if (fabsf(sigma) <= 1.0e-6f || near_rel(oe, K_ALPHA_T, 1.0e-4f) ||
-                  near_rel(oe, K_MAX_ALPHA, 1.0e-4f))
-                near = 1;
-              if (sigma < 0.0f || alpha < K_ALPHA_T) continue;
-              const float next_T = T * (1.0f - alpha);
-              if (near_rel(next_T, K_T_EPS, 1.0e-3f)) near = 1;
-              if (next_T <= K_T_EPS) break;
-              const float vis = alpha * T;
-              for (int ch = 0; ch < channels; ++ch)
-                render_colors[pix * channels + ch] += colors[(int64_t)g * channels + ch] * vis;
-              cur = (int32_t)idx;
-              T = next_T;
-            }
-            render_alphas[pix] = 1.0f - T;
-            for (int ch = 0; ch < channels; ++ch) {
-              const float bg = backgrounds ? backgrounds[im * channels + ch] : 0.0f;
-              render_colors[pix * channels + ch] += T * bg;
-            }
-            last_ids[pix] = cur;
-            if (near_threshold) near_threshold[pix] = (uint8_t)near;
-          }
-        }
-      }
-  return 0;
+  RasterCall a = {I, N, channels, width, height, tile_size, tile_width, tile_height,
+                  means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                  n_isects, flatten_ids, render_colors, render_alphas, last_ids,
+                  NULL, NULL, NULL, NULL};
+  RasterGrads none = {0};
+  return raster_run(&a, &none, 0, nthreads);
 }
 
-/* gsplat_rasterize.cpp:371-569 (CPU) == metal/gsplat_rasterize.metal:122-251. */
 int orc_raster_bwd(int I, int N, int channels, const float* means2d,
                    const float* conics, const float* colors,
                    const float* opacities, const float* backgrounds,
@@ -1101,7 +1331,8 @@ int orc_raster_bwd(int I, int N, int channels, const float* means2d,
                    const float* render_alphas, const int32_t* last_ids,
                    const float* v_render_colors, const float* v_render_alphas,
                    float* v_means2d_abs, float* v_means2d, float* v_conics,
-                   float* v_colors, float* v_opacities, float* v_backgrounds) {
+                   float* v_colors, float* v_opacities, float* v_backgrounds,
+                   int nthreads) {
   if (I <= 0 || channels <= 0 || tile_size <= 0) return ORC_ERR_ARG;
   const int64_t nG = (int64_t)I * N;
   if (v_means2d_abs) memset(v_means2d_abs, 0, sizeof(float) * 2 * (size_t)nG);
@@ -1110,111 +1341,12 @@ int orc_raster_bwd(int I, int N, int channels, const float* means2d,
   memset(v_colors, 0, sizeof(float) * (size_t)channels * nG);
   memset(v_opacities, 0, sizeof(float) * (size_t)nG);
   if (v_backgrounds) memset(v_backgrounds, 0, sizeof(float) * (size_t)I * channels);
-  float* buf = (float*)malloc(sizeof(float) * (size_t)channels);
-  int64_t cap = 1024;
-  int64_t* ids = (int64_t*)malloc(sizeof(int64_t) * (size_t)cap);
-  float* al = (float*)malloc(sizeof(float) * (size_t)cap);
-  float* vi = (float*)malloc(sizeof(float) * (size_t)cap);
-  if (!buf || !ids || !al || !vi) { free(buf); free(ids); free(al); free(vi); return ORC_ERR_NOMEM; }
-  int rc = 0;
-  for (int im = 0; im < I && !rc; ++im)
-    for (int ty = 0; ty < tile_height && !rc; ++ty)
-      for (int tx = 0; tx < tile_width && !rc; ++tx) {
-        const int tid = ty * tile_width + tx;
-        const int64_t oi = (int64_t)im * tile_height * tile_width + tid;
-        if (masks && !masks[oi]) continue;
-        const int64_t start = tile_offsets[oi];
-        const int64_t end = (im == I - 1 && tid == tile_width * tile_height - 1)
-                                ? n_isects
-                                : tile_offsets[oi + 1];
-        for (int ly = 0; ly < tile_size; ++ly) {
-          const int y = ty * tile_size + ly;
-          if (y >= height) continue;
-          for (int lx = 0; lx < tile_size; ++lx) {
-            const int x = tx * tile_size + lx;
-            if (x >= width) continue;
-            const int64_t pix = ((int64_t)im * height + y) * width + x;
-            const int32_t bin_final = last_ids[pix];
-            const float px = (float)x + 0.5f, py = (float)y + 0.5f;
-            int64_t nv = 0;
-            for (int64_t idx = start; idx < end && idx <= bin_final; ++idx) {
-              const int g = flatten_ids[idx];
-              const float dx = means2d[g * 2] - px, dy = means2d[g * 2 + 1] - py;
-              const float c0 = conics[g * 3], c1 = conics[g * 3 + 1], c2 = conics[g * 3 + 2];
-              const float sigma = 0.5f * (c0 * dx * dx + c2 * dy * dy) + c1 * dx * dy;
-              const float vis = expf(-sigma);
-              const float alpha = fminf(K_MAX_ALPHA, opacities[g] * vis);
-              if (sigma < 0.0f || alpha < K_ALPHA_T) continue;
-              if (nv == cap) {
-                cap *= 2;
-                int64_t* ni = (int64_t*)realloc(ids, sizeof(int64_t) * (size_t)cap);
-                float* na = (float*)realloc(al, sizeof(float) * (size_t)cap);
-                float* nvv = (float*)realloc(vi, sizeof(float) * (size_t)cap);
-                if (ni) ids = ni;
-                if (na) al = na;
-                if (nvv) vi = nvv;
-                if (!ni || !na || !nvv) { rc = ORC_ERR_NOMEM; break; }
-              }
-              ids[nv] = idx;
-              al[nv] = alpha;
-              vi[nv] = vis;
-              ++nv;
-            }
-            if (rc) break;
-            const float T_final = 1.0f - render_alphas[pix];
-            float T = T_final;
-            for (int ch = 0; ch < channels; ++ch) buf[ch] = 0.0f;
-            const float v_a = v_render_alphas[pix];
-            const float* v_c = v_render_colors + pix * channels;
-            if (v_backgrounds)
-              for (int ch = 0; ch < channels; ++ch)
-                v_backgrounds[im * channels + ch] += T_final * v_c[ch];
-            for (int64_t l = nv - 1; l >= 0; --l) {
-              const int g = flatten_ids[ids[l]];
-              const float alpha = al[l], vis = vi[l];
-              const float ra = 1.0f / fmaxf(K_MIN_1MA, 1.0f - alpha);
-              T *= ra;
-              const float fac = alpha * T;
-              for (int ch = 0; ch < channels; ++ch)
-                v_colors[(int64_t)g * channels + ch] += fac * v_c[ch];
-              float v_alpha = 0.0f;
-              for (int ch = 0; ch < channels; ++ch)
-                v_alpha += (colors[(int64_t)g * channels + ch] * T - buf[ch] * ra) * v_c[ch];
-              v_alpha += T_final * ra * v_a;
-              if (backgrounds) {
-                float acc = 0.0f;
-                for (int ch = 0; ch < channels; ++ch)
-                  acc += backgrounds[im * channels + ch] * v_c[ch];
-                v_alpha += -T_final * ra * acc;
-              }
-              if (opacities[g] * vis <= K_MAX_ALPHA) {
-                const float dx = means2d[g * 2] - px, dy = means2d[g * 2 + 1] - py;
-                const float c0 = conics[g * 3], c1 = conics[g * 3 + 1], c2 = conics[g * 3 + 2];
-                const float v_sigma = -opacities[g] * vis * v_alpha;
-                const float vx = v_sigma * (c0 * dx + c1 * dy);
-                const float vy = v_sigma * (c1 * dx + c2 * dy);
-                v_conics[g * 3] += 0.5f * v_sigma * dx * dx;
-                v_conics[g * 3 + 1] += v_sigma * dx * dy;
-                v_conics[g * 3 + 2] += 0.5f * v_sigma * dy * dy;
-                v_means2d[g * 2] += vx;
-                v_means2d[g * 2 + 1] += vy;
-                if (v_means2d_abs) {
-                  v_means2d_abs[g * 2] += fabsf(vx);
-                  v_means2d_abs[g * 2 + 1] += fabsf(vy);
-                }
-                v_opacities[g] += vis * v_alpha;
-              }
-              for (int ch = 0; ch < channels; ++ch)
-                buf[ch] += colors[(int64_t)g * channels + ch] * fac;
-            }
-          }
-        }
-      }
-  free(buf);
-  free(ids);
-  free(al);
-  free(vi);
-  return rc;
+  RasterCall a = {I, N, channels, width, height, tile_size, tile_width, tile_height,
+                  means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                  n_isects, flatten_ids, NULL, NULL, NULL,
+                  render_alphas, v_render_colors, v_render_alphas, last_ids};
+  RasterGrads out = {v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, v_backgrounds};
+  return raster_run(&a, &out, 1, nthreads);
 }
 
 /* ------------------------------------------------------------------ */

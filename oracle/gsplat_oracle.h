@@ -78,7 +78,7 @@ int orc_raster_fwd(int I, int N, int channels, const float* means2d,
                    int tile_width, int tile_height, const int32_t* tile_offsets,
                    int64_t n_isects, const int32_t* flatten_ids,
                    float* render_colors, float* render_alphas,
-                   int32_t* last_ids, uint8_t* near_threshold);
+                   int32_t* last_ids, int nthreads);
 int orc_raster_bwd(int I, int N, int channels, const float* means2d,
                    const float* conics, const float* colors,
                    const float* opacities, const float* backgrounds,
@@ -88,7 +88,8 @@ int orc_raster_bwd(int I, int N, int channels, const float* means2d,
                    const float* render_alphas, const int32_t* last_ids,
                    const float* v_render_colors, const float* v_render_alphas,
                    float* v_means2d_abs, float* v_means2d, float* v_conics,
-                   float* v_colors, float* v_opacities, float* v_backgrounds);
+                   float* v_colors, float* v_opacities, float* v_backgrounds,
+                   int nthreads);
 
 int orc_sh_glue_fwd(int C, int N, int K, int degree, const float* means,
                     const float* viewmats, const float* coeffs,

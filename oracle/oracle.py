@@ -44,6 +44,16 @@ def _u8(a):
     return None if a is None else np.ascontiguousarray(a, dtype=np.uint8)
 
 
+def raster_threads(bytes_per_thread: int = 0) -> int:
+    """Worker threads of the oracle's rasterizer: every core this process
+    may use (GSPLAT_ORACLE_THREADS overrides), fewer when each backward
+    worker's private gradient copy would take more than 4 GB in total."""
+    n = int(os.environ.get("GSPLAT_ORACLE_THREADS", "0")) or len(os.sched_getaffinity(0))
+    if bytes_per_thread > 0:
+        n = min(n, max(1, int(4e9 // bytes_per_thread)))
+    return max(1, min(n, 256))
+
+
 def _check(rc, lib, what):
     if rc != 0:
         msg = ""
@@ -175,7 +185,9 @@ class _Common:
 
     def raster_fwd(self, means2d, conics, colors, opacities, tile_offsets,
                    flatten_ids, width, height, tile_size, backgrounds=None,
-                   masks=None):
+                   masks=None, threads=None):
+        """threads: worker threads of the C restatement (default: every
+        core); the results do not depend on it."""
         I, N, ch, th, tw = self._raster_dims(means2d, colors, tile_offsets)
         prefix = np.asarray(tile_offsets).shape[:-2]
         flatten_ids = _i32(flatten_ids)
@@ -184,19 +196,22 @@ class _Common:
             "render_alphas": np.zeros(prefix + (height, width, 1), np.float32),
             "last_ids": np.zeros(prefix + (height, width), np.int32),
         }
-        near = self._raster_fwd(I, N, ch, _f32(means2d), _f32(conics), _f32(colors),
-                                _f32(opacities), _f32(backgrounds), _u8(masks), width,
-                                height, tile_size, tw, th, _i32(tile_offsets),
-                                flatten_ids.size, flatten_ids, out["render_colors"],
-                                out["render_alphas"], out["last_ids"])
-        if near is not None:
-            out["near_threshold"] = near.reshape(prefix + (height, width))
+        self._raster_fwd(I, N, ch, _f32(means2d), _f32(conics), _f32(colors),
+                         _f32(opacities), _f32(backgrounds), _u8(masks), width,
+                         height, tile_size, tw, th, _i32(tile_offsets),
+                         flatten_ids.size, flatten_ids, out["render_colors"],
+                         out["render_alphas"], out["last_ids"], threads)
         return out
 
     def raster_bwd(self, means2d, conics, colors, opacities, tile_offsets,
                    flatten_ids, width, height, tile_size, render_alphas,
                    last_ids, v_render_colors, v_render_alphas,
-                   backgrounds=None, masks=None, absgrad=False):
+                   backgrounds=None, masks=None, absgrad=False, threads=None):
+        """threads: worker threads of the C restatement (default: every
+        core, fewer for very large gradient buffers).  Each worker sums its
+        tiles' contributions separately, so the gradients depend on the
+        thread count through the order of the float additions only;
+        threads=1 gives the reference's tile order."""
         I, N, ch, th, tw = self._raster_dims(means2d, colors, tile_offsets)
         flatten_ids = _i32(flatten_ids)
         shape2 = np.asarray(means2d).shape
@@ -217,7 +232,7 @@ class _Common:
                          _f32(v_render_colors), _f32(v_render_alphas),
                          absgrad, out.get("v_means2d_abs"), out["v_means2d"],
                          out["v_conics"], out["v_colors"], out["v_opacities"],
-                         out.get("v_backgrounds"))
+                         out.get("v_backgrounds"), threads)
         return out
 
 
@@ -241,8 +256,8 @@ class Oracle(_Common):
         L.orc_isect_encode.argtypes = [_i, _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i64, _vp, _vp]
         L.orc_isect_sort.argtypes = [_i64, _vp, _vp, _vp, _vp]
         L.orc_isect_offset.argtypes = [_i64, _vp, _i, _i, _i, _vp]
-        L.orc_raster_fwd.argtypes = [_i, _i, _i] + [_vp] * 6 + [_i] * 5 + [_vp, _i64] + [_vp] * 5
-        L.orc_raster_bwd.argtypes = [_i, _i, _i] + [_vp] * 6 + [_i] * 5 + [_vp, _i64] + [_vp] * 11
+        L.orc_raster_fwd.argtypes = [_i, _i, _i] + [_vp] * 6 + [_i] * 5 + [_vp, _i64] + [_vp] * 4 + [_i]
+        L.orc_raster_bwd.argtypes = [_i, _i, _i] + [_vp] * 6 + [_i] * 5 + [_vp, _i64] + [_vp] * 11 + [_i]
         L.orc_sh_glue_fwd.argtypes = [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]
         L.orc_sh_glue_bwd.argtypes = [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
 
@@ -311,19 +326,20 @@ class Oracle(_Common):
         _check(self.lib.orc_isect_offset(m, _p(ids), I, tw, th, _p(out)), self.lib, "isect_offset")
 
     def _raster_fwd(self, I, N, ch, m2, con, col, op, bg, masks, W, H, ts, tw, th,
-                    toff, m, fids, rc, ra, li):
-        near = np.zeros(I * H * W, np.uint8)
+                    toff, m, fids, rc, ra, li, threads=None):
         _check(self.lib.orc_raster_fwd(I, N, ch, _p(m2), _p(con), _p(col), _p(op), _p(bg), _p(masks),
                                        W, H, ts, tw, th, _p(toff), m, _p(fids), _p(rc), _p(ra), _p(li),
-                                       _p(near)), self.lib, "raster_fwd")
-        return near.astype(bool)
+                                       threads or raster_threads()), self.lib, "raster_fwd")
 
     def _raster_bwd(self, I, N, ch, m2, con, col, op, bg, masks, W, H, ts, tw, th,
-                    toff, m, fids, ra, li, vrc, vra, absgrad, vabs, vm2, vcon, vcol, vop, vbg):
+                    toff, m, fids, ra, li, vrc, vra, absgrad, vabs, vm2, vcon, vcol, vop, vbg,
+                    threads=None):
+        per_thread = 4 * I * N * (6 + ch + (2 if absgrad else 0))
         _check(self.lib.orc_raster_bwd(I, N, ch, _p(m2), _p(con), _p(col), _p(op), _p(bg), _p(masks),
                                        W, H, ts, tw, th, _p(toff), m, _p(fids), _p(ra), _p(li), _p(vrc),
                                        _p(vra), _p(vabs) if absgrad else None, _p(vm2), _p(vcon),
-                                       _p(vcol), _p(vop), _p(vbg)), self.lib, "raster_bwd")
+                                       _p(vcol), _p(vop), _p(vbg), threads or raster_threads(per_thread)),
+               self.lib, "raster_bwd")
 
     # ---------------- SH training glue (oracle only) ----------------
     def sh_glue_fwd(self, degree, means, viewmats, coeffs, masks=None):
@@ -419,14 +435,14 @@ class Reference(_Common):
         _check(self.lib.ref_isect_offset(m, _p(ids), I, tw, th, _p(out)), self.lib, "ref isect_offset")
 
     def _raster_fwd(self, I, N, ch, m2, con, col, op, bg, masks, W, H, ts, tw, th,
-                    toff, m, fids, rc, ra, li):
+                    toff, m, fids, rc, ra, li, threads=None):
         _check(self.lib.ref_raster_fwd(I, N, ch, _p(m2), _p(con), _p(col), _p(op), _p(bg), _p(masks),
                                        W, H, ts, tw, th, _p(toff), m, _p(fids), _p(rc), _p(ra), _p(li)),
                self.lib, "ref raster_fwd")
-        return None
 
     def _raster_bwd(self, I, N, ch, m2, con, col, op, bg, masks, W, H, ts, tw, th,
-                    toff, m, fids, ra, li, vrc, vra, absgrad, vabs, vm2, vcon, vcol, vop, vbg):
+                    toff, m, fids, ra, li, vrc, vra, absgrad, vabs, vm2, vcon, vcol, vop, vbg,
+                    threads=None):
         _check(self.lib.ref_raster_bwd(I, N, ch, _p(m2), _p(con), _p(col), _p(op), _p(bg), _p(masks),
                                        W, H, ts, tw, th, _p(toff), m, _p(fids), _p(ra), _p(li), _p(vrc),
                                        _p(vra), int(absgrad), _p(vabs), _p(vm2), _p(vcon), _p(vcol),

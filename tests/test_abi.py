@@ -47,17 +47,36 @@ def test_ctypes_signatures_match_header(gs):
         assert len(args) == decls[name], f"{name}: ctypes {len(args)} args, header {decls[name]}"
 
 
-def test_param_struct_layouts(gs):
+def test_param_struct_layouts(gs, tmp_path):
+    """Every ctypes mirror has the size and field offsets that the C
+    compiler gives the header's struct (compiled and run here)."""
+    import shutil
+    import subprocess
     from gsplat_core import _lib as L
-    # Sizes of the POD parameter structs as a C compiler lays them out.
-    assert ct.sizeof(L.QS2CParams) == 24
-    assert ct.sizeof(L.ProjectionParams) == 52
-    assert ct.sizeof(L.SHParams) == 24
-    assert ct.sizeof(L.SHGlueParams) == 24
-    assert ct.sizeof(L.IsectParams) == 36
-    assert ct.sizeof(L.RasterParams) == 64
-    assert ct.sizeof(L.DensifyParams) == 20
-    assert ct.sizeof(L.DensifyMaskParams) == 96
+    cc = shutil.which("cc") or shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    pairs = {"gs_qs2c_params": L.QS2CParams, "gs_projection_params": L.ProjectionParams,
+             "gs_sh_params": L.SHParams, "gs_sh_glue_params": L.SHGlueParams,
+             "gs_isect_params": L.IsectParams, "gs_raster_params": L.RasterParams,
+             "gs_adam_params": L.AdamParams, "gs_densify_params": L.DensifyParams,
+             "gs_densify_mask_params": L.DensifyMaskParams, "gs_spz_params": L.SpzParams}
+    lines = []
+    for cname, py in pairs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stddef.h>\n#include <stdio.h>\n#include \"gsplat_b200.h\"\n"
+                   "int main(void) {\n" + "\n".join(lines) + "\nreturn 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                       text=True).stdout.splitlines())
+    for cname, py in pairs.items():
+        assert int(out[cname]) == ct.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(out[f"{cname}.{f}"]) == getattr(py, f).offset, f"{cname}.{f}"
 
 
 def test_host_helpers(gs):

@@ -1,14 +1,14 @@
 """GPU parity of every operator against the CPU oracle and the golden
 fixtures (the reference's own outputs).  Integer results (radii, tile
-counts, keys, sort order, offsets) must be bit-exact; float forward values
-within 1e-5 abs / 1e-4 rel; gradients within 1e-3 rel.
+counts, keys, sort order, offsets, last ids) must be bit-exact on every
+entry; float forward values within 1e-5 abs / 1e-4 rel; gradients within
+1e-3 rel.
 
-Rasterization decides per pixel x Gaussian whether alpha clears 1/255 and
-whether T(1-alpha) drops to 1e-4; a GPU exp() and the C library's exp()
-may round differently right at those thresholds.  The oracle flags pixels
-whose decision lies within rounding of a threshold (near_threshold); those
-pixels are excluded from forward comparisons and get zero cotangents in
-backward comparisons, and the test asserts they are rare.
+Rasterization decides per pixel x Gaussian whether alpha clears 1/255,
+whether it is clamped at 0.99 and whether T(1-alpha) drops to 1e-4.  The
+kernels make those decisions exactly as the reference does (its sigma, the
+correctly rounded exponential wherever the fast one is within its error of
+a threshold), so every pixel is compared, with no exclusions.
 """
 from __future__ import annotations
 
@@ -86,6 +86,7 @@ def _scene_subset(cfg, n, seed=0):
 @pytest.mark.parametrize("cfg,n,use_opac,comp", [
     ("config1", 10_000, False, False), ("config1", 10_000, True, True),
     ("config3", 200_000, False, False), ("config3", 200_000, True, False),
+    ("config3", 1_000_000, True, True),
 ])
 def test_projection_fwd_exact(gs, oracle, cuda, cfg, n, use_opac, comp):
     sc, idx = _scene_subset(cfg, n)
@@ -99,19 +100,15 @@ def test_projection_fwd_exact(gs, oracle, cuda, cfg, n, use_opac, comp):
     g = gs.projection_ewa_3dgs_fused_forward(inputs, W, H, calc_compensations=comp)
     e = oracle.proj_fwd(means, sc.viewmats[None], sc.Ks[None], W, H, quats=quats, scales=scales,
                         opacities=opac, calc_compensations=comp)
-    # Compiled without FMA contraction in the reference's operation order:
-    # everything but the log() of the opacity-aware extent is bit-identical.
-    if use_opac:
-        rg, re = to_np(g["radii"]), e["radii"]
-        diff = (rg != re).any(-1)
-        assert diff.mean() < 1e-4, f"radii differ on {diff.sum()} entries"
-        ok = ~diff
-        assert_exact(rg[ok], re[ok], "radii")
-    else:
-        assert_exact(g["radii"], e["radii"], "radii")
-        assert_exact(g["means2d"], e["means2d"], "means2d")
-        assert_exact(g["depths"], e["depths"], "depths")
-        assert_exact(g["conics"], e["conics"], "conics")
+    # Compiled without FMA contraction in the reference's operation order,
+    # with the correctly rounded log for the opacity-aware extent: every
+    # output is bit-identical.
+    assert_exact(g["radii"], e["radii"], "radii")
+    assert_exact(g["means2d"], e["means2d"], "means2d")
+    assert_exact(g["depths"], e["depths"], "depths")
+    assert_exact(g["conics"], e["conics"], "conics")
+    if comp:
+        assert_exact(g["compensations"], e["compensations"], "compensations")
     assert_fwd_close(g["means2d"], e["means2d"], "means2d")
     assert_fwd_close(g["depths"], e["depths"], "depths")
     assert_fwd_close(g["conics"], e["conics"], "conics", atol=1e-5 * max(1, np.abs(e["conics"]).max()))
@@ -499,6 +496,44 @@ def test_sort_error_words_clear(gs, cuda):
     assert bool((ok[1:] >= ok[:-1]).all())
 
 
+def test_sort_wait_gives_up_and_reports(gs, cuda):
+    """The give-up path of the bounded look-back wait: a radix pass whose
+    second tile runs alone waits 16 polls for the first, which never
+    publishes, then raises the error word and finishes; the check entry
+    reports GS_ERR_DEVICE (and clears after a normal sort in the same
+    workspace).  Its outputs stay in range: the second tile's keys land at
+    places inside the arrays, the rest keeps the fill."""
+    import ctypes as ct
+    from gsplat_core import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(5)
+    n = 6000
+    keys = T(rng.integers(0, 1 << 12, size=n).astype(np.int64))
+    vals = T(np.arange(n, dtype=np.int32))
+    ok = torch.full_like(keys, -7)
+    ov = torch.full_like(vals, -7)
+    ws = torch.empty(lib.gs_isect_sort_workspace_size(n), dtype=torch.uint8, device="cuda")
+    s = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ct.c_void_p(t.data_ptr())  # noqa: E731
+    assert lib.gs_isect_sort_wait_selftest(n, P(keys), P(vals), P(ok), P(ov), P(ws), ws.numel(),
+                                           16, s) == 0, lib.gs_last_error()
+    assert lib.gs_isect_sort_check(n, P(ws), s) == 6  # GS_ERR_DEVICE
+    assert b"gave up" in lib.gs_last_error()
+    torch.cuda.synchronize()
+    # the 1904 keys of tile 1 were written, each an input key of tile 1
+    written = (ov != -7).cpu().numpy()
+    assert written.sum() == n - 4096
+    assert set(to_np(ov)[written].tolist()) == set(range(4096, n))
+    # bad arguments are refused before any launch
+    assert lib.gs_isect_sort_wait_selftest(4096, P(keys), P(vals), P(ok), P(ov), P(ws),
+                                           ws.numel(), 16, s) == 1
+    assert lib.gs_isect_sort_wait_selftest(n, P(keys), P(vals), P(ok), P(ov), P(ws),
+                                           ws.numel(), 5000, s) == 1
+    # a normal sort in the same workspace clears the word
+    assert lib.gs_isect_sort(n, 44, P(keys), P(vals), P(ok), P(ov), P(ws), ws.numel(), s) == 0
+    assert lib.gs_isect_sort_check(n, P(ws), s) == 0
+
+
 @pytest.mark.parametrize("n", [1, 31, 4095, 4096, 4097, 100_000, 1_000_003])
 @pytest.mark.parametrize("bits", [40, 46, 64])
 def test_sort_stable_exact(gs, oracle, cuda, n, bits):
@@ -541,21 +576,15 @@ def test_rasterize_fwd_bwd(gs, oracle, golden, cuda, name, channels):
     W, H, ts, inp = _raster_case(oracle, name, d, channels)
     e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
     g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, W, H, ts)
-    near = e["near_threshold"]
-    assert near.mean() < 0.01, f"{near.sum()} near-threshold pixels"
-    ok = ~near
-    assert_exact(to_np(g["last_ids"])[ok], e["last_ids"][ok], "last_ids")
-    assert_fwd_close(to_np(g["render_alphas"])[..., 0][ok], e["render_alphas"][..., 0][ok], "alphas")
-    assert_fwd_close(to_np(g["render_colors"])[ok], e["render_colors"][ok], "colors")
+    assert_exact(to_np(g["last_ids"]), e["last_ids"], "last_ids")
+    assert_fwd_close(to_np(g["render_alphas"]), e["render_alphas"], "alphas")
+    assert_fwd_close(to_np(g["render_colors"]), e["render_colors"], "colors")
     if channels == 3:
-        gold_ok = ~near
-        assert_fwd_close(to_np(g["render_colors"])[gold_ok], d["rf_render_colors"][gold_ok],
-                         "colors vs golden")
-    # Backward from the oracle's forward state, near-threshold pixels muted.
+        assert_exact(to_np(g["last_ids"]), d["rf_last_ids"], "last_ids vs golden")
+        assert_fwd_close(to_np(g["render_colors"]), d["rf_render_colors"], "colors vs golden")
+    # Backward from the oracle's forward state, every pixel driven.
     vrc = np.random.default_rng(5).normal(size=e["render_colors"].shape).astype(np.float32)
     vra = np.random.default_rng(6).normal(0, 0.1, size=e["render_alphas"].shape).astype(np.float32)
-    vrc[near] = 0
-    vra[near] = 0
     fo = {"render_alphas": e["render_alphas"], "last_ids": e["last_ids"]}
     b = gs.rasterize_to_pixels_3dgs_backward(
         {k: T(v) for k, v in inp.items()}, {k: T(v) for k, v in fo.items()},
@@ -596,11 +625,10 @@ def test_rasterize_masks_backward(gs, oracle, golden, cuda):
     inp = dict(inp, masks=masks)
     e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
     g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, W, H, ts)
-    ok = ~e["near_threshold"]
-    assert_fwd_close(to_np(g["render_colors"])[ok], e["render_colors"][ok], "masked colors")
+    assert_exact(to_np(g["last_ids"]), e["last_ids"], "masked last_ids")
+    assert_fwd_close(to_np(g["render_colors"]), e["render_colors"], "masked colors")
     vrc = np.random.default_rng(5).normal(size=e["render_colors"].shape).astype(np.float32)
     vra = np.zeros(e["render_alphas"].shape, np.float32)
-    vrc[~ok] = 0
     b = gs.rasterize_to_pixels_3dgs_backward(
         {k: T(v) for k, v in inp.items()},
         {"render_alphas": T(e["render_alphas"]), "last_ids": T(e["last_ids"])},
@@ -652,17 +680,13 @@ def test_rasterize_tile_cull_boundary(gs, oracle, cuda):
                flatten_ids=np.arange(I, dtype=np.int32))
     e = oracle.raster_fwd(width=16, height=16, tile_size=16, **inp)
     g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, 16, 16, 16)
-    near = e["near_threshold"]
-    ok = ~near
-    assert_exact(to_np(g["last_ids"])[ok], e["last_ids"][ok], "last_ids")
+    assert_exact(to_np(g["last_ids"]), e["last_ids"], "last_ids")
     ga = to_np(g["render_alphas"])[..., 0]
-    assert_fwd_close(ga[ok], e["render_alphas"][..., 0][ok], "alphas")
+    assert_fwd_close(ga, e["render_alphas"][..., 0], "alphas")
     hit = ga.reshape(I, -1).max(1) > 0
     assert np.array_equal(hit, np.array(above)), "a Gaussian reaching the threshold was dropped"
     vrc = rng.normal(size=e["render_colors"].shape).astype(np.float32)
     vra = rng.normal(0, 0.1, size=e["render_alphas"].shape).astype(np.float32)
-    vrc[near] = 0
-    vra[near] = 0
     b = gs.rasterize_to_pixels_3dgs_backward(
         {k: T(v) for k, v in inp.items()},
         {"render_alphas": T(e["render_alphas"]), "last_ids": T(e["last_ids"])},
@@ -671,3 +695,140 @@ def test_rasterize_tile_cull_boundary(gs, oracle, cuda):
                            last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra, **inp)
     for k, v in eb.items():
         assert_grad_close(b[k], v, f"cull {k}", atol_frac=1e-4)
+
+
+def _threshold_cases(seed=31, per_kind=700):
+    """One 16x16 image per case, one tile, a short list of Gaussians whose
+    decisions at pixel (7, 9) sit within a few ulps of a threshold, computed
+    with the C library's expf and float32 arithmetic in the reference's
+    order: alpha against 1/255, o e^-sigma against the 0.99 clamp, and
+    T (1 - alpha) against 1e-4 (with exact and with inexact exponentials)."""
+    import ctypes
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.restype = ctypes.c_float
+    libm.expf.argtypes = [ctypes.c_float]
+    f = np.float32
+    expf = lambda x: f(libm.expf(f(x)))  # noqa: E731
+    rng = np.random.default_rng(seed)
+    px, py = f(7.5), f(9.5)
+
+    def sigma(m, c):
+        dx, dy = f(m[0]) - px, f(m[1]) - py
+        return f(0.5) * (c[0] * dx * dx + c[2] * dy * dy) + c[1] * dx * dy
+
+    def conic(scale):
+        th = rng.uniform(0, np.pi)
+        s1 = scale
+        s2 = s1 / rng.uniform(1, 8)
+        R = np.array([[np.cos(th), -np.sin(th)], [np.sin(th), np.cos(th)]])
+        inv = np.linalg.inv(R @ np.diag([s1 * s1, s2 * s2]) @ R.T)
+        return np.array([inv[0, 0], inv[0, 1], inv[1, 1]], np.float32)
+
+    def nudge(v, k):   # k ulps away
+        return (np.array([v], np.float32).view(np.int32) + np.int32(k)).view(np.float32)[0]
+
+    cases = []
+    for i in range(per_kind):            # alpha against 1/255
+        c = conic(rng.uniform(1.0, 6.0))
+        m = np.array([7.5, 9.5], np.float32) + rng.uniform(-6, 6, 2).astype(np.float32)
+        s = sigma(m, c)
+        e = expf(-s)
+        if not (0 <= s < 5.0):
+            continue
+        o = f(f(1.0 / 255.0) / e)
+        o = nudge(o, int(rng.integers(-3, 4)))
+        if o >= 1:
+            continue
+        cases.append(([m], [c], [o]))
+    for i in range(per_kind):            # o e^-sigma against the 0.99 clamp
+        c = conic(rng.uniform(2.0, 6.0))
+        m = np.array([7.5, 9.5], np.float32) + rng.uniform(-0.2, 0.2, 2).astype(np.float32)
+        s = sigma(m, c)
+        e = expf(-s)
+        o = nudge(f(f(0.99) / e), int(rng.integers(-3, 4)))
+        if not (0 <= s and o <= 1):
+            continue
+        cases.append(([m], [c], [o]))
+    for exact_exp in (True, False):      # T (1 - alpha) against 1e-4
+        for i in range(per_kind):
+            k = int(rng.integers(4, 12))
+            ms, cs, os_ = [], [], []
+            T = f(1.0)
+            for j in range(k - 1):
+                c = conic(rng.uniform(3.0, 8.0))
+                m = (np.array([7.5, 9.5], np.float32) if exact_exp else
+                     np.array([7.5, 9.5], np.float32) + rng.uniform(-1, 1, 2).astype(np.float32))
+                o = f(rng.uniform(0.3, 0.8))
+                a = min(f(0.99), o * expf(-sigma(m, c)))
+                if sigma(m, c) < 0 or a < f(1 / 255):
+                    continue
+                nT = T * (f(1) - a)
+                if nT <= f(2e-4):
+                    break
+                T = nT
+                ms.append(m); cs.append(c); os_.append(o)
+            c = conic(rng.uniform(3.0, 8.0))
+            m = (np.array([7.5, 9.5], np.float32) if exact_exp else
+                 np.array([7.5, 9.5], np.float32) + rng.uniform(-1, 1, 2).astype(np.float32))
+            e = expf(-sigma(m, c))
+            need = (1.0 - 1e-4 / float(T)) / float(e)
+            if not (0.02 < need < 0.97):
+                continue
+            o = nudge(f(need), int(rng.integers(-4, 5)))
+            ms.append(m); cs.append(c); os_.append(o)
+            cases.append((ms, cs, os_))
+    return cases
+
+
+def _threshold_inputs(channels):
+    cases = _threshold_cases()
+    I = len(cases)
+    N = max(len(c[2]) for c in cases)
+    rng = np.random.default_rng(32)
+    means = np.zeros((I, N, 2), np.float32)
+    conics = np.tile(np.array([1, 0, 1], np.float32), (I, N, 1))
+    opac = np.zeros((I, N), np.float32)
+    fids, offs = [], []
+    for i, (ms, cs, os_) in enumerate(cases):
+        offs.append(len(fids))
+        for j in range(len(os_)):
+            means[i, j], conics[i, j], opac[i, j] = ms[j], cs[j], os_[j]
+            fids.append(i * N + j)
+    inp = dict(means2d=means, conics=conics, opacities=opac,
+               colors=rng.uniform(0, 1, size=(I, N, channels)).astype(np.float32),
+               tile_offsets=np.array(offs, np.int32).reshape(I, 1, 1),
+               flatten_ids=np.array(fids, np.int32),
+               backgrounds=np.tile(np.linspace(0.1, 0.3, channels, dtype=np.float32), (I, 1)))
+    return cases, offs, inp
+
+
+@pytest.mark.parametrize("channels", [3, 5])
+def test_rasterize_threshold_decisions_exact(gs, oracle, cuda, channels):
+    """Decisions within a few ulps of 1/255, 0.99 and 1e-4 (16x16 kernels
+    with 3 channels, the generic kernels with 5): last ids bit for bit,
+    renders and gradients as the oracle's on every pixel; the cases fall on
+    both sides of each threshold."""
+    cases, offs, inp = _threshold_inputs(channels)
+    rng = np.random.default_rng(33)
+    e = oracle.raster_fwd(width=16, height=16, tile_size=16, **inp)
+    # both outcomes occur at the target pixel
+    lid = e["last_ids"][:, 9, 7] - np.array(offs)
+    nk = np.array([len(c[2]) for c in cases])
+    alpha_p = e["render_alphas"][:, 9, 7, 0]
+    assert (alpha_p == 0).any() and (alpha_p > 0).any()
+    assert (lid == nk - 1).any() and (lid == nk - 2).any()
+    g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, 16, 16, 16)
+    assert_exact(to_np(g["last_ids"]), e["last_ids"], "last_ids")
+    assert_fwd_close(to_np(g["render_alphas"]), e["render_alphas"], "alphas")
+    assert_fwd_close(to_np(g["render_colors"]), e["render_colors"], "colors")
+    vrc = rng.normal(size=e["render_colors"].shape).astype(np.float32)
+    vra = rng.normal(0, 0.1, size=e["render_alphas"].shape).astype(np.float32)
+    b = gs.rasterize_to_pixels_3dgs_backward(
+        {k: T(v) for k, v in inp.items()},
+        {"render_alphas": T(e["render_alphas"]), "last_ids": T(e["last_ids"])},
+        {"v_render_colors": T(vrc), "v_render_alphas": T(vra)}, 16, 16, 16, absgrad=True)
+    eb = oracle.raster_bwd(width=16, height=16, tile_size=16, render_alphas=e["render_alphas"],
+                           last_ids=e["last_ids"], v_render_colors=vrc, v_render_alphas=vra,
+                           absgrad=True, **inp)
+    for k, v in eb.items():
+        assert_grad_close(b[k], v, f"threshold {k}", atol_frac=1e-4)

@@ -35,11 +35,12 @@ def _chain_case(oracle, d):
     rf = oracle.raster_fwd(m2, proj["conics"].reshape(1, -1, 3), d["colors"],
                            d["opacities"][None], out["tile_offsets"], it["flatten_ids"], W, H, ts,
                            backgrounds=d["backgrounds"])
-    out.update({"rf_" + k: v for k, v in rf.items() if k != "near_threshold"})
+    out.update({"rf_" + k: v for k, v in rf.items()})
     rb = oracle.raster_bwd(m2, proj["conics"].reshape(1, -1, 3), d["colors"],
                            d["opacities"][None], out["tile_offsets"], it["flatten_ids"], W, H, ts,
                            rf["render_alphas"], rf["last_ids"], d["v_render_colors"],
-                           d["v_render_alphas"], backgrounds=d["backgrounds"], absgrad=True)
+                           d["v_render_alphas"], backgrounds=d["backgrounds"], absgrad=True,
+                           threads=1)
     out.update({"rb_" + k: v for k, v in rb.items()})
     shb = oracle.sh_bwd(deg, d["dirs"], d["coeffs"], d["v_sh"])
     out.update({"shb_" + k: v for k, v in shb.items()})

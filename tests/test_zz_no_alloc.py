@@ -35,8 +35,9 @@ def _keys(n, bits, seed):
 def test_noalloc_sort_matches_workspace_sort(gs, cuda):
     lib = gs.load()
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # Two calls in a row: the second must not see anything of the first.
-    for n, bits, seed in ((300_001, 46, 1), (MAX_ISECTS, 64, 2)):
+    # Calls in a row, small then the largest then small again: none may see
+    # anything of the one before it in the shared scratch array.
+    for n, bits, seed in ((300_001, 46, 1), (MAX_ISECTS, 64, 2), (5_000, 46, 3)):
         k, v = _keys(n, bits, seed)
         keys = torch.from_numpy(k).to(cuda)
         vals = torch.from_numpy(v).to(cuda)
@@ -47,9 +48,14 @@ def test_noalloc_sort_matches_workspace_sort(gs, cuda):
                                        ct.c_void_p(vals.data_ptr()), ct.c_void_p(got_k.data_ptr()),
                                        ct.c_void_p(got_v.data_ptr()), stream)
         assert rc == 0, lib.gs_last_error()
+        # no bounded wait of this sort gave up
+        assert lib.gs_isect_sort_noalloc_check(n, stream) == 0, lib.gs_last_error()
         torch.cuda.synchronize()
         assert_exact(got_k, want_k, f"keys (n={n})")
         assert_exact(got_v, want_v, f"values (n={n})")
+    # an empty sort launches nothing and succeeds
+    assert lib.gs_isect_sort_noalloc(0, 46, None, None, None, None, stream) == 0
+    assert lib.gs_isect_sort_noalloc_check(0, stream) == 0
 
 
 def test_noalloc_sort_rejects_oversize(gs, cuda):
