@@ -16,8 +16,8 @@ per-Gaussian gradients are summed with one NCCL all-reduce per step.
 Prints one JSON line (rank 0).  `value` is Mpix/s over all ranks; ms/step and
 intersections sorted/s ride along.  The reference arm times the
 reference's own CPU code (eval_cpu compiled from the reference sources,
-oracle/_ref) -- or the C restatement when that build is absent -- on a
-bounded sample of the same workload.
+oracle/_ref) -- or the C restatement when that build is absent -- running
+full steps of the same workload on every host thread (oracle/ref_step.py).
 """
 from __future__ import annotations
 
@@ -224,43 +224,26 @@ def our_kernel_launches(entry_passes, bins, slots, tile_cull=False):
 
 # ------------------------------------------------------------------ CPU arms
 
-def cpu_step(checker, sc, vrc, vra, stride):
-    """One reference-CPU step on a bounded sample: projection, SH colours
-    and the intersection pipeline over all Gaussians; rasterize fwd+bwd on
-    every `stride`-th tile (tile masks), with the raster time scaled by
-    `stride`.  Returns (seconds, extrapolated seconds, intersections,
-    seconds of the intersect encode + sort)."""
-    t0 = time.perf_counter()
-    p = checker.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
-                         quats=sc.quats[None], scales=sc.scales[None])
-    campos = -(sc.viewmats[0, :3, :3].T @ sc.viewmats[0, :3, 3])
-    dirs = (sc.means - campos).astype(np.float32)
-    dirs /= np.maximum(np.linalg.norm(dirs, axis=-1, keepdims=True), 1e-8)
-    colors = np.clip(checker.sh_fwd(sc.sh_degree, dirs, sc.coeffs) + 0.5, 0, 1)[None]
-    m2 = p["means2d"].reshape(1, -1, 2)
-    ti = time.perf_counter()
-    it = checker.isect_tile(m2, p["radii"].reshape(1, -1, 2), p["depths"].reshape(1, -1), 1,
-                            sc.tile_size, sc.tile_width, sc.tile_height)
-    t_isect = time.perf_counter() - ti
-    offs = checker.isect_offset(it["isect_ids"], 1, sc.tile_width, sc.tile_height)
-    t1 = time.perf_counter()
-    masks = np.zeros((1, sc.tile_height, sc.tile_width), bool)
-    masks.reshape(-1)[::stride] = True
-    kw = dict(means2d=m2, conics=p["conics"].reshape(1, -1, 3), colors=colors,
-              opacities=sc.opacities[None], tile_offsets=offs, flatten_ids=it["flatten_ids"],
-              width=sc.width, height=sc.height, tile_size=sc.tile_size, masks=masks)
-    rf = checker.raster_fwd(**kw)
-    rb = checker.raster_bwd(render_alphas=rf["render_alphas"], last_ids=rf["last_ids"],
-                            v_render_colors=vrc, v_render_alphas=vra, **kw)
-    t2 = time.perf_counter()
-    checker.sh_bwd(sc.sh_degree, dirs, sc.coeffs, rb["v_colors"][0])
-    checker.proj_bwd(sc.means[None], sc.viewmats[None], sc.Ks[None], sc.width, sc.height,
-                     p["radii"], p["conics"], rb["v_means2d"][None],
-                     np.zeros(p["depths"].shape, np.float32), rb["v_conics"][None],
-                     quats=sc.quats[None], scales=sc.scales[None])
-    t3 = time.perf_counter()
-    full = (t1 - t0) + (t2 - t1) * stride + (t3 - t2)
-    return t3 - t0, full, int(it["isect_ids"].size), t_isect
+def cpu_steps(checker, sc, vrc, vra, steps, warmup):
+    """The reference's CPU step of one camera, timed in full on every host
+    thread (oracle.ref_step: the reference's own eval_cpu code per Gaussian
+    chunk / tile set, the Metal culling applied, the same intersections as
+    the GPU step).  Returns (seconds per step, intersections, seconds of the
+    intersect pipeline per step, threads)."""
+    from oracle.ref_step import ParallelReferenceStep
+    st = ParallelReferenceStep(checker, sc, vrc, vra)
+    try:
+        for _ in range(warmup):
+            st.run()
+        secs, isect = [], []
+        m = 0
+        for _ in range(steps):
+            t, m, ti = st.run()
+            secs.append(t)
+            isect.append(ti)
+    finally:
+        st.close()
+    return float(np.mean(secs)), m, float(np.mean(isect)), st.T
 
 
 def composited_pairs(step):
@@ -291,6 +274,11 @@ def make_checker():
 
 
 def run_reference_arm(args):
+    """The reference's CPU path on the same workload: each step is one full
+    camera step (every Gaussian, every tile, forward and backward), timed
+    wall-clock on all host threads; multi-camera workloads time one camera
+    per step and scale by the camera count (stated in `sample`).  Under
+    torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
@@ -300,23 +288,15 @@ def run_reference_arm(args):
     cams = full_sc.cameras
     sc = first_camera(full_sc)
     vrc, vra = S.cotangents(args.seed, 1, sc.height, sc.width)
-    stride = args.cpu_stride
-    for _ in range(args.warmup):
-        cpu_step(checker, sc, vrc, vra, stride)
-    fulls = []
-    isects = []
-    m = 0
-    for _ in range(args.steps):
-        _, full, m, t_isect = cpu_step(checker, sc, vrc, vra, stride)
-        fulls.append(full)
-        isects.append(t_isect)
-    ms = 1e3 * float(np.mean(fulls)) * cams
+    sec, m, t_isect, threads = cpu_steps(checker, sc, vrc, vra, args.steps, args.warmup)
+    ms = 1e3 * sec * cams
     pixels = sc.width * sc.height * cams
     value = pixels / (ms / 1e3) / 1e6
-    sample = (f"{args.workload} step of one camera; projection/SH/intersect on all {sc.n} "
-              f"Gaussians, rasterize fwd+bwd on every {stride}th of "
-              f"{sc.tile_width * sc.tile_height} tiles, raster time scaled x{stride} "
-              f"(extrapolated)" + (f"; x{cams} cameras (extrapolated)" if cams > 1 else ""))
+    sample = (f"{args.workload}: every step one full camera step timed wall-clock "
+              f"(projection, SH, intersect on all {sc.n} Gaussians, rasterize fwd+bwd on all "
+              f"{sc.tile_width * sc.tile_height} tiles, SH and projection backward) on "
+              f"{threads} host threads" +
+              (f"; x{cams} cameras (one camera per step, scaled)" if cams > 1 else ""))
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "Mpix/s",
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": round(ms, 3), "higher_is_better": True,
@@ -324,8 +304,8 @@ def run_reference_arm(args):
            "data": f"synthetic (seeded, BASELINE {args.workload} shapes)",
            "config": {"workload": WORKLOADS[args.workload][0], "cameras": cams,
                       "gaussians": sc.n, "isects_per_camera": m},
-           "intersections_sorted_per_s": round(m / float(np.mean(isects)), 1),
-           "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": 1,
+           "intersections_sorted_per_s": round(m / t_isect, 1),
+           "cpu_baseline": {"value": round(value, 4), "unit": "Mpix/s", "cores": threads,
                             "kind": kind, "sample": sample},
            "e2e": {"value": round(value, 4), "unit": "Mpix/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -573,12 +553,13 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             checker, kind = make_checker()
             sc0 = first_camera(sc)
-            _, full, _, _ = cpu_step(checker, sc0, vrc_np[:1], vra_np[:1], args.cpu_stride)
-            cpu = {"value": round(sc0.width * sc0.height / full / 1e6, 4), "unit": "Mpix/s",
-                   "cores": 1, "kind": kind,
-                   "sample": (f"one camera of the {args.workload} step; rasterize fwd+bwd on "
-                              f"every {args.cpu_stride}th tile, raster time scaled "
-                              f"x{args.cpu_stride} (extrapolated); other stages in full; the "
+            sec, _, _, threads = cpu_steps(checker, sc0, vrc_np[:1], vra_np[:1],
+                                           args.cpu_steps, 1)
+            cpu = {"value": round(sc0.width * sc0.height / sec / 1e6, 4), "unit": "Mpix/s",
+                   "cores": threads, "kind": kind,
+                   "sample": (f"{args.cpu_steps} full steps of one camera of the "
+                              f"{args.workload} step (every tile, forward and backward) after "
+                              f"one warm-up step, wall-clock on {threads} host threads; the "
                               f"per-camera rate stands for all {C_total} cameras")}
         out = {
             "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
@@ -628,7 +609,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-stride", type=int, default=8)
+    ap.add_argument("--cpu-steps", type=int, default=3,
+                    help="full reference steps timed for the cpu_baseline field")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3",
                     help="BASELINE config (cfg3 is the headline; the others fill the "

@@ -62,7 +62,7 @@ constexpr float kStepErr = 2.0e-7f;    // three roundings of 2^-24
 // calls, returns the same float on all but 7.7e-5 of the floats in
 // [-16, 0] (exhaustive comparison), and there by one ulp, which moves a
 // decision only when the product o e^-sigma itself sits on a threshold.
-__device__ __noinline__ float exp_cr(float x) { return __double2float_rn(exp((double)x)); }
+__device__ __forceinline__ float exp_cr(float x) { return __double2float_rn(exp((double)x)); }
 
 __device__ __forceinline__ float next_up(float x) { return nextafterf(x, INFINITY); }
 __device__ __forceinline__ float next_down(float x) { return nextafterf(x, -INFINITY); }
@@ -226,24 +226,25 @@ __device__ __forceinline__ void tile_range(const RArgs& a, int64_t slot, int& st
 // per thread; the next chunk's loads are issued before this one is folded)
 // the composited entries are compacted in list order into shared memory
 // with their colours, thread 0 folds them into T in order (stopping where
-// the reference stops), and thread c sums channel c (and c + kWalk) over
-// the folded entries in order.  The longest walk bounds the fix-up
+// the reference stops) together with the colour sums (with a runtime
+// channel count, thread c sums channel c and c + kWalk afterwards).  The longest walk bounds the fix-up
 // kernel's time, so a walk gets every thread of the CTA.
 constexpr int kWalk = 256;
 
 struct WalkSmem {
-  float al[kWalk];       // alpha of the kept entries, in list order
-  int g[kWalk];          // their Gaussian
-  int ix[kWalk];         // their list index
-  float vis[kWalk];      // alpha T of the folded ones
-  float col[kWalk][4];   // their colours (CH in 1..4)
+  __align__(16) float al[kWalk + 4];      // alpha of the kept entries, in list order
+  int g[kWalk];                           // their Gaussian
+  __align__(16) int ix[kWalk + 4];        // their list index
+  float vis[kWalk];                       // alpha T of the folded ones
+  __align__(16) float col[kWalk + 4][4];  // their colours (CH in 1..4)
   int wcnt[kWalk / 32];  // kept entries per warp
   float T;
   int cur, nfold, stop;
 };
 
 template <int CH>
-__device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int image, int64_t pix,
+__device__ __forceinline__ void exact_walk(const RArgs& a, int start, int end, int image,
+                                           int64_t pix,
                                         float px, float py, WalkSmem& w, float* render_colors,
                                         float* render_alphas, int32_t* last_ids) {
   const int ch = CH > 0 ? CH : a.CH;
@@ -253,10 +254,14 @@ __device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int 
     w.cur = 0;
     w.stop = 0;
   }
-  float acc0 = 0.0f, acc1 = 0.0f;  // channels tid and tid + kWalk (<= 64)
+  float acc0 = 0.0f, acc1 = 0.0f;  // CH == 0: channels tid and tid + kWalk (<= 64)
+  float acc[CH > 0 ? CH : 1];       // CH > 0: thread 0's colour sums
+#pragma unroll
+  for (int c = 0; c < (CH > 0 ? CH : 1); ++c) acc[c] = 0.0f;
   int g = 0;
   float2 m = make_float2(0.f, 0.f), sb = make_float2(0.f, 0.f);
   float c0 = 0.f, c1 = 0.f, c2 = 0.f, o = 0.f;
+  float4 cl = make_float4(0.f, 0.f, 0.f, 0.f);  // CH > 0: the entry's colour
   auto load = [&](int cb) {
     const int idx = cb + tid;
     if (idx < end) {
@@ -268,6 +273,13 @@ __device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int 
       c2 = __ldg(con + 2);
       o = __ldg(a.opacities + opac_index(a, g));
       if (a.sbounds) sb = __ldg(a.sbounds + opac_index(a, g));
+      if (CH > 0) {
+        const float* cp = a.colors + (int64_t)g * ch;
+        cl.x = __ldg(cp);
+        if (CH > 1) cl.y = __ldg(cp + 1);
+        if (CH > 2) cl.z = __ldg(cp + 2);
+        if (CH > 3) cl.w = __ldg(cp + 3);
+      }
     }
   };
   load(start);
@@ -276,6 +288,7 @@ __device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int 
     bool take = false;
     float al = 0.0f;
     const int gk = g;
+    const float4 clk = cl;
     if (idx < end) {
       const float sigma = gauss_sigma(__fsub_rn(m.x, px), __fsub_rn(m.y, py), c0, c1, c2).s;
       if (!a.sbounds) sb = sigma_bounds(o);
@@ -298,37 +311,56 @@ __device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int 
       w.al[slot] = al;
       w.g[slot] = gk;
       w.ix[slot] = idx;
-      if (CH > 0) {
-#pragma unroll
-        for (int c = 0; c < (CH > 0 ? CH : 1); ++c)
-          w.col[slot][c] = __ldg(a.colors + (int64_t)gk * ch + c);
-      }
+      if (CH > 0) *reinterpret_cast<float4*>(w.col[slot]) = clk;
     }
     __syncthreads();
     if (tid == 0) {
+      // T and, with CH > 0, the colour sums (thread 0 keeps them in acc[])
+      // four entries per round from vector loads, so that the shared
+      // memory reads do not sit on the T recurrence
       float T = w.T;
       int k = 0, cur = w.cur;
-      for (; k < cnt; ++k) {
-        const float ak = w.al[k];
-        const float nT = __fmul_rn(T, __fsub_rn(1.0f, ak));
-        if (nT <= kTransmittanceThreshold) {
-          w.stop = 1;
-          break;
+      bool stop = false;
+      for (int k4 = 0; k4 < cnt && !stop; k4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(w.al + k4);
+        const int4 i4 = *reinterpret_cast<const int4*>(w.ix + k4);
+        float4 col4[4];
+        if (CH > 0) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) col4[j] = *reinterpret_cast<const float4*>(w.col[k4 + j]);
         }
-        w.vis[k] = __fmul_rn(ak, T);
-        cur = w.ix[k];
-        T = nT;
+        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+        const int iv[4] = {i4.x, i4.y, i4.z, i4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (k4 + j >= cnt || stop) break;
+          const float nT = __fmul_rn(T, __fsub_rn(1.0f, av[j]));
+          if (nT <= kTransmittanceThreshold) {
+            stop = true;
+            break;
+          }
+          const float vis = __fmul_rn(av[j], T);
+          if (CH > 0) {
+            const float cc[4] = {col4[j].x, col4[j].y, col4[j].z, col4[j].w};
+#pragma unroll
+            for (int c = 0; c < (CH > 0 ? CH : 1); ++c)
+              acc[c] = __fadd_rn(acc[c], __fmul_rn(cc[c], vis));
+          } else {
+            w.vis[k4 + j] = vis;
+          }
+          cur = iv[j];
+          T = nT;
+          k = k4 + j + 1;
+        }
       }
+      if (stop) w.stop = 1;
       w.T = T;
       w.cur = cur;
       w.nfold = k;
     }
     __syncthreads();
     const int nf = w.nfold;
-    if (CH > 0) {
-      if (tid < CH)
-        for (int k = 0; k < nf; ++k) acc0 = __fadd_rn(acc0, __fmul_rn(w.col[k][tid], w.vis[k]));
-    } else {
+    if (CH == 0) {
       for (int k = 0; k < nf; ++k) {
         const float vis = w.vis[k];
         const int64_t gq = w.g[k];
@@ -342,11 +374,21 @@ __device__ __noinline__ void exact_walk(const RArgs& a, int start, int end, int 
     if (stop) break;
   }
   const float T = w.T;
-  for (int j = 0; j < 2; ++j) {
-    const int c = tid + j * kWalk;
-    if (c < ch) {
-      const float bg = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
-      render_colors[pix * ch + c] = __fadd_rn(j ? acc1 : acc0, __fmul_rn(T, bg));
+  if (CH > 0) {
+    if (tid == 0) {
+#pragma unroll
+      for (int c = 0; c < (CH > 0 ? CH : 1); ++c) {
+        const float bg = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
+        render_colors[pix * ch + c] = __fadd_rn(acc[c], __fmul_rn(T, bg));
+      }
+    }
+  } else {
+    for (int j = 0; j < 2; ++j) {
+      const int c = tid + j * kWalk;
+      if (c < ch) {
+        const float bg = a.backgrounds ? __ldg(a.backgrounds + image * ch + c) : 0.0f;
+        render_colors[pix * ch + c] = __fadd_rn(j ? acc1 : acc0, __fmul_rn(T, bg));
+      }
     }
   }
   if (tid == 0) {
@@ -466,11 +508,12 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
 
 // Recomputes exactly the pixels that the forward kernel left undecided
 // (last_ids == kUndecided).  The CTAs scan the rendered rows in row-major
-// order, kFixPixels pixels per CTA (one wave covers an image of millions of
-// pixels), and walk each undecided pixel they find with all their threads
+// order, one pixel per thread (so that the few undecided pixels land in
+// different CTAs and are walked at once), and walk each undecided pixel they
+// find with all their threads
 // (exact_walk).  Kept out of the forward kernels: the walk code there took
 // registers from the compositing loop.
-constexpr int kFixPixels = 4 * kWalk;
+constexpr int kFixPixels = kWalk;
 
 template <int CH>
 __global__ void __launch_bounds__(kWalk) raster_fix_kernel(RArgs a,

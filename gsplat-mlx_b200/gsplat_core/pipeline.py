@@ -96,6 +96,9 @@ class TrainingStep:
         self.conics, self.radii = e((C, N, 3)), e((C, N, 2), i32)
         self.colors = e((C, N, 3))
         self.sbounds = e((N, 2))  # exact alpha decisions per opacity (sigma bounds)
+        # the sigma bounds run on a side stream, beside the intersection
+        # encode (a chain of small, latency-bound kernels)
+        self.side = torch.cuda.Stream(device=self.dev)
         self.tiles_per_gauss = e((C, N), i32)
         # [intersections, bin entries of the binned encode]
         self.total = torch.zeros((2,), dtype=torch.int64, device=self.dev)
@@ -204,6 +207,9 @@ class TrainingStep:
                                   _p(viewmats), _p(Ks), _p(self.means2d), _p(self.depths),
                                   _p(self.conics), None, _p(self.radii), s), "projection_fwd")
         self._mark("projection_fwd")
+        projected = torch.cuda.Event()
+        projected.record()
+        bounded = None
         gp = SHGlueParams(C, N, self.K, self.deg, 0)
         glue_pending = colors is None
         if glue_pending:
@@ -240,12 +246,16 @@ class TrainingStep:
                                        _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
                 self._mark("sh_fwd")
                 glue_pending = False
-            if b == 0:
-                check(L.gs_rasterize_sigma_bounds(N, _p(opac), _p(self.radii), C,
-                                                  _p(self.sbounds), s),
-                      "rasterize_sigma_bounds")
-                self._mark("sigma_bounds")
             counted.synchronize()  # the reference's host read of the total
+            if bounded is None:
+                # launched now, the bounds kernel runs beside the encode
+                self.side.wait_event(projected)
+                check(L.gs_rasterize_sigma_bounds(N, _p(opacities), _p(self.radii), C,
+                                                  _p(self.sbounds),
+                                                  ct.c_void_p(self.side.cuda_stream)),
+                      "rasterize_sigma_bounds")
+                bounded = torch.cuda.Event()
+                bounded.record(self.side)
             m, bins = (int(v) for v in self.total_host.tolist())
             if m > self.max_isects_per_pass and y1 == 0:
                 # too many intersections for one pass (int32 offsets, memory):
@@ -298,6 +308,7 @@ class TrainingStep:
                 check(L.gs_isect_offset_rows(m, _p(self.sorted_ids), C, self.tw, self.th, r0, r1,
                                              _p(self.tile_offsets), s), "isect_offset")
                 self._mark("isect_offset")
+            torch.cuda.current_stream().wait_event(bounded)
             rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
                               int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0), 1,
                               _p(self.sbounds))

@@ -273,3 +273,44 @@ def test_densify_oracle_matches_reference(golden):
                 int(d["step"]), n, cfg, grow=False, prune=True)
     assert_exact(np.nonzero(~p["prune"])[0], d["prune_keep"], "prune keep set")
     assert_exact(p["prune_breakdown"], d["prune_breakdown"], "prune breakdown")
+
+
+def test_parallel_reference_step_matches_one_thread(oracle):
+    """bench.py's reference arm splits the reference's step over host
+    threads (oracle/ref_step.py): Gaussian chunks, a stable merge of the
+    chunks' sorted lists, tile sets per thread.  Its lists and forward
+    outputs are those of one single-threaded pass bit for bit, its
+    gradients the same up to the order of the float sums."""
+    from gsplat_core import synthetic as S
+    from oracle.ref_step import ParallelReferenceStep, metal_cull
+    sc = S.config3(seed=3, n=20_000)
+    sc.Ks = sc.Ks.copy()
+    sc.Ks[:, :2, :] /= 4
+    sc.width, sc.height = sc.width // 4, sc.height // 4
+    vrc, vra = S.cotangents(3, 1, sc.height, sc.width)
+    st = ParallelReferenceStep(oracle, sc, vrc, vra, threads=5)
+    _, m, _ = st.run()
+    st.close()
+    got = st.last
+    W, H = sc.width, sc.height
+    p = metal_cull(oracle.proj_fwd(sc.means[None], sc.viewmats[None], sc.Ks[None], W, H,
+                                   quats=sc.quats[None], scales=sc.scales[None]), W, H)
+    N = sc.n
+    it = oracle.isect_tile(p["means2d"].reshape(1, N, 2), p["radii"].reshape(1, N, 2),
+                           p["depths"].reshape(1, N), 1, 16, sc.tile_width, sc.tile_height)
+    assert m == it["isect_ids"].size
+    assert_exact(got["isect_ids"], it["isect_ids"], "keys")
+    assert_exact(got["flatten_ids"], it["flatten_ids"], "flatten ids")
+    offs = oracle.isect_offset(it["isect_ids"], 1, sc.tile_width, sc.tile_height)
+    assert_exact(got["tile_offsets"], offs, "offsets")
+    kw = dict(means2d=p["means2d"].reshape(1, N, 2), conics=p["conics"].reshape(1, N, 3),
+              colors=got["colors"], opacities=sc.opacities[None], tile_offsets=offs,
+              flatten_ids=it["flatten_ids"], width=W, height=H, tile_size=16)
+    rf = oracle.raster_fwd(threads=1, **kw)
+    for k, v in rf.items():
+        assert_exact(got["rf_" + k], v, k)
+    rb = oracle.raster_bwd(render_alphas=rf["render_alphas"], last_ids=rf["last_ids"],
+                           v_render_colors=vrc, v_render_alphas=vra, threads=1, **kw)
+    for k, v in rb.items():
+        scale = np.abs(v).max()
+        assert np.allclose(got["rb_" + k], v, rtol=1e-4, atol=1e-5 * scale), k
