@@ -42,7 +42,7 @@ LINK_GBS = 770.0
 # DRAM bytes (read + write) per launch of each stage's dominant kernel from
 # one ncu capture of this benchmark (profiles/*_config3.md); None = not
 # captured.  Valid for the config-3 workload only.
-PROFILED_TRAFFIC = {"rasterize_bwd": 44.4e6 + 0.2e6, "rasterize_fwd": 15.9e6 + 0.01e6,
+PROFILED_TRAFFIC = {"rasterize_bwd": 46.8e6, "rasterize_fwd": 19.0e6,
                     "sh_bwd": 120.0e6 + 151.8e6, "projection_bwd": 86.4e6 + 13.7e6}
 
 
@@ -169,32 +169,49 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ helpers
 
-def algorithmic_bytes(stage, n, visible, m, pixels, K, slots, kept=None):
-    """Bytes each stage must move at minimum (the roofline convention):
-    what it reads once and writes once, not what an implementation's
-    intermediate passes move.  ``slots``: tile offsets written; ``kept``:
-    the intersections left after the encode's tile culling (the lists the
-    rasterizers walk), else m."""
+def algorithmic_bytes(stage, N, C, visible, m, pixels, K, slots, kept=None):
+    """Bytes each stage must move at minimum (the roofline convention): what
+    it reads once and writes once, not what an implementation's intermediate
+    passes move.  N Gaussians seen by C cameras (C N elements); ``visible``:
+    Gaussians some camera sees, whose coefficient rows the fused SH kernels
+    read (and write) once for all cameras; ``slots``: tile offsets written;
+    ``kept``: the intersections left after the encode's tile culling (the
+    lists the rasterizers walk), else m."""
     mk = m if kept is None else kept
+    e = N * C
     return {
-        # means/quats/scales in (40 B), 2D outputs out (36 B) per Gaussian
-        "projection_fwd": n * (40 + 36),
-        # means + campos in, colours out for all; coefficient rows of visible
-        "sh_fwd": n * (12 + 8 + 12) + visible * K * 12,
+        # means/quats/scales in once (40 B), 2D outputs out (36 B) per element
+        "projection_fwd": N * 40 + e * 36,
+        # means in, campos per camera, colours out per element; the
+        # coefficient row of every visible Gaussian once
+        "sh_fwd": N * 12 + C * 16 + e * 12 + visible * K * 12,
         # rects from means2d/radii, counts out, their total
-        "isect_count": n * (16 + 4),
+        "isect_count": e * (16 + 4),
         # means2d, radii, depths in; sorted keys + flatten ids and the tile
         # offsets out (the binned encode writes the offsets itself)
-        "isect_encode_sort": n * (8 + 8 + 4) + mk * 12 + slots * 4,
+        "isect_encode_sort": e * (8 + 8 + 4) + mk * 12 + slots * 4,
         "isect_offset": m * 8,
         # opacity in, its two sigma bounds out
-        "sigma_bounds": n * (4 + 8),
+        "sigma_bounds": N * (4 + 8),
         # per intersection: flatten id + Gaussian record; per pixel: outputs
         "rasterize_fwd": mk * 40 + pixels * 20,
         "rasterize_bwd": mk * (40 + 36) + pixels * 20,
-        "projection_bwd": n * (8 + 12 + 8 + 4 + 12) + n * (40 + 40),
-        "sh_bwd": n * (12 + 12 + 12) + visible * K * 12 + n * K * 12,
+        # per element: radii, conics, cotangents; per Gaussian: parameters in,
+        # gradients out
+        "projection_bwd": e * (8 + 12 + 8 + 4 + 12) + N * (40 + 40),
+        # means in and v_means out per Gaussian, v_colours in per element,
+        # coefficient rows of visible Gaussians in, every v_coeffs row out
+        "sh_bwd": N * (12 + 12) + e * 12 + visible * K * 12 + N * K * 12,
     }[stage]
+
+
+# Warp instructions per launch of the rasterizers at config 3 (one pass of
+# `ncu --metrics smsp__inst_executed.sum`, profiles/raster_bwd16_config3.md
+# and raster_fwd16_config3.md): their roofline is the SMs' instruction issue,
+# 148 SMs x 4 schedulers x the sampled SM clock, not HBM.
+PROFILED_INSTS = {"rasterize_bwd": 364_690_155,
+                  # the forward kernel and its exact fix-up kernel
+                  "rasterize_fwd": 197_541_410 + 6_994_831}
 
 
 def bin_count(cameras, tw, th):
@@ -524,18 +541,21 @@ def run_ours(args):
     if rank == 0:
         peaks, peak_kind = load_peaks()
         hbm = float(peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
-        visible = int(((step.radii[..., 0] > 0) & (step.radii[..., 1] > 0)).sum().item())
+        vis_el = (step.radii[..., 0] > 0) & (step.radii[..., 1] > 0)
+        visible = int(vis_el.sum().item())
+        visible_any = int(vis_el.any(dim=0).sum().item())
         K = sc.coeffs.shape[1]
         passes = bin_sort_passes(sharded.C, sc.tile_width, sc.tile_height)
         slots = sharded.C * sc.tile_width * sc.tile_height
         avg = {k: float(np.mean(v)) for k, v in stage_ms.items()}
         top = max((k for k in avg if k != "exchange"), key=avg.get)
-        # this rank's units: (camera, Gaussian) elements and pixels
-        n_el, pix_local = sc.n * sharded.C, sc.width * sc.height * sharded.C
-        vis_b = visible
+        # this rank's units: N Gaussians, C cameras, pixels
+        pix_local = sc.width * sc.height * sharded.C
         kept = step.kept_isects() if step.bands == 1 else None
-        bytes_top = algorithmic_bytes(top, n_el, vis_b, m, pix_local, K, slots, kept)
-        achieved = bytes_top / (avg[top] / 1e3) / 1e9
+        sm_mhz = clk.get("sm_mhz") or clk.get("sm_max_mhz") or 1965.0
+        issue_peak = 148 * 4 * sm_mhz * 1e6 / 1e9  # G warp instructions / s
+        bytes_of = lambda k: algorithmic_bytes(k, sc.n, sharded.C, visible_any, m,  # noqa: E731
+                                               pix_local, K, slots, kept)
         stages = {}
         for k, v in avg.items():
             if k == "exchange":
@@ -546,9 +566,29 @@ def run_ours(args):
                              "GBps_sent": round(b / (v / 1e3) / 1e9, 1),
                              "frac_link": round(b / (v / 1e3) / 1e9 / LINK_GBS, 4)}
                 continue
-            b = algorithmic_bytes(k, n_el, vis_b, m, pix_local, K, slots, kept)
+            b = bytes_of(k)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
+            if k in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+                ginst = PROFILED_INSTS[k] / (v / 1e3) / 1e9
+                stages[k]["Ginst_per_s"] = round(ginst, 1)
+                stages[k]["frac_issue"] = round(ginst / issue_peak, 4)
+        if top in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+            ginst = PROFILED_INSTS[top] / (avg[top] / 1e3) / 1e9
+            roofline = {"kernel": top, "bound": "issue", "achieved": round(ginst, 1),
+                        "peak": round(issue_peak, 1), "unit": "G warp-instructions/s",
+                        "frac": round(ginst / issue_peak, 4),
+                        "peak_source": "148 SMs x 4 schedulers x median sampled SM clock",
+                        "warp_instructions": int(PROFILED_INSTS[top]),
+                        "traffic": PROFILED_TRAFFIC.get(top),
+                        "algorithmic_bytes": int(bytes_of(top)),
+                        "frac_hbm": round(bytes_of(top) / (avg[top] / 1e3) / 1e9 / hbm, 4)}
+        else:
+            achieved = bytes_of(top) / (avg[top] / 1e3) / 1e9
+            roofline = {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1),
+                        "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                        "peak_source": peak_kind, "traffic": PROFILED_TRAFFIC.get(top),
+                        "algorithmic_bytes": int(bytes_of(top))}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             checker, kind = make_checker()
@@ -567,7 +607,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
             "data": f"synthetic (seeded, BASELINE {args.workload} distributions)",
             "config": {"workload": desc, "cameras": C_total,
-                       "gaussians": sc.n, "visible": visible, "isects": m,
+                       "gaussians": sc.n, "visible": visible, "visible_any": visible_any,
+                       "isects": m,
                        # after the encode's opacity-aware tile culling
                        "isects_kept": kept, "tile_cull": step.tile_cull,
                        # (per band when the step renders bands of tile rows)
@@ -580,10 +621,7 @@ def run_ours(args):
             # M / (encode + sort) time of this rank's step
             "intersections_sorted_per_s": round(m / (avg["isect_encode_sort"] / 1e3), 1),
             "stages_ms": stages,
-            "roofline": {"kernel": top, "bound": "hbm", "achieved": round(achieved, 1),
-                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "peak_source": peak_kind, "traffic": PROFILED_TRAFFIC.get(top),
-                         "algorithmic_bytes": int(bytes_top)},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
@@ -615,7 +653,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3",
                     help="BASELINE config (cfg3 is the headline; the others fill the "
                          "per-config records)")
-    ap.add_argument("--exchange", choices=["auto", "allreduce", "gather"], default="auto",
+    ap.add_argument("--exchange", choices=["auto", "allreduce", "gather", "shard"], default="auto",
                     help="gradient exchange of the camera-sharded step (N > 1)")
     ap.add_argument("--tile-cull", action="store_true",
                     help="opacity-aware tile culling in the encode (the renders are the "

@@ -337,6 +337,15 @@ __global__ void __launch_bounds__(256) glue_fwd_kernel(int C, int N, int K,
   }
 }
 
+// Row of viewmats for the c-th camera of the colour cotangents: with
+// groups > 1 the cotangents are ordered (camera c_g of group g) as
+// c = c_g * groups + g while viewmats holds group g's C / groups cameras
+// contiguously (the order in which a camera-sharded step's per-camera
+// all-to-alls deliver them); else c itself.
+__device__ __forceinline__ int cam_row(int c, int C, int groups) {
+  return groups > 1 ? (c % groups) * (C / groups) + c / groups : c;
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
                                                        const float* __restrict__ means,
@@ -347,7 +356,7 @@ __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
                                                        const float* __restrict__ v_colors,
                                                        float* __restrict__ v_means,
                                                        float* __restrict__ v_coeffs,
-                                                       int skip_zero) {
+                                                       int skip_zero, int groups) {
   for (int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; n < N;
        n += (int64_t)gridDim.x * blockDim.x) {
     const float m[3] = {__ldg(means + n * 3), __ldg(means + n * 3 + 1), __ldg(means + n * 3 + 2)};
@@ -359,7 +368,7 @@ __global__ void __launch_bounds__(256) glue_bwd_kernel(int C, int N, int K,
       const int64_t e = (int64_t)c * N + n;
       if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
       float cp[3];
-      campos_of(viewmats + (int64_t)c * 16, cp);
+      campos_of(viewmats + (int64_t)cam_row(c, C, groups) * 16, cp);
       const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
       const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
       const float mm = fmaxf(s, 1.0e-8f);
@@ -572,7 +581,7 @@ __device__ __forceinline__ void glue_bwd_vec_one(
     const float* __restrict__ viewmats, const float* __restrict__ coeffs,
     const uint8_t* __restrict__ masks, const int32_t* __restrict__ radii,
     const float* __restrict__ v_colors, float* __restrict__ v_means, float* __restrict__ v_coeffs,
-    int skip_zero) {
+    int skip_zero, int groups) {
   constexpr int A = (D + 1) * (D + 1);
   constexpr int NV = (A * 3 + 3) / 4;
   float4* out = reinterpret_cast<float4*>(v_coeffs + n * (int64_t)K * 3);
@@ -596,7 +605,7 @@ __device__ __forceinline__ void glue_bwd_vec_one(
     const int64_t e = (int64_t)c * N + n;
     if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
     float cp[3];
-    campos_of(viewmats + (int64_t)c * 16, cp);
+    campos_of(viewmats + (int64_t)cam_row(c, C, groups) * 16, cp);
     const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
     const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
     const float mm = fmaxf(s, 1.0e-8f);
@@ -679,7 +688,7 @@ __global__ void __launch_bounds__(32 * kGlueBwdWarps, ACC ? 3 : 4) glue_bwd_vec_
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
     const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
     const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
-    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero) {
+    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero, int groups) {
   __shared__ int s_q[kGlueBwdWarps][64];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int* q = s_q[warp];
@@ -709,14 +718,14 @@ __global__ void __launch_bounds__(32 * kGlueBwdWarps, ACC ? 3 : 4) glue_bwd_vec_
     __syncwarp();
     if (qn >= 32) {
       glue_bwd_vec_one<D, ACC>(q[qn - 32 + lane], C, N, K, means, viewmats, coeffs, masks, radii,
-                               v_colors, v_means, v_coeffs, skip_zero);
+                               v_colors, v_means, v_coeffs, skip_zero, groups);
       qn -= 32;
       __syncwarp();
     }
   }
   if (lane < qn)
     glue_bwd_vec_one<D, ACC>(q[lane], C, N, K, means, viewmats, coeffs, masks, radii, v_colors,
-                             v_means, v_coeffs, skip_zero);
+                             v_means, v_coeffs, skip_zero, groups);
 }
 
 template <int D>
@@ -773,7 +782,7 @@ __global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
     int C, int N, int K, const float* __restrict__ means, const float* __restrict__ viewmats,
     const float* __restrict__ coeffs, const uint8_t* __restrict__ masks,
     const int32_t* __restrict__ radii, const float* __restrict__ v_colors,
-    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero) {
+    float* __restrict__ v_means, float* __restrict__ v_coeffs, int skip_zero, int groups) {
   extern __shared__ float smem[];
   const int R = K * 3, S = R | 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -801,7 +810,7 @@ __global__ void __launch_bounds__(kWsThreads) glue_bwd_ws_kernel(
         const int64_t e = (int64_t)c * N + n;
         if (!bwd_visible(masks, radii, v_colors, skip_zero, e)) continue;
         float cp[3];
-        campos_of(viewmats + (int64_t)c * 16, cp);
+        campos_of(viewmats + (int64_t)cam_row(c, C, groups) * 16, cp);
         const float u[3] = {m[0] - cp[0], m[1] - cp[1], m[2] - cp[2]};
         const float s = sqrtf(u[0] * u[0] + u[1] * u[1] + u[2] * u[2]);
         const float mm = fmaxf(s, 1.0e-8f);
@@ -1016,23 +1025,23 @@ struct GlueBwdL {
       constexpr int DV = D < 3 ? D : 3;
       auto kern = p->C > 1 ? glue_bwd_vec_kernel<DV, true> : glue_bwd_vec_kernel<DV, false>;
       kern<<<grid_for(p->N, 32 * kGlueBwdWarps), 32 * kGlueBwdWarps, 0, s>>>(
-          p->C, p->N, p->K, means, viewmats, coeffs,
-                                                p->use_masks ? masks : nullptr, radii, v_colors,
-                                                v_means, v_coeffs, p->skip_zero_cotangents);
+          p->C, p->N, p->K, means, viewmats, coeffs, p->use_masks ? masks : nullptr, radii,
+          v_colors, v_means, v_coeffs, p->skip_zero_cotangents, p->camera_groups);
       return launch_status("sh_glue_bwd");
     }
     if (p->K * 3 <= kWsMaxR) {
       int C = p->C, N = p->N, K = p->K;
       const uint8_t* mk = p->use_masks ? masks : nullptr;
-      int skip = p->skip_zero_cotangents;
+      int skip = p->skip_zero_cotangents, groups = p->camera_groups;
       void* args[] = {&C, &N, &K, &means, &viewmats, &coeffs, &mk, &radii, &v_colors, &v_means,
-                      &v_coeffs, &skip};
+                      &v_coeffs, &skip, &groups};
       return ws_launch(glue_bwd_ws_kernel<D>, N, K, 2, s, "sh_glue_bwd", args);
     }
     glue_bwd_kernel<D><<<grid_for(p->N, 256), 256, 0, s>>>(p->C, p->N, p->K, means, viewmats,
                                                            coeffs, p->use_masks ? masks : nullptr,
                                                            radii, v_colors, v_means, v_coeffs,
-                                                           p->skip_zero_cotangents);
+                                                           p->skip_zero_cotangents,
+                                                           p->camera_groups);
     return launch_status("sh_glue_bwd");
   }
 };
@@ -1048,6 +1057,8 @@ int check_sh(const gs_sh_params* p) {
 
 int check_glue(const gs_sh_glue_params* p) {
   if (!p || p->C < 0 || p->N < 0) return invalid("sh_glue: bad params");
+  if (p->camera_groups > 1 && p->C % p->camera_groups)
+    return invalid("sh_glue: the camera count must be a multiple of camera_groups");
   if (p->degrees_to_use < 0 || p->degrees_to_use > 4)
     return invalid("sh_glue: degree must be 0..4");
   if (p->K < (p->degrees_to_use + 1) * (p->degrees_to_use + 1))

@@ -44,7 +44,7 @@ class SHParams(ct.Structure):
 
 class SHGlueParams(ct.Structure):
     _fields_ = [("C", _i32), ("N", _i32), ("K", _i32), ("degrees_to_use", _i32),
-                ("use_masks", _i32), ("skip_zero_cotangents", _i32)]
+                ("use_masks", _i32), ("skip_zero_cotangents", _i32), ("camera_groups", _i32)]
 
 
 class DensifyParams(ct.Structure):

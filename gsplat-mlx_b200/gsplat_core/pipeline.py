@@ -52,7 +52,7 @@ def sh_colors(degree, means, viewmats, coeffs, masks=None, radii=None):
 
 
 def sh_colors_backward(degree, means, viewmats, coeffs, masks, v_colors, v_means_accum,
-                       radii=None, v_coeffs=None, skip_zero_cotangents=False):
+                       radii=None, v_coeffs=None, skip_zero_cotangents=False, camera_groups=1):
     """Reverse mode of sh_colors as MLX autograd forms it; adds into
     v_means_accum [N,3] and returns v_coeffs [N,K,3] (summed over cameras).
     With skip_zero_cotangents, entries whose colour cotangent is zero are
@@ -63,7 +63,8 @@ def sh_colors_backward(degree, means, viewmats, coeffs, masks, v_colors, v_means
     K = coeffs.shape[-2]
     if v_coeffs is None:
         v_coeffs = torch.empty_like(coeffs)
-    p = SHGlueParams(C, N, K, int(degree), int(masks is not None), int(skip_zero_cotangents))
+    p = SHGlueParams(C, N, K, int(degree), int(masks is not None), int(skip_zero_cotangents),
+                     int(camera_groups))
     check(_lib.load().gs_sh_glue_bwd(ct.byref(p), _p(means), _p(viewmats), _p(coeffs), _p(masks),
                                      _p(radii), _p(v_colors), _p(v_means_accum), _p(v_coeffs),
                                      _s()), "sh_colors_backward")

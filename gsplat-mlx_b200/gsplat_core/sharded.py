@@ -6,7 +6,7 @@ sum that the reference's projection backward forms by looping over the
 cameras (metal/gsplat_projection.metal:488-545) and that MLX autograd forms
 over the trainers' camera loop.  So each rank holds the full Gaussian set,
 renders its own contiguous slice of the cameras with ``TrainingStep``, and
-the ranks exchange gradients once per step.  Two exchanges give the same
+the ranks exchange gradients once per step.  Three exchanges give the same
 sums (up to fp32 summation order):
 
 * ``"allreduce"`` -- every rank runs the whole backward for its cameras and
@@ -22,9 +22,20 @@ sums (up to fp32 summation order):
   backward over all cameras, which writes the full v_coeffs and adds the
   SH part of v_means.
 
-``"auto"`` picks the exchange that moves fewer bytes per rank (ring
-estimates in ``exchange_bytes``): at SH degree 3 gather wins up to 3
-cameras per rank on 8 ranks and up to 16 on 2.
+* ``"shard"`` -- the SH glue backward is split by Gaussian instead of
+  replicated: rank q owns the Gaussians [q N/R, (q+1) N/R).  One all-to-all
+  per local camera moves each slice of the colour cotangents to its owner
+  (started as soon as the rasterizer backward is queued, so it overlaps the
+  projection backward); a reduce-scatter sums the projection part per slice;
+  each rank runs the SH glue backward for its slice over every camera
+  (adding the SH part of v_means into its reduced slice) and one all-gather
+  assembles the full gradient on every rank.  Per rank: (R-1)/R (12 C_local
+  + 4 (11 + 3K)) N bytes and 1/R of the SH backward, whatever R.  Needs N
+  divisible by R.
+
+``"auto"`` picks shard when N divides evenly and the SH degree is above 0
+(it moves the fewest bytes and keeps the SH backward per rank constant),
+else the cheaper of the other two (ring estimates in ``exchange_bytes``).
 """
 from __future__ import annotations
 
@@ -52,15 +63,83 @@ def exchange_bytes(mode, n, K, cameras_per_rank, world):
         return ring * 4.0 * (11 + 3 * K) * n
     if mode == "gather":
         return ring * 44.0 * n + (world - 1) * 12.0 * n * cameras_per_rank
+    if mode == "shard":
+        part = (world - 1) / world
+        return part * (12.0 * cameras_per_rank + 4.0 * (11 + 3 * K)) * n + part * 44.0 * n
     raise ValueError(f"unknown exchange {mode!r}")
 
 
 def choose_exchange(n, K, cameras_per_rank, world):
     if world <= 1:
         return "allreduce"
+    if K > 1 and n % world == 0:
+        return "shard"
     ar = exchange_bytes("allreduce", n, K, cameras_per_rank, world)
     ga = exchange_bytes("gather", n, K, cameras_per_rank, world)
     return "gather" if ga < ar else "allreduce"
+
+
+# [v_means | v_quats | v_scales | v_opacities] of the flat gradient buffer:
+# (offset, width) in units of N floats; v_coeffs follows at 11 N.
+PROJ_FIELDS = ((0, 3), (3, 4), (7, 3), (10, 1))
+
+
+class _Works:
+    def __init__(self, works):
+        self.works = [w for w in works if w is not None]
+
+    def wait(self):
+        for w in self.works:
+            w.wait()
+
+
+def _coalesced(fn, pairs, group, device):
+    """Asynchronous collectives ``fn(out, inp)`` over (out, inp) pairs: one
+    NCCL group launch (coalescing manager) with NCCL, separate ops with
+    gloo.  Returns a handle with wait()."""
+    if dist.get_backend(group) == "nccl":
+        with dist.distributed_c10d._coalescing_manager(group=group, device=device,
+                                                       async_ops=True) as cm:
+            for out, inp in pairs:
+                fn(out, inp, group=group)
+        return cm
+    return _Works([fn(out, inp, group=group, async_op=True) for out, inp in pairs])
+
+
+def start_shard_all_to_all(recv, v_colors_local, group):
+    """Moves each Gaussian slice of this rank's colour cotangents
+    [C_local, N, 3] to the slice's owner: recv [C_local * R, N / R, 3]
+    receives, for local camera j of rank g, row j R + g (the order
+    camera_groups = R of the SH glue backward reads)."""
+    R = dist.get_world_size(group)
+    C_local = v_colors_local.shape[0]
+    works = []
+    for j in range(C_local):
+        works.append(dist.all_to_all_single(recv[j * R:(j + 1) * R].reshape(-1),
+                                            v_colors_local[j].reshape(-1), group=group,
+                                            async_op=True))
+    return _Works(works)
+
+
+def shard_exchange(grad_flat, n, K, reduced, coeff_slice, sh_slice_backward, moving, group=None,
+                   device=None):
+    """The "shard" exchange after this rank's projection backward:
+    ``grad_flat`` holds this rank's projection part for all N Gaussians;
+    ``moving`` is the handle of start_shard_all_to_all.  ``reduced``: the
+    four per-slice field buffers ([d N / R] each, see PROJ_FIELDS);
+    ``coeff_slice`` [N / R, K, 3].  ``sh_slice_backward()`` runs the SH
+    glue backward of this rank's slice over every camera, writing
+    coeff_slice and adding the SH part of v_means into reduced[0].
+    Afterwards every rank holds the full summed gradient in grad_flat."""
+    summing = _coalesced(dist.reduce_scatter_tensor,
+                         [(reduced[i], grad_flat[o * n:(o + d) * n])
+                          for i, (o, d) in enumerate(PROJ_FIELDS)], group, device)
+    moving.wait()
+    summing.wait()
+    sh_slice_backward()
+    pairs = [(grad_flat[o * n:(o + d) * n], reduced[i]) for i, (o, d) in enumerate(PROJ_FIELDS)]
+    pairs.append((grad_flat[11 * n:11 * n + 3 * K * n], coeff_slice.reshape(-1)))
+    _coalesced(dist.all_gather_into_tensor, pairs, group, device).wait()
 
 
 def _all_gather(out, inp, group, async_op=False):
@@ -125,13 +204,23 @@ class ShardedTrainingStep:
         self.step = TrainingStep(n, sh_degree, K, self.C, width, height, **step_kw)
         self.exchange = (choose_exchange(self.N, self.K, self.C, self.world)
                          if exchange == "auto" else exchange)
-        if self.exchange not in ("allreduce", "gather"):
+        if self.exchange not in ("allreduce", "gather", "shard"):
             raise ValueError(f"unknown exchange {exchange!r}")
+        if self.exchange == "shard" and self.N % self.world:
+            raise ValueError(f"the shard exchange needs N ({self.N}) divisible by the "
+                             f"{self.world} ranks")
         self.v_colors_all = self.v_means_sh = None
+        dev = self.step.dev
+        e = lambda *shape: torch.empty(shape, dtype=torch.float32, device=dev)  # noqa: E731
         if self.exchange == "gather" and self.world > 1:
-            self.v_colors_all = torch.empty((self.C_total, self.N, 3), dtype=torch.float32,
-                                            device=self.step.dev)
-            self.v_means_sh = torch.empty((self.N, 3), dtype=torch.float32, device=self.step.dev)
+            self.v_colors_all = e(self.C_total, self.N, 3)
+            self.v_means_sh = e(self.N, 3)
+        if self.exchange == "shard" and self.world > 1:
+            ns = self.N // self.world
+            self.slice0 = self.rank * ns
+            self.recv = e(self.C_total, ns, 3)
+            self.reduced = [e(d * ns) for _, d in PROJ_FIELDS]
+            self.coeff_slice = e(ns, self.K, 3)
 
 
     def local(self, t):
@@ -146,18 +235,35 @@ class ShardedTrainingStep:
         from .pipeline import sh_colors_backward
         st = self.step
         gather = self.exchange == "gather" and self.world > 1
+        shard = self.exchange == "shard" and self.world > 1
         gathering = []
 
         def start_gather():
             # the colour cotangents are final once the rasterizer backward
-            # ran: their all-gather overlaps the projection backward
-            gathering.append(_all_gather(self.v_colors_all.view(-1), st.v_colors.reshape(-1),
-                                         self.group, async_op=True))
+            # ran: their exchange overlaps the projection backward
+            if shard:
+                gathering.append(start_shard_all_to_all(self.recv, st.v_colors, self.group))
+            else:
+                gathering.append(_all_gather(self.v_colors_all.view(-1),
+                                             st.v_colors.reshape(-1), self.group, async_op=True))
 
         flat, m = st.run(means, quats, scales, opacities, coeffs, self.local(viewmats_all),
                          self.local(Ks_all), v_render_colors, v_render_alphas,
-                         sh_backward=not gather, after_raster=start_gather if gather else None)
+                         sh_backward=not (gather or shard),
+                         after_raster=start_gather if (gather or shard) else None)
         if self.world == 1:
+            return flat, m
+        if shard:
+            a, b = self.slice0, self.slice0 + self.N // self.world
+
+            def sh_slice():
+                sh_colors_backward(self.deg, means[a:b], viewmats_all, coeffs[a:b], None,
+                                   self.recv, self.reduced[0].view(-1, 3), radii=None,
+                                   v_coeffs=self.coeff_slice, skip_zero_cotangents=True,
+                                   camera_groups=self.world)
+
+            shard_exchange(flat, self.N, self.K, self.reduced, self.coeff_slice, sh_slice,
+                           gathering[0], self.group, st.dev)
             return flat, m
 
         def sh_bwd(v_all):

@@ -141,6 +141,13 @@ typedef struct {
   int32_t skip_zero_cotangents; /* bwd: an entry whose colour cotangent is 0
                                    contributes nothing and is skipped (for
                                    cameras whose radii are not at hand) */
+  int32_t camera_groups; /* bwd: > 1 = the colour cotangents (and masks /
+                            radii) come in the order of G = camera_groups
+                            groups interleaved: entry camera c = j G + g is
+                            camera j of group g, whose pose is viewmats row
+                            g (C / G) + j (the order a camera-sharded step's
+                            per-camera all-to-alls deliver them); else the
+                            viewmats order */
 } gs_sh_glue_params;
 
 int gs_sh_glue_fwd(const gs_sh_glue_params* p, const float* means,

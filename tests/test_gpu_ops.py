@@ -255,6 +255,32 @@ def test_sh_large(gs, oracle, cuda, deg, K):
     assert_grad_close(b["v_coeffs"], eb["v_coeffs"], "sh v_coeffs")
 
 
+@pytest.mark.parametrize("K", [16, 25])
+def test_sh_glue_bwd_camera_groups(gs, oracle, cuda, K):
+    """The glue backward reading colour cotangents in the interleaved order
+    of the camera-sharded step (camera_groups = G: row j G + g is camera j
+    of group g) gives the oracle's gradients for the same cameras in
+    viewmats order; with zero-cotangent skipping and no radii, as that step
+    runs it, on both kernel families."""
+    from gsplat_core import pipeline, synthetic as S
+    sc, idx = _scene_subset("config3", 40_000)
+    means = sc.means[idx]
+    rng = np.random.default_rng(7)
+    coeffs = (sc.coeffs[idx] if K == 16 else
+              rng.normal(0, 0.3, size=(means.shape[0], K, 3)).astype(np.float32))
+    G, Cg = 4, 2
+    views = S.orbit(G * Cg, 4.0)
+    vout = rng.normal(size=(G * Cg, means.shape[0], 3)).astype(np.float32)
+    vout[rng.uniform(size=vout.shape[:2]) < 0.5] = 0.0
+    perm = [g * Cg + j for j in range(Cg) for g in range(G)]   # row j G + g
+    e = oracle.sh_glue_bwd(3, means, views, coeffs, vout, None)
+    vm = torch.zeros((means.shape[0], 3), dtype=torch.float32, device="cuda")
+    vc = pipeline.sh_colors_backward(3, T(means), T(views), T(coeffs), None, T(vout[perm]), vm,
+                                     skip_zero_cotangents=True, camera_groups=G)
+    assert_grad_close(vc, e["v_coeffs"], "grouped v_coeffs", atol_frac=1e-5)
+    assert_grad_close(vm, e["v_means"], "grouped v_means", atol_frac=1e-5)
+
+
 @pytest.mark.parametrize("deg,K,misalign", [(3, 16, False), (3, 16, True), (2, 16, False),
                                              (1, 4, False), (0, 4, False), (0, 1, False),
                                              (2, 9, False), (4, 25, False)])

@@ -1,4 +1,4 @@
-"""Camera-sharded step on two GPUs (NCCL): both gradient exchanges give the
+"""Camera-sharded step on two GPUs (NCCL): every gradient exchange gives the
 gradients of one single-GPU TrainingStep over all cameras.  Skipped where
 fewer than two GPUs are visible."""
 from __future__ import annotations
@@ -54,7 +54,7 @@ def _worker(rank, world, port, mode, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["allreduce", "gather"])
+@pytest.mark.parametrize("mode", ["allreduce", "gather", "shard"])
 def test_two_gpu_exchange_matches_single_gpu(gs, cuda, tmp_path, mode):
     import torch
     import torch.multiprocessing as mp

@@ -34,10 +34,14 @@ def test_exchange_choice():
     from gsplat_core.sharded import choose_exchange, exchange_bytes
     n = 1_000_000
     assert choose_exchange(n, 16, 1, 1) == "allreduce"
-    assert choose_exchange(n, 16, 1, 8) == "gather"
-    assert choose_exchange(n, 16, 3, 8) == "gather"
-    assert choose_exchange(n, 16, 4, 8) == "allreduce"      # 32 cameras on 8 GPUs
+    assert choose_exchange(n, 16, 1, 8) == "shard"          # N divides evenly
+    assert choose_exchange(n, 16, 4, 8) == "shard"          # 32 cameras on 8 GPUs
+    assert choose_exchange(n + 1, 16, 1, 8) == "gather"     # uneven slices
+    assert choose_exchange(n + 1, 16, 3, 8) == "gather"
+    assert choose_exchange(n + 1, 16, 4, 8) == "allreduce"
     assert choose_exchange(n, 1, 1, 8) == "allreduce"       # SH degree 0
+    # shard moves fewer bytes than the all-reduce for the 32-camera batch
+    assert exchange_bytes("shard", n, 16, 4, 8) < exchange_bytes("allreduce", n, 16, 4, 8)
     assert exchange_bytes("allreduce", n, 16, 1, 2) == pytest.approx(236e6)
 
 
@@ -108,6 +112,8 @@ def _worker(rank, world, port, mode, out_dir):
         a, b = camera_shard(sc.viewmats.shape[0], world, rank)
         cams = list(range(a, b))
         flat_np, v_colors = _camera_grads(oracle, sc, cams, vrc, vra, with_sh=(mode == "allreduce"))
+        if mode == "shard":
+            flat_np[11 * sc.n:] = 0.0
         v_local = torch.from_numpy(np.ascontiguousarray(v_colors))
         flat = torch.from_numpy(flat_np)
         v_all = torch.empty((sc.viewmats.shape[0], sc.n, 3), dtype=torch.float32)
@@ -119,6 +125,27 @@ def _worker(rank, world, port, mode, out_dir):
             flat[11 * n:] = torch.from_numpy(gb["v_coeffs"].ravel())
             return torch.from_numpy(gb["v_means"])
 
+        if mode == "shard":
+            from gsplat_core.sharded import PROJ_FIELDS, shard_exchange, start_shard_all_to_all
+            ns = n // world
+            C_local = len(cams)
+            recv = torch.empty((sc.viewmats.shape[0], ns, 3), dtype=torch.float32)
+            reduced = [torch.empty(d * ns, dtype=torch.float32) for _, d in PROJ_FIELDS]
+            coeff_slice = torch.empty((ns, K, 3), dtype=torch.float32)
+            moving = start_shard_all_to_all(recv, v_local, None)
+            # recv row j * world + g holds camera j of rank g
+            perm = [g * C_local + j for j in range(C_local) for g in range(world)]
+            a = rank * ns
+
+            def sh_slice():
+                gb = oracle.sh_glue_bwd(sc.sh_degree, sc.means[a:a + ns], sc.viewmats[perm],
+                                        sc.coeffs[a:a + ns], recv.numpy(), None)
+                coeff_slice.copy_(torch.from_numpy(gb["v_coeffs"]))
+                reduced[0].add_(torch.from_numpy(gb["v_means"]).reshape(-1))
+
+            shard_exchange(flat, n, K, reduced, coeff_slice, sh_slice, moving)
+            np.save(os.path.join(out_dir, f"{mode}_{rank}.npy"), flat.numpy())
+            return
         gathering = None
         if mode == "gather_started":
             # the sharded step starts the colour all-gather before its
@@ -132,7 +159,7 @@ def _worker(rank, world, port, mode, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["allreduce", "gather", "gather_started"])
+@pytest.mark.parametrize("mode", ["allreduce", "gather", "gather_started", "shard"])
 def test_two_rank_exchange_matches_single_process(oracle, tmp_path, mode):
     sc, vrc, vra = _scene()
     expect, _ = _camera_grads(oracle, sc, list(range(sc.viewmats.shape[0])), vrc, vra, True)
