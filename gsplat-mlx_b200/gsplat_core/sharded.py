@@ -189,9 +189,13 @@ class ShardedTrainingStep:
     have the same number of cameras (C_total divisible by the world size)."""
 
     def __init__(self, n, sh_degree, K, cameras_total, width, height, group=None, exchange="auto",
-                 **step_kw):
+                 heartbeat=None, **step_kw):
         from .pipeline import TrainingStep
         self.group = group
+        # liveness.Heartbeat: before a step's first collective every rank
+        # must have reached the step (bounded wait, PeerLost otherwise)
+        self.heartbeat = heartbeat
+        self.steps = 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if cameras_total % self.world:
@@ -234,6 +238,9 @@ class ShardedTrainingStep:
         Returns (grad_flat summed over all cameras, local intersections)."""
         from .pipeline import sh_colors_backward
         st = self.step
+        self.steps += 1
+        if self.heartbeat is not None and self.world > 1:
+            self.heartbeat.check(self.steps)
         gather = self.exchange == "gather" and self.world > 1
         shard = self.exchange == "shard" and self.world > 1
         gathering = []

@@ -87,3 +87,61 @@ def test_two_gpu_exchange_matches_single_gpu(gs, cuda, tmp_path, mode):
                        ("v_scales", 7 * n, 10 * n), ("v_opacities", 10 * n, 11 * n),
                        ("v_coeffs", 11 * n, expect.size)):
         assert_grad_close(outs[0][a:b], expect[a:b], f"{mode} {name}", atol_frac=1e-4)
+
+
+def _leaver(rank, world, port, out_dir):
+    """NCCL ranks on their own GPUs; the last rank leaves after step 1 with
+    nothing in flight; the others must learn it on the host (heartbeat)
+    before step 2's collective and abort their communicators."""
+    import json
+    import time
+    import torch
+    import torch.distributed as dist
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from gsplat_core.liveness import Heartbeat, PeerLost, abort_group, init_group
+    store = init_group("nccl", rank, world, timeout_s=20.0, device=dev, master_port=port)
+    hb = Heartbeat(store, rank, world, deadline_s=2.0)
+    x = torch.ones(1 << 16, device=dev)
+    hb.check(1)
+    dist.all_reduce(x)
+    torch.cuda.synchronize()
+    if rank == world - 1:
+        os._exit(0)
+    t0 = time.monotonic()
+    res = {"error": None}
+    try:
+        hb.check(2)
+        dist.all_reduce(x)
+        torch.cuda.synchronize()
+    except PeerLost as e:
+        res = {"error": "PeerLost", "ranks": e.ranks}
+    res["seconds"] = time.monotonic() - t0
+    abort_group()
+    with open(os.path.join(out_dir, f"leave_{rank}.json"), "w") as f:
+        json.dump(res, f)
+    os._exit(0)
+
+
+def test_two_gpu_rank_leaving_is_detected(gs, cuda, tmp_path):
+    import json
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("the surviving rank did not return")
+    res = json.load(open(tmp_path / "leave_0.json"))
+    assert res["error"] == "PeerLost" and res["ranks"] == [1], res
+    assert res["seconds"] < 10, res
