@@ -14,6 +14,12 @@
 //   * `argsort` is stable (std::stable_sort) and returns uint32 indices;
 //     MLX's CPU argsort is also a stable sort, but it is not this code.
 // Everything the reference does not use is absent.
+//
+// Device mode (compiled with -DGSPLAT_SHIM_CUDA, for the GPU test of the
+// CUDA eval_gpu adapter only): buffers are CUDA managed memory, a primitive
+// on a gpu stream is evaluated with eval_gpu instead of eval_cpu, and the
+// host-side ops (reshape, cumsum, argsort, take) and `eval` first wait for
+// the device, as MLX's eval does before the host reads a result.
 #pragma once
 
 #include <algorithm>
@@ -27,6 +33,10 @@
 #include <utility>
 #include <variant>
 #include <vector>
+
+#ifdef GSPLAT_SHIM_CUDA
+#include <cuda_runtime_api.h>
+#endif
 
 namespace mlx {
 namespace core {
@@ -76,6 +86,17 @@ inline Stream to_stream(StreamOrDevice s) {
   return Stream(0, Device(Device::cpu));
 }
 
+namespace detail {
+// Waits for the device before a host read (device mode only).
+inline void sync() {
+#ifdef GSPLAT_SHIM_CUDA
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    throw std::runtime_error("shim: device synchronisation failed");
+  }
+#endif
+}
+}  // namespace detail
+
 namespace allocator {
 struct Buffer {
   void* ptr;
@@ -83,11 +104,26 @@ struct Buffer {
 inline Buffer malloc(size_t nbytes) {
   // Always hand out a real allocation so that zero-sized arrays still have a
   // valid data pointer, as MLX does.
-  void* p = std::malloc(nbytes == 0 ? 16 : nbytes);
+  const size_t bytes = nbytes == 0 ? 16 : nbytes;
+#ifdef GSPLAT_SHIM_CUDA
+  void* p = nullptr;
+  if (cudaMallocManaged(&p, bytes) != cudaSuccess) {
+    p = nullptr;
+  }
+#else
+  void* p = std::malloc(bytes);
+#endif
   if (p == nullptr) {
-    throw std::runtime_error("shim allocator: out of host memory");
+    throw std::runtime_error("shim allocator: out of memory");
   }
   return Buffer{p};
+}
+inline void free(void* p) {
+#ifdef GSPLAT_SHIM_CUDA
+  cudaFree(p);
+#else
+  std::free(p);
+#endif
 }
 }  // namespace allocator
 
@@ -147,7 +183,7 @@ class array {
   }
 
   void set_data(allocator::Buffer buf) {
-    desc_->data = std::shared_ptr<void>(buf.ptr, [](void* p) { std::free(p); });
+    desc_->data = std::shared_ptr<void>(buf.ptr, [](void* p) { allocator::free(p); });
   }
   void eval() {}
 
@@ -200,6 +236,13 @@ class Primitive {
     for (size_t i = 0; i < shapes.size(); ++i) {
       outputs[i].init(std::move(shapes[i]), dtypes[i]);
     }
+#ifdef GSPLAT_SHIM_CUDA
+    if (prim->stream().device.type == Device::gpu) {
+      prim->eval_gpu(inputs, outputs);
+      return outputs;
+    }
+    detail::sync();
+#endif
     prim->eval_cpu(inputs, outputs);
     return outputs;
   }
@@ -226,7 +269,9 @@ inline std::vector<array> array::make_arrays(
 }
 
 template <typename... Arrays>
-inline void eval(Arrays&&...) {}
+inline void eval(Arrays&&...) {
+  detail::sync();
+}
 
 inline array contiguous(const array& a, bool = false, StreamOrDevice = {}) {
   return a;
@@ -245,6 +290,7 @@ inline array zeros_like(const array& a, StreamOrDevice s = {}) {
 }
 
 inline array reshape(const array& a, Shape shape, StreamOrDevice = {}) {
+  detail::sync();
   array out = array::from_host(a.data<void>(), std::move(shape), a.dtype());
   if (out.size() != a.size()) {
     throw std::runtime_error("shim reshape: size mismatch");
@@ -258,6 +304,7 @@ inline array cumsum(const array& a, bool reverse, bool inclusive,
   if (a.dtype() != int32 || reverse) {
     throw std::runtime_error("shim cumsum: only forward int32 scans");
   }
+  detail::sync();
   array out = zeros(a.shape(), int32);
   const int32_t* in = a.data<int32_t>();
   int32_t* o = out.data<int32_t>();
@@ -278,6 +325,7 @@ inline array argsort(const array& a, StreamOrDevice = {}) {
   if (a.dtype() != int64 || a.ndim() != 1) {
     throw std::runtime_error("shim argsort: only 1-D int64 keys");
   }
+  detail::sync();
   const int64_t* k = a.data<int64_t>();
   std::vector<uint32_t> idx(a.size());
   std::iota(idx.begin(), idx.end(), 0u);
@@ -290,6 +338,7 @@ inline array take(const array& a, const array& indices, StreamOrDevice = {}) {
   if (indices.dtype() != uint32 || a.ndim() != 1) {
     throw std::runtime_error("shim take: only 1-D gathers by uint32");
   }
+  detail::sync();
   array out = zeros(indices.shape(), a.dtype());
   const uint32_t* idx = indices.data<uint32_t>();
   const size_t item = a.itemsize();

@@ -21,6 +21,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(_HERE, "liboracle.so")
 REF_SO = os.path.join(_HERE, "_ref", "libgsplat_ref.so")
+REF_CUDA_SO = os.path.join(_HERE, "_ref", "libgsplat_ref_cuda.so")
 
 _vp = ct.c_void_p
 _i = ct.c_int
@@ -447,3 +448,26 @@ class Reference(_Common):
                                        W, H, ts, tw, th, _p(toff), m, _p(fids), _p(ra), _p(li), _p(vrc),
                                        _p(vra), int(absgrad), _p(vabs), _p(vm2), _p(vcon), _p(vcol),
                                        _p(vop), _p(vbg)), self.lib, "ref raster_bwd")
+
+
+class ReferenceOnDevice(Reference):
+    """The reference's front-ends with every node evaluated by the product's
+    CUDA eval_gpu adapter (``make -C oracle ref_cuda``): the C++ integration
+    path, run on host buffers through the same bridge as ``Reference``."""
+
+    @staticmethod
+    def available(path: str = REF_CUDA_SO) -> bool:
+        return os.path.exists(path)
+
+    def __init__(self, path: str = REF_CUDA_SO):
+        super().__init__(path)
+        self.lib.ref_b200_sort.argtypes = [_i64, _i, _vp, _vp, _vp, _vp]
+
+    def b200_sort(self, isect_ids, flatten_ids, key_bits):
+        """The adapter's one-Primitive stable sort."""
+        ids = np.ascontiguousarray(isect_ids, np.int64)
+        fids = np.ascontiguousarray(flatten_ids, np.int32)
+        out_ids, out_fids = np.zeros_like(ids), np.zeros_like(fids)
+        _check(self.lib.ref_b200_sort(ids.size, int(key_bits), _p(ids), _p(fids), _p(out_ids),
+                                      _p(out_fids)), self.lib, "adapter sort")
+        return out_ids, out_fids

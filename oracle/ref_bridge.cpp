@@ -4,6 +4,12 @@
 // CPU baseline of bench.py to run the reference's `eval_cpu` code on host
 // buffers.  Nothing in the product links or loads this file.
 //
+// Built a second time with -DGSPLAT_SHIM_CUDA (oracle/_ref/
+// libgsplat_ref_cuda.so) together with the product's eval_gpu adapter
+// (gsplat-mlx_b200/adapter/): the same reference front-ends then dispatch
+// every node to the adapter's eval_gpu bodies, which call the B200 library --
+// the GPU test of that adapter.
+//
 // Every entry returns 0 on success and -1 when the reference threw; the
 // message is then available from ref_last_error().  Shapes are the dense
 // shapes the reference's tests use (leading [B] / [B,C] / [I] dims).
@@ -18,6 +24,9 @@
 #include "gsplat_core/include/gsplat_quat_scale_to_covar.h"
 #include "gsplat_core/include/gsplat_rasterize.h"
 #include "gsplat_core/include/gsplat_spherical_harmonics.h"
+#ifdef GSPLAT_SHIM_CUDA
+#include "gsplat_b200_mlx.h"
+#endif
 
 namespace mx = mlx::core;
 using gsplat_core::kCompensations;
@@ -25,6 +34,15 @@ using gsplat_core::kCompensations;
 namespace {
 
 thread_local std::string g_last_error;
+
+// The CPU build evaluates every node with eval_cpu; the device build
+// (GSPLAT_SHIM_CUDA, with the CUDA eval_gpu adapter linked in) puts every
+// front-end on a gpu stream, so that each node runs its eval_gpu.
+#ifdef GSPLAT_SHIM_CUDA
+constexpr mx::Device kDevice{mx::Device::gpu};
+#else
+constexpr mx::Device kDevice{mx::Device::cpu};
+#endif
 
 mx::array host(const void* p, mx::Shape shape, mx::Dtype dt) {
   return mx::array::from_host(p, std::move(shape), dt);
@@ -37,6 +55,7 @@ mx::array opt(const void* p, mx::Shape shape, mx::Dtype dt) {
 }
 
 void copy_out(const mx::array& a, void* dst) {
+  mx::detail::sync();
   if (dst != nullptr && a.nbytes() != 0) {
     std::memcpy(dst, a.data<void>(), a.nbytes());
   }
@@ -67,7 +86,7 @@ int ref_qs2c_fwd(const float* quats, const float* scales, int n,
     gsplat_core::QuatScaleToCovarPreciInput in = {
         .quats = host(quats, {n, 4}, mx::float32),
         .scales = host(scales, {n, 3}, mx::float32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .compute_covar = compute_covar != 0,
         .compute_preci = compute_preci != 0,
         .triu = triu != 0,
@@ -89,7 +108,7 @@ int ref_qs2c_bwd(const float* quats, const float* scales, const float* v_covars,
         .scales = host(scales, {n, 3}, mx::float32),
         .v_covars = opt(v_covars, cot, mx::float32),
         .v_precis = opt(v_precis, cot, mx::float32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .triu = triu != 0,
         .use_v_covars = v_covars != nullptr,
         .use_v_precis = v_precis != nullptr,
@@ -118,7 +137,7 @@ int ref_proj_fwd(int B, int C, int N, const float* means, const float* covars,
         .viewmats = host(viewmats, {B, C, 4, 4}, mx::float32),
         .Ks = host(Ks, {B, C, 3, 3}, mx::float32),
         .viewspace_points = empty_f32(),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .params = {
             .image_width = width,
             .image_height = height,
@@ -167,7 +186,7 @@ int ref_proj_bwd(int B, int C, int N, const float* means, const float* covars,
         .v_depths = host(v_depths, {B, C, N}, mx::float32),
         .v_conics = host(v_conics, {B, C, N, 3}, mx::float32),
         .v_compensations = opt(v_compensations, {B, C, N}, mx::float32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .params = {
             .image_width = width,
             .image_height = height,
@@ -200,7 +219,7 @@ int ref_sh_fwd(int n, int K, int degree, const float* dirs,
         .dirs = host(dirs, {n, 3}, mx::float32),
         .coeffs = host(coeffs, {n, K, 3}, mx::float32),
         .masks = opt(masks, {n}, mx::bool_),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .use_masks = masks != nullptr,
     };
     auto out = gsplat_core::gsplat_spherical_harmonics_forward(in);
@@ -220,7 +239,7 @@ int ref_sh_bwd(int n, int K, int degree, const float* dirs,
         .coeffs = host(coeffs, {n, K, 3}, mx::float32),
         .masks = opt(masks, {n}, mx::bool_),
         .v_colors = host(v_colors, {n, 3}, mx::float32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .use_masks = masks != nullptr,
         .compute_v_dirs = compute_v_dirs != 0,
     };
@@ -248,7 +267,7 @@ int ref_isect_tile(int I, int N, const float* means2d, const int32_t* radii,
         .opacities = empty_f32(),
         .image_ids = mx::zeros({0}, mx::int64),
         .gaussian_ids = mx::zeros({0}, mx::int64),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .params = {
             .I = I,
             .tile_size = tile_size,
@@ -279,7 +298,7 @@ int ref_isect_offset(int64_t n_isects, const int64_t* isect_ids, int I,
   return guarded([&] {
     auto out = gsplat_core::gsplat_intersect_offset(
         host(isect_ids, {static_cast<int>(n_isects)}, mx::int64), I,
-        tile_width, tile_height, mx::Device::cpu);
+        tile_width, tile_height, kDevice);
     copy_out(out, offsets);
   });
 }
@@ -305,7 +324,7 @@ int ref_raster_fwd(int I, int N, int channels, const float* means2d,
                              mx::int32),
         .flatten_ids = host(flatten_ids, {static_cast<int>(n_isects)},
                             mx::int32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .params = {
             .image_width = width,
             .image_height = height,
@@ -353,7 +372,7 @@ int ref_raster_bwd(int I, int N, int channels, const float* means2d,
                                 mx::float32),
         .v_render_alphas = host(v_render_alphas, {I, height, width, 1},
                                 mx::float32),
-        .s = mx::Device::cpu,
+        .s = kDevice,
         .params = {
             .image_width = width,
             .image_height = height,
@@ -373,5 +392,23 @@ int ref_raster_bwd(int I, int N, int channels, const float* means2d,
     copy_out(out[gsplat_core::kRasterVBackgrounds], v_backgrounds);
   });
 }
+
+#ifdef GSPLAT_SHIM_CUDA
+// The adapter's one-Primitive stable sort (gsplat_b200_mlx::
+// intersect_tile_sort), the replacement of argsort + take in
+// gsplat_intersect.cpp:266-286.
+int ref_b200_sort(int64_t n, int key_bits, const int64_t* isect_ids,
+                  const int32_t* flatten_ids, int64_t* sorted_isect_ids,
+                  int32_t* sorted_flatten_ids) {
+  return guarded([&] {
+    const int m = static_cast<int>(n);
+    auto out = gsplat_b200_mlx::intersect_tile_sort(host(isect_ids, {m}, mx::int64),
+                                                    host(flatten_ids, {m}, mx::int32),
+                                                    key_bits, kDevice);
+    copy_out(out[0], sorted_isect_ids);
+    copy_out(out[1], sorted_flatten_ids);
+  });
+}
+#endif
 
 }  // extern "C"
