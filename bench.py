@@ -193,6 +193,10 @@ def algorithmic_bytes(stage, N, C, visible, m, pixels, K, slots, kept=None):
         "isect_offset": m * 8,
         # opacity in, its two sigma bounds out
         "sigma_bounds": N * (4 + 8),
+        # tile offsets (forward) or the forward's tile costs (backward) in,
+        # the schedule out
+        "tile_order": slots * 8,
+        "tile_order_bwd": slots * 8,
         # per intersection: flatten id + Gaussian record; per pixel: outputs
         "rasterize_fwd": mk * 40 + pixels * 20,
         "rasterize_bwd": mk * (40 + 36) + pixels * 20,
@@ -235,8 +239,10 @@ def our_kernel_launches(entry_passes, bins, slots, tile_cull=False):
     scan = lambda n: 1 if n <= 16384 else 3  # noqa: E731
     binned = (3 + 1 + entry_passes + 1 + 1 + scan(bins) + 1 + 1 + scan(slots) + int(tile_cull)
               + 1)
-    # + the sigma bounds of the opacities 1
-    return 1 + 1 + 1 + 1 + binned + 1 + 1 + 1 + 1
+    # + the sigma bounds of the opacities 1, the totals' store to pinned host
+    # memory 1, the rasterizers' tile orders 2, the forward's fix-up pass of
+    # undecided pixels 1
+    return 1 + 1 + 1 + 1 + binned + 1 + 1 + 1 + 1 + 1 + 2 + 1
 
 
 # ------------------------------------------------------------------ CPU arms
@@ -462,6 +468,9 @@ def run_ours(args):
         for (n0, a), (n1, b) in zip(evs[:-1], evs[1:]):
             if n1 != "start":
                 this[n1] = this.get(n1, 0.0) + a.elapsed_time(b)
+        # stages on the side stream, beside the intersect pipeline
+        for n1, a, b in getattr(step, "side_spans", []):
+            this[n1] = this.get(n1, 0.0) + a.elapsed_time(b)
         for k, v in this.items():
             stage_ms.setdefault(k, []).append(v)
     step.events = None

@@ -179,7 +179,23 @@ struct RArgs {
   const int32_t* tile_offsets;
   const int32_t* flatten_ids;
   const float2* sbounds;  // per opacity entry: (keep, clamp) of sigma_bounds; null: computed
+  const int32_t* tile_order;  // CTA b renders slot tile_order[b]; null: slot b
+  int32_t* tile_cost;  // fwd, optional: per slot, the list entries its pixels walk
 };
+
+// The forward's record of a tile's cost for the backward's schedule: the
+// number of list entries the backward walks for the tile, max over its
+// pixels of (min(end - 1, last id) - start + 1), with an undecided pixel
+// counted as the whole list.  `my` is the thread's max of min(end - 1,
+// last id) (-1: no pixel); every thread of the CTA calls this.
+__device__ __forceinline__ void record_tile_cost(const RArgs& a, int64_t slot, int start, int my,
+                                                 int* s_cost) {
+  if (!a.tile_cost) return;
+  my = __reduce_max_sync(0xffffffffu, my);
+  if ((threadIdx.x & 31) == 0) atomicMax(s_cost, my);
+  __syncthreads();
+  if (threadIdx.x == 0) a.tile_cost[slot] = max(0, *s_cost - start + 1);
+}
 
 // Index of entry g's opacity (and opacity gradient).
 __device__ __forceinline__ int64_t opac_index(const RArgs& a, int64_t g) {
@@ -200,7 +216,7 @@ struct TileIdx {
 
 __device__ __forceinline__ TileIdx tile_of(const RArgs& a) {
   TileIdx t;
-  t.slot = blockIdx.x;
+  t.slot = a.tile_order ? __ldg(a.tile_order + blockIdx.x) : (int)blockIdx.x;
   const int64_t per = (int64_t)a.rows * a.tw;
   t.image = (int)(t.slot / per);
   const int loc = (int)(t.slot - (int64_t)t.image * per);
@@ -413,6 +429,7 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   float2* s_sb = reinterpret_cast<float2*>(smem + 6 * BLOCK);  // sigma bounds
   float* s_col = smem + 8 * BLOCK;                              // [BLOCK][ch]
 
+  __shared__ int s_cost;
   const TileIdx ti = tile_of(a);
   const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x;
@@ -428,8 +445,10 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
       render_alphas[pix] = 0.0f;
       last_ids[pix] = 0;
     }
+    if (a.tile_cost && tid == 0) a.tile_cost[ti.slot] = 0;
     return;
   }
+  if (tid == 0) s_cost = -1;
   int start, end;
   tile_range(a, ti.slot, start, end);
   const float px = (float)x + 0.5f, py = (float)y + 0.5f;
@@ -504,6 +523,9 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   // a pixel whose stop decision fell within the error bound is left to
   // raster_fix_kernel
   if (inside && unsure) last_ids[pix] = kUndecided;
+  __syncthreads();
+  record_tile_cost(a, ti.slot, start, inside ? (unsure ? end - 1 : min(end - 1, cur)) : -1,
+                   &s_cost);
 }
 
 // Recomputes exactly the pixels that the forward kernel left undecided
@@ -920,6 +942,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   __shared__ float2 s_d[THREADS];
   __shared__ int s_idx[THREADS];
   __shared__ int s_wcnt[THREADS / 32];
+  __shared__ int s_cost;
   const TileIdx ti = tile_of(a);
   const int image = ti.image, tile_x = ti.tile_x, tile_y = ti.tile_y;
   const int tid = threadIdx.x;
@@ -941,8 +964,10 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
       render_alphas[pix] = 0.0f;
       last_ids[pix] = 0;
     }
+    if (a.tile_cost && tid == 0) a.tile_cost[ti.slot] = 0;
     return;
   }
+  if (tid == 0) s_cost = -1;
   int start, end;
   tile_range(a, ti.slot, start, end);
   const float px = (float)x + 0.5f;
@@ -1005,9 +1030,14 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   }
   // pixels whose stop decision fell within the error bound are left to
   // raster_fix_kernel
+  int my = -1;
 #pragma unroll
-  for (int q = 0; q < P; ++q)
+  for (int q = 0; q < P; ++q) {
     if (uns >> q & 1u) last_ids[pix0 + (int64_t)q * RS * a.W] = kUndecided;
+    if (in[q]) my = max(my, (uns >> q & 1u) ? end - 1 : min(end - 1, cur[q]));
+  }
+  __syncthreads();
+  record_tile_cost(a, ti.slot, start, my, &s_cost);
 }
 
 // Reverse step of one pixel for one Gaussian (gsplat_rasterize.cpp:503-562);
@@ -1321,7 +1351,93 @@ RArgs make_args(const gs_raster_params* p, const float* means2d, const float* co
                opacities,
                p->use_backgrounds ? backgrounds : nullptr, p->use_masks ? masks : nullptr,
                tile_offsets, flatten_ids,
-               reinterpret_cast<const float2*>(p->sigma_bounds)};
+               reinterpret_cast<const float2*>(p->sigma_bounds), p->tile_order, p->tile_cost};
+}
+
+// Schedule of the rasterizer's CTAs: the slots in descending order of their
+// intersection-list length, bucketed at 1/8-octave steps (bucket = 8 floor
+// log2 len + the next three bits of len).  The hardware hands CTAs to SMs
+// in blockIdx order, so the longest tiles start first and the short ones
+// fill in behind them (longest-processing-time-first), instead of a long
+// tile that happens to come last running alone on an otherwise idle GPU.
+// One CTA: a shared histogram of the buckets, its scan, a scatter.  The
+// order inside a bucket is that of the shared atomics; it changes no
+// output, only which SM renders which tile when.
+constexpr int kOrderThreads = 1024;
+constexpr int kOrderBuckets = 256;
+
+__device__ __forceinline__ int length_bucket(int len) {
+  if (len <= 0) return 0;
+  const int lz = 31 - __clz(len);
+  const int frac = lz >= 3 ? (len >> (lz - 3)) & 7 : (len << (3 - lz)) & 7;
+  return min(kOrderBuckets - 1, lz * 8 + frac + 1);
+}
+
+__device__ __forceinline__ int slot_cost(const RArgs& a, const int32_t* cost, int t) {
+  if (cost) return __ldg(cost + t);
+  int start, end;
+  tile_range(a, t, start, end);
+  return end - start;
+}
+
+// Slots whose buckets the kernel keeps in shared memory between its passes
+// (more are recomputed in the second pass).
+constexpr int kOrderKeep = 32768;
+constexpr int kOrderUnroll = 4;
+
+__global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(RArgs a,
+                                                                  const int32_t* __restrict__ cost,
+                                                                  int32_t* __restrict__ order) {
+  __shared__ int hist[kOrderBuckets];
+  __shared__ uint8_t s_bucket[kOrderKeep];
+  const int n_slots = a.I * a.rows * a.tw;
+  const bool keep = n_slots <= kOrderKeep;
+  for (int i = threadIdx.x; i < kOrderBuckets; i += kOrderThreads) hist[i] = 0;
+  __syncthreads();
+  for (int t0 = threadIdx.x; t0 < n_slots; t0 += kOrderUnroll * kOrderThreads) {
+    int b[kOrderUnroll];
+#pragma unroll
+    for (int u = 0; u < kOrderUnroll; ++u) {  // the loads of every slot in flight first
+      const int t = t0 + u * kOrderThreads;
+      b[u] = t < n_slots ? slot_cost(a, cost, t) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < kOrderUnroll; ++u) {
+      const int t = t0 + u * kOrderThreads;
+      if (t >= n_slots) break;
+      const int bk = length_bucket(b[u]);
+      if (keep) s_bucket[t] = (uint8_t)bk;
+      atomicAdd(&hist[kOrderBuckets - 1 - bk], 1);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // exclusive scan of the 256 counts by one warp, 8 per lane
+    const int lane = threadIdx.x;
+    int v[8], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[k] = hist[lane * 8 + k];
+      sum += v[k];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += u;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      hist[lane * 8 + k] = run;
+      run += v[k];
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < n_slots; t += kOrderThreads) {
+    const int bk = keep ? (int)s_bucket[t] : length_bucket(slot_cost(a, cost, t));
+    order[atomicAdd(&hist[kOrderBuckets - 1 - bk], 1)] = t;
+  }
 }
 
 }  // namespace
@@ -1351,6 +1467,8 @@ extern "C" int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,
                             flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
   cudaStream_t s = as_stream(stream);
+  // the schedule: longest tile lists first
+  if (p->tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, nullptr, p->tile_order);
   switch (p->channels) {
     case 1: return launch_fwd<1>(a, block, render_colors, render_alphas, last_ids, s);
     case 2: return launch_fwd<2>(a, block, render_colors, render_alphas, last_ids, s);
@@ -1401,6 +1519,9 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
                             flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
   float* vbg = p->use_backgrounds ? v_backgrounds : nullptr;
+  // the schedule: costliest tiles (by the forward's record, else by list
+  // length) first
+  if (p->tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, p->tile_cost, p->tile_order);
   switch (p->channels) {
     case 1: return launch_bwd<1>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
     case 2: return launch_bwd<2>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
@@ -1408,6 +1529,21 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
     case 4: return launch_bwd<4>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
     default: return launch_bwd<0>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
   }
+}
+
+extern "C" int gs_raster_tile_order(const gs_raster_params* p, const int32_t* tile_offsets,
+                                    const int32_t* tile_cost, int32_t* tile_order,
+                                    gs_stream_t stream) {
+  if (int rc = check_raster(p)) return rc;
+  if (!tile_order || (!tile_offsets && !tile_cost))
+    return invalid("raster_tile_order: missing buffer");
+  gs_raster_params q = *p;
+  q.tile_order = nullptr;
+  q.tile_cost = nullptr;
+  const RArgs a = make_args(&q, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                            tile_offsets, nullptr);
+  tile_order_kernel<<<1, kOrderThreads, 0, as_stream(stream)>>>(a, tile_cost, tile_order);
+  return launch_status("raster_tile_order");
 }
 
 extern "C" int gs_rasterize_sigma_bounds(int64_t n, const float* opacities,

@@ -81,7 +81,8 @@ class RasterParams(ct.Structure):
                 ("image_height", _i32), ("tile_size", _i32), ("tile_width", _i32),
                 ("tile_height", _i32), ("n_isects", _i64), ("use_backgrounds", _i32),
                 ("use_masks", _i32), ("absgrad", _i32), ("tile_y0", _i32), ("tile_y1", _i32),
-                ("accumulate", _i32), ("shared_opacities", _i32), ("sigma_bounds", _vp)]
+                ("accumulate", _i32), ("shared_opacities", _i32), ("sigma_bounds", _vp),
+                ("tile_order", _vp), ("tile_cost", _vp)]
 
 
 _P = ct.POINTER
@@ -131,6 +132,7 @@ SIGNATURES = {
     "gs_isect_sort_noalloc": (ct.c_int, [_i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gs_isect_sort_noalloc_check": (ct.c_int, [_i64, _vp]),
     "gs_rasterize_sigma_bounds": (ct.c_int, [_i64, _vp, _vp, _i32, _vp, _vp]),
+    "gs_raster_tile_order": (ct.c_int, [_vp, _vp, _vp, _vp, _vp]),
     "gs_isect_sort_wait_selftest": (ct.c_int, [_i64, _vp, _vp, _vp, _vp, _vp, _sz,
                                                ct.c_uint32, _vp]),
     "gs_fit_activate": (ct.c_int, [_i64] + [_vp] * 9),

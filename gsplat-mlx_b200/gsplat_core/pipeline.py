@@ -105,6 +105,10 @@ class TrainingStep:
         self.total = torch.zeros((2,), dtype=torch.int64, device=self.dev)
         self.total_host = torch.zeros((2,), dtype=torch.int64, pin_memory=True)
         self.tile_offsets = e((C, self.th, self.tw), i32)
+        # the rasterizers' tile schedule (costliest tiles first), and the
+        # forward's per-tile cost record that orders the backward
+        self.tile_order = e((C * self.th * self.tw,), i32)
+        self.tile_cost = e((C * self.th * self.tw,), i32)
         self.render_colors = e((C, self.H, self.W, 3))
         self.render_alphas = e((C, self.H, self.W, 1))
         self.last_ids = e((C, self.H, self.W), i32)
@@ -171,6 +175,20 @@ class TrainingStep:
             ev.record()
             self.events.append((name, ev))
 
+    def _side_mark(self):
+        """A timing event on the side stream (None when not timing)."""
+        if self.events is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(self.side)
+        return ev
+
+    def _side_span(self, name, ev0):
+        """Records the side-stream stage that began at ``ev0``."""
+        ev1 = self._side_mark()
+        if ev0 is not None and ev1 is not None:
+            self.side_spans.append((name, ev0, ev1))
+
     def run(self, means, quats, scales, opacities, coeffs, viewmats, Ks, v_render_colors,
             v_render_alphas, sh_backward=True, colors=None, target=None, after_raster=None):
         """Forward and backward; returns the flat gradient buffer (a view of
@@ -210,6 +228,7 @@ class TrainingStep:
         self._mark("projection_fwd")
         projected = torch.cuda.Event()
         projected.record()
+        self.side_spans = []
         bounded = None
         gp = SHGlueParams(C, N, self.K, self.deg, 0)
         glue_pending = colors is None
@@ -241,8 +260,10 @@ class TrainingStep:
             counted = torch.cuda.Event()
             counted.record()
             if glue_pending:
-                # the SH colours are first needed by the rasterizer: the
-                # device computes them while the host reads the totals
+                # The SH colours are first needed by the rasterizer: the
+                # device computes them while the host reads the totals.  (On
+                # the side stream, beside the encode, they slowed the encode
+                # by about their own time: no gain.)
                 check(L.gs_sh_glue_fwd(ct.byref(gp), _p(means), _p(viewmats), _p(coeffs), None,
                                        _p(self.radii), _p(self.colors), s), "sh_glue_fwd")
                 self._mark("sh_fwd")
@@ -251,10 +272,12 @@ class TrainingStep:
             if bounded is None:
                 # launched now, the bounds kernel runs beside the encode
                 self.side.wait_event(projected)
+                t0 = self._side_mark()
                 check(L.gs_rasterize_sigma_bounds(N, _p(opacities), _p(self.radii), C,
                                                   _p(self.sbounds),
                                                   ct.c_void_p(self.side.cuda_stream)),
                       "rasterize_sigma_bounds")
+                self._side_span("sigma_bounds", t0)
                 bounded = torch.cuda.Event()
                 bounded.record(self.side)
             m, bins = (int(v) for v in self.total_host.tolist())
@@ -309,10 +332,10 @@ class TrainingStep:
                 check(L.gs_isect_offset_rows(m, _p(self.sorted_ids), C, self.tw, self.th, r0, r1,
                                              _p(self.tile_offsets), s), "isect_offset")
                 self._mark("isect_offset")
-            torch.cuda.current_stream().wait_event(bounded)
             rp = RasterParams(C, N, 3, self.W, self.H, self.ts, self.tw, self.th, m,
                               int(self.backgrounds is not None), 0, 0, y0, y1, int(b > 0), 1,
-                              _p(self.sbounds))
+                              _p(self.sbounds), _p(self.tile_order), _p(self.tile_cost))
+            torch.cuda.current_stream().wait_event(bounded)
             check(L.gs_rasterize_fwd(ct.byref(rp), _p(self.means2d), _p(self.conics),
                                      _p(colors), _p(opac), _p(self.backgrounds), None,
                                      _p(self.tile_offsets), _p(self.sorted_flatten),

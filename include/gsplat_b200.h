@@ -446,7 +446,34 @@ typedef struct {
                                 the kernels derive them per staged entry
                                 (same results, slower).  No reference
                                 counterpart. */
+  int32_t* tile_order;       /* optional scratch [slots = I * rows *
+                                tile_width]: when given, each rasterizer call
+                                first writes into it the order in which its
+                                kernel takes the tiles -- costliest first
+                                (gs_raster_tile_order: the forward by list
+                                length, the backward by tile_cost when given)
+                                -- so that no long tile is left to run alone
+                                at the end of the grid.  The outputs do not
+                                depend on it.  No reference counterpart. */
+  int32_t* tile_cost;        /* optional [slots]: gs_rasterize_fwd writes per
+                                tile the number of its list entries that its
+                                pixels walk, max over the pixels of
+                                (min(end - 1, last id) - start + 1) -- the
+                                backward pass's work on the tile;
+                                gs_rasterize_bwd orders its tiles by it.  No
+                                reference counterpart. */
 } gs_raster_params;
+
+/* The tiles of p's grid (its band, when tile_y1 > tile_y0) in descending
+ * order of their cost, at 1/8-octave resolution (bucket = 8 floor(log2 c) +
+ * the next three bits of c), into tile_order [I * rows * tile_width]: what
+ * the rasterizer calls write into p->tile_order before their kernels.  The
+ * cost is tile_cost [slots] when given, else the intersection-list length
+ * (p->n_isects and tile_offsets as for the rasterizer calls).  No reference
+ * counterpart. */
+int gs_raster_tile_order(const gs_raster_params* p, const int32_t* tile_offsets,
+                         const int32_t* tile_cost, int32_t* tile_order,
+                         gs_stream_t stream);
 
 /* The exact alpha decisions of the rasterizer as two sigma bounds per
  * opacity: bounds[2i] = the largest sigma at which o = opacities[i] still

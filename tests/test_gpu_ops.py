@@ -858,3 +858,115 @@ def test_rasterize_threshold_decisions_exact(gs, oracle, cuda, channels):
                            absgrad=True, **inp)
     for k, v in eb.items():
         assert_grad_close(b[k], v, f"threshold {k}", atol_frac=1e-4)
+
+
+def _length_bucket(x):
+    """The tile scheduler's cost bucket: 8 floor(log2 x) + the next three
+    bits of x, + 1 (0 for x <= 0)."""
+    x = np.asarray(x, np.int64)
+    out = np.zeros(x.shape, np.int64)
+    nz = x > 0
+    lz = np.floor(np.log2(x[nz])).astype(np.int64)
+    frac = np.where(lz >= 3, (x[nz] >> np.maximum(lz - 3, 0)) & 7,
+                    (x[nz] << np.maximum(3 - lz, 0)) & 7)
+    out[nz] = np.minimum(255, lz * 8 + frac + 1)
+    return out
+
+
+@pytest.mark.parametrize("I,tw,th", [(1, 82, 53), (3, 37, 23), (1, 1, 1)])
+def test_raster_tile_order(gs, cuda, I, tw, th):
+    """The rasterizers' tile schedule is a permutation of the slots in
+    non-increasing cost bucket: by list length from the offsets, or by the
+    given per-tile costs."""
+    import ctypes as ct
+    from gsplat_core import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(I * 1000 + tw)
+    n = I * tw * th
+    lens = rng.integers(0, 6000, size=n).astype(np.int64)
+    lens[::5] = 0
+    lens[1::7] = rng.integers(0, 8, size=lens[1::7].shape)
+    offs = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int32)
+    m = int(lens.sum())
+    rp = _lib.RasterParams(I, 10, 3, tw * 16, th * 16, 16, tw, th, m, 0, 0, 0)
+    s = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ct.c_void_p(t.data_ptr())  # noqa: E731
+    order = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+    assert lib.gs_raster_tile_order(ct.byref(rp), P(T(offs)), None, P(order), s) == 0
+    o = to_np(order).astype(np.int64)
+    assert np.array_equal(np.sort(o), np.arange(n))
+    b = _length_bucket(lens[o])
+    assert np.all(b[1:] <= b[:-1])
+    cost = rng.integers(0, 500, size=n).astype(np.int32)
+    assert lib.gs_raster_tile_order(ct.byref(rp), None, P(T(cost)), P(order), s) == 0
+    o = to_np(order).astype(np.int64)
+    assert np.array_equal(np.sort(o), np.arange(n))
+    b = _length_bucket(cost[o])
+    assert np.all(b[1:] <= b[:-1])
+
+
+def test_rasterize_fwd_tile_cost_and_ordered_backward(gs, oracle, golden, cuda):
+    """The forward's per-tile cost record (the list entries its pixels walk)
+    matches the oracle's last ids, and forward / backward run in the
+    schedules it gives produce the same images and gradients."""
+    import ctypes as ct
+    from gsplat_core import _lib
+    lib = _lib.load()
+    d = golden("chain_cfg3")
+    W, H, ts, inp = _raster_case(oracle, "chain_cfg3", d)
+    e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
+    dev = {k: T(v) for k, v in inp.items()}
+    th, tw = inp["tile_offsets"].shape[-2:]
+    n = tw * th
+    m = int(inp["flatten_ids"].size)
+    N = inp["means2d"].shape[1]
+    s = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ct.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+    order = torch.empty((n,), dtype=torch.int32, device="cuda")
+    cost = torch.full((n,), -7, dtype=torch.int32, device="cuda")
+    rp = _lib.RasterParams(1, N, 3, W, H, ts, tw, th, m, 1, 0, 0)
+    rp.tile_order = P(order)
+    rp.tile_cost = P(cost)
+    assert lib.gs_raster_tile_order(ct.byref(rp), P(dev["tile_offsets"]), None, P(order), s) == 0
+    rc = torch.empty((1, H, W, 3), device="cuda")
+    ra = torch.empty((1, H, W, 1), device="cuda")
+    li = torch.empty((1, H, W), dtype=torch.int32, device="cuda")
+    assert lib.gs_rasterize_fwd(ct.byref(rp), P(dev["means2d"]), P(dev["conics"]),
+                                P(dev["colors"]), P(dev["opacities"]), P(dev["backgrounds"]),
+                                None, P(dev["tile_offsets"]), P(dev["flatten_ids"]), P(rc),
+                                P(ra), P(li), s) == 0
+    assert_exact(to_np(li), e["last_ids"], "last_ids (length-ordered schedule)")
+    assert_exact(to_np(ra), to_np(gs.rasterize_to_pixels_3dgs_forward(dev, W, H, ts)[
+        "render_alphas"]), "alphas (length-ordered schedule)")
+    # the cost record from the oracle's last ids
+    off = inp["tile_offsets"].reshape(-1).astype(np.int64)
+    end = np.append(off[1:], m)
+    lp = np.full((th * ts, tw * ts), -1, np.int64)
+    lp[:H, :W] = np.minimum(e["last_ids"][0], np.repeat(np.repeat(
+        (end - 1).reshape(th, tw), ts, 0), ts, 1)[:H, :W])
+    tmax = lp.reshape(th, ts, tw, ts).max(axis=(1, 3)).reshape(-1)
+    want = np.maximum(0, tmax - off + 1)
+    # a tile with a pixel whose stop decision was left to the fix-up pass
+    # records its whole list
+    got = to_np(cost).astype(np.int64)
+    assert np.all((got == want) | (got == end - off)), "tile_cost"
+    assert np.mean(got == want) > 0.95
+    # the backward in the cost order equals the unordered backward
+    assert lib.gs_raster_tile_order(ct.byref(rp), None, P(cost), P(order), s) == 0
+    rng = np.random.default_rng(12)
+    vrc = T(rng.normal(size=(1, H, W, 3)).astype(np.float32))
+    vra = T(rng.normal(0, 0.1, size=(1, H, W, 1)).astype(np.float32))
+    out = {k: torch.empty_like(dev[src]) for k, src in
+           (("v_means2d", "means2d"), ("v_conics", "conics"), ("v_colors", "colors"),
+            ("v_opacities", "opacities"), ("v_backgrounds", "backgrounds"))}
+    assert lib.gs_rasterize_bwd(ct.byref(rp), P(dev["means2d"]), P(dev["conics"]),
+                                P(dev["colors"]), P(dev["opacities"]), P(dev["backgrounds"]),
+                                None, P(dev["tile_offsets"]), P(dev["flatten_ids"]), P(ra),
+                                P(li), P(vrc), P(vra), None, P(out["v_means2d"]),
+                                P(out["v_conics"]), P(out["v_colors"]), P(out["v_opacities"]),
+                                P(out["v_backgrounds"]), s) == 0
+    ref = gs.rasterize_to_pixels_3dgs_backward(dev, {"render_alphas": ra, "last_ids": li},
+                                               {"v_render_colors": vrc, "v_render_alphas": vra},
+                                               W, H, ts)
+    for k, v in out.items():
+        assert_grad_close(to_np(v), to_np(ref[k]), "ordered " + k, atol_frac=1e-5)
