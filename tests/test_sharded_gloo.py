@@ -34,7 +34,8 @@ def test_exchange_choice():
     from gsplat_core.sharded import choose_exchange, exchange_bytes
     n = 1_000_000
     assert choose_exchange(n, 16, 1, 1) == "allreduce"
-    assert choose_exchange(n, 16, 1, 8) == "shard"          # N divides evenly
+    assert choose_exchange(n, 16, 1, 8) == "gather"         # one camera per rank
+    assert choose_exchange(n, 16, 1, 2) == "gather"
     assert choose_exchange(n, 16, 4, 8) == "shard"          # 32 cameras on 8 GPUs
     assert choose_exchange(n + 1, 16, 1, 8) == "gather"     # uneven slices
     assert choose_exchange(n + 1, 16, 3, 8) == "gather"
