@@ -42,7 +42,7 @@ LINK_GBS = 770.0
 # DRAM bytes (read + write) per launch of each stage's dominant kernel from
 # one ncu capture of this benchmark (profiles/*_config3.md); None = not
 # captured.  Valid for the config-3 workload only.
-PROFILED_TRAFFIC = {"rasterize_bwd": 46.8e6, "rasterize_fwd": 19.0e6,
+PROFILED_TRAFFIC = {"rasterize_bwd": 47.1e6, "rasterize_fwd": 19.0e6,
                     "sh_bwd": 120.0e6 + 151.8e6, "projection_bwd": 86.4e6 + 13.7e6}
 
 
@@ -210,12 +210,13 @@ def algorithmic_bytes(stage, N, C, visible, m, pixels, K, slots, kept=None):
 
 
 # Warp instructions per launch of the rasterizers at config 3 (one pass of
-# `ncu --metrics smsp__inst_executed.sum`, profiles/raster_bwd16_config3.md
-# and raster_fwd16_config3.md): their roofline is the SMs' instruction issue,
+# `ncu --metrics gpu__time_duration.sum,smsp__inst_executed.sum`,
+# profiles/config3_step_launch_list.md): their roofline is the SMs' instruction issue,
 # 148 SMs x 4 schedulers x the sampled SM clock, not HBM.
-PROFILED_INSTS = {"rasterize_bwd": 364_690_155,
-                  # the forward kernel and its exact fix-up kernel
-                  "rasterize_fwd": 197_541_410 + 6_994_831}
+PROFILED_INSTS = {"rasterize_bwd": 363_260_217 + 9_720,  # + its tile-order kernel
+                  # the forward kernel, its tile-order kernel and the exact
+                  # fix-up kernel
+                  "rasterize_fwd": 198_175_693 + 9_720 + 6_878_520}
 
 
 def bin_count(cameras, tw, th):

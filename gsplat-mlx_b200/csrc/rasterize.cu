@@ -51,8 +51,9 @@ constexpr int32_t kUndecided = -1;
 //   within half an ulp; the product rounds once; zero for a clamped alpha,
 //   which is exact) and kStepErr the three roundings between the two
 //   recurrences.  A pixel
-//   whose next T lies within E of 1e-4 is marked and recomputed exactly by
-//   one warp at the end of the tile (exact_walk).
+//   whose next T lies within E of 1e-4 is marked undecided (last id
+//   kUndecided) and recomputed exactly, with the correctly rounded
+//   exponential, by raster_fix_kernel after the forward (exact_walk).
 constexpr float kAlphaErrS = 1.4e-7f;  // per unit of sigma: 1.173 ulp
 constexpr float kAlphaErr0 = 4.2e-7f;  // 2 ulp of __expf, 0.5 of the rounded e, 1 of the product
 constexpr float kStepErr = 2.0e-7f;    // three roundings of 2^-24

@@ -33,9 +33,10 @@ sums (up to fp32 summation order):
   + 4 (11 + 3K)) N bytes and 1/R of the SH backward, whatever R.  Needs N
   divisible by R.
 
-``"auto"`` picks shard when N divides evenly and the SH degree is above 0
-(it moves the fewest bytes and keeps the SH backward per rank constant),
-else the cheaper of the other two (ring estimates in ``exchange_bytes``).
+``"auto"`` picks the exchange that sends the fewest bytes per rank (ring
+estimates in ``exchange_bytes``; ties to the one with fewer collective
+steps): gather with one camera per rank (config 3's weak scaling), shard
+with many cameras per rank and N divisible by R.
 """
 from __future__ import annotations
 
