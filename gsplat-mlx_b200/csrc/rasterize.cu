@@ -192,6 +192,7 @@ struct RArgs {
 __device__ __forceinline__ void record_tile_cost(const RArgs& a, int64_t slot, int start, int my,
                                                  int* s_cost) {
   if (!a.tile_cost) return;
+  __syncthreads();  // s_cost's initial value is visible to every warp
   my = __reduce_max_sync(0xffffffffu, my);
   if ((threadIdx.x & 31) == 0) atomicMax(s_cost, my);
   __syncthreads();
@@ -199,13 +200,19 @@ __device__ __forceinline__ void record_tile_cost(const RArgs& a, int64_t slot, i
 }
 
 // Index of entry g's opacity (and opacity gradient).
-__device__ __forceinline__ int64_t opac_index(const RArgs& a, int64_t g) {
-  return a.opac_shared ? g % a.N : g;
+// With shared opacities entry g reads g mod N.  The lists of a tile of
+// image i hold the elements i N .. i N + N - 1 (the encode's flatten ids), so
+// g - i N is that remainder without a 64-bit division; other ids take the
+// division.
+__device__ __forceinline__ int64_t opac_index(const RArgs& a, int64_t g, int image) {
+  if (!a.opac_shared) return g;
+  const int64_t r = g - (int64_t)image * a.N;
+  return (uint64_t)r < (uint64_t)a.N ? r : g % a.N;
 }
 
-// (keep, clamp) sigma bounds of entry g with opacity o.
-__device__ __forceinline__ float2 entry_bounds(const RArgs& a, int64_t g, float o) {
-  return a.sbounds ? __ldg(a.sbounds + opac_index(a, g)) : sigma_bounds(o);
+// (keep, clamp) sigma bounds of entry g (of a tile of `image`) with opacity o.
+__device__ __forceinline__ float2 entry_bounds(const RArgs& a, int64_t g, int image, float o) {
+  return a.sbounds ? __ldg(a.sbounds + opac_index(a, g, image)) : sigma_bounds(o);
 }
 
 // The CTA's tile: `slot` indexes tile_offsets ([I, rows, tw]), `mask` the
@@ -266,6 +273,7 @@ __device__ __forceinline__ void exact_walk(const RArgs& a, int start, int end, i
                                         float* render_alphas, int32_t* last_ids) {
   const int ch = CH > 0 ? CH : a.CH;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __syncthreads();  // every thread has read the previous walk's final T
   if (tid == 0) {
     w.T = 1.0f;
     w.cur = 0;
@@ -288,8 +296,8 @@ __device__ __forceinline__ void exact_walk(const RArgs& a, int start, int end, i
       c0 = __ldg(con);
       c1 = __ldg(con + 1);
       c2 = __ldg(con + 2);
-      o = __ldg(a.opacities + opac_index(a, g));
-      if (a.sbounds) sb = __ldg(a.sbounds + opac_index(a, g));
+      o = __ldg(a.opacities + opac_index(a, g, image));
+      if (a.sbounds) sb = __ldg(a.sbounds + opac_index(a, g, image));
       if (CH > 0) {
         const float* cp = a.colors + (int64_t)g * ch;
         cl.x = __ldg(cp);
@@ -468,11 +476,11 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
     const int idx = b0 + tid;
     if (idx < end) {
       const int g = __ldg(a.flatten_ids + idx);
-      const float o = __ldg(a.opacities + opac_index(a, g));
+      const float o = __ldg(a.opacities + opac_index(a, g, image));
       s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
       s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
                               __ldg(a.conics + (int64_t)g * 3 + 2), o);
-      s_sb[tid] = entry_bounds(a, g, o);
+      s_sb[tid] = entry_bounds(a, g, image, o);
       for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
     }
     __syncthreads();
@@ -524,7 +532,6 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
   // a pixel whose stop decision fell within the error bound is left to
   // raster_fix_kernel
   if (inside && unsure) last_ids[pix] = kUndecided;
-  __syncthreads();
   record_tile_cost(a, ti.slot, start, inside ? (unsure ? end - 1 : min(end - 1, cur)) : -1,
                    &s_cost);
 }
@@ -582,6 +589,15 @@ inline unsigned fix_grid(const RArgs& a) {
   const int y0 = a.ty0 * a.ts, y1 = a.H < (a.ty0 + a.rows) * a.ts ? a.H : (a.ty0 + a.rows) * a.ts;
   const int64_t total = (int64_t)a.I * (y1 - y0) * a.W;
   return (unsigned)(total > 0 ? ceil_div(total, kFixPixels) : 1);
+}
+
+// The fix-up pass after a forward kernel.  (A variant that visited only the
+// tiles the forward flagged, one CTA walking all of a tile's undecided
+// pixels, was slower: the walks, not the scan, set this kernel's time, and
+// the pixel-row CTAs spread them wider.)
+template <int CH>
+void launch_fix(const RArgs& a, float* rc, float* ra, int32_t* li, cudaStream_t s) {
+  raster_fix_kernel<CH><<<fix_grid(a), kWalk, 0, s>>>(a, rc, ra, li);
 }
 
 // ------------------------------------------------------------------ backward
@@ -745,11 +761,11 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
     __syncthreads();
     if (tid < cnt) {
       const int g = __ldg(a.flatten_ids + b0 + tid);
-      const float o = __ldg(a.opacities + opac_index(a, g));
+      const float o = __ldg(a.opacities + opac_index(a, g, image));
       s_xy[tid] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
       s_co[tid] = make_float4(__ldg(a.conics + (int64_t)g * 3), __ldg(a.conics + (int64_t)g * 3 + 1),
                               __ldg(a.conics + (int64_t)g * 3 + 2), o);
-      s_sb[tid] = entry_bounds(a, g, o);
+      s_sb[tid] = entry_bounds(a, g, image, o);
       for (int c = 0; c < ch; ++c) s_col[tid * ch + c] = __ldg(a.colors + (int64_t)g * ch + c);
     }
     for (int i = tid; i < cnt * NT; i += BLOCK) s_acc[i] = 0.0f;
@@ -833,7 +849,7 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
       const int64_t gg = __ldg(a.flatten_ids + b0 + j);
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
       else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
-      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg), v);
+      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg, image), v);
       else if (k < 8) {
         if (absgrad) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);
       } else atomicAdd(v_colors + gg * ch + (k - 8), v);
@@ -862,7 +878,8 @@ constexpr int kT16SmallPixels = 1;
 // b = (conic2, opacity, col0, col1), c = (col2, col3), the intersection
 // index and the Gaussian id.
 template <int CH, int THREADS>
-__device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0, float y0,
+__device__ __forceinline__ int stage16(const RArgs& a, int image, int b0, int end, float x0,
+                                       float y0,
                                        float4* sa, float4* sb, float2* sc, float2* sd, int* sidx,
                                        int* sgid, int* swcnt) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -874,7 +891,7 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
     const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
     const float* con = a.conics + (int64_t)g * 3;
     keep = tile_may_hit(m.x, m.y, __ldg(con), __ldg(con + 1), __ldg(con + 2),
-                        __ldg(a.opacities + opac_index(a, g)), x0, y0);
+                        __ldg(a.opacities + opac_index(a, g, image)), x0, y0);
   }
   const unsigned bal = __ballot_sync(0xffffffffu, keep);
   if (lane == 0) swcnt[warp] = __popc(bal);
@@ -895,11 +912,11 @@ __device__ __forceinline__ int stage16(const RArgs& a, int b0, int end, float x0
     float cc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int c = 0; c < CH; ++c) cc[c] = __ldg(col + c);
-    const float o = __ldg(a.opacities + opac_index(a, g));
+    const float o = __ldg(a.opacities + opac_index(a, g, image));
     sa[slot] = make_float4(m.x, m.y, __ldg(con), __ldg(con + 1));
     sb[slot] = make_float4(__ldg(con + 2), o, cc[0], cc[1]);
     sc[slot] = make_float2(cc[2], cc[3]);
-    sd[slot] = entry_bounds(a, g, o);
+    sd[slot] = entry_bounds(a, g, image, o);
     sidx[slot] = idx;
     if (sgid) sgid[slot] = g;
   }
@@ -989,7 +1006,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
 
   for (int b0 = start; b0 < end; b0 += THREADS) {
     if (__syncthreads_count(!all_done()) == 0) break;
-    const int cnt = stage16<CH, THREADS>(a, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a,
+    const int cnt = stage16<CH, THREADS>(a, image, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a,
                                          s_b, s_c, s_d, s_idx, nullptr, s_wcnt);
     for (int j = 0; j < cnt; ++j) {
       if (all_done()) break;
@@ -1037,7 +1054,6 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
     if (uns >> q & 1u) last_ids[pix0 + (int64_t)q * RS * a.W] = kUndecided;
     if (in[q]) my = max(my, (uns >> q & 1u) ? end - 1 : min(end - 1, cur[q]));
   }
-  __syncthreads();
   record_tile_cost(a, ti.slot, start, my, &s_cost);
 }
 
@@ -1172,7 +1188,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
   for (int b_end = cta_last + 1; b_end > start; b_end -= THREADS) {
     const int b0 = max(start, b_end - THREADS);
     __syncthreads();
-    const int cnt = stage16<CH, THREADS>(a, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f,
+    const int cnt = stage16<CH, THREADS>(a, image, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f,
                                          s_a, s_b, s_c, s_d, s_idx, s_gid, s_wcnt);
     for (int i = tid; i < cnt * NT; i += THREADS) s_acc[i] = 0.0f;
     __syncthreads();
@@ -1229,7 +1245,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
       const int64_t gg = s_gid[j];
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
       else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
-      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg), v);
+      else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg, image), v);
       else if (k < CB) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);  // ABS only
       else atomicAdd(v_colors + gg * CH + (k - CB), v);
     }
@@ -1274,14 +1290,14 @@ int launch_fwd(const RArgs& a, int block, float* rc, float* ra, int32_t* li, cud
     else
       raster_fwd16_kernel<C1, kT16Pixels><<<(unsigned)tiles, 256 / kT16Pixels, 0, s>>>(a, rc, ra,
                                                                                         li);
-    raster_fix_kernel<C1><<<fix_grid(a), kWalk, 0, s>>>(a, rc, ra, li);
+    launch_fix<C1>(a, rc, ra, li, s);
     return launch_status("rasterize_fwd");
   }
   const int smem = smem_bytes(block, a.CH, false);
   cudaFuncSetAttribute(raster_fwd_kernel<CH>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int64_t tiles = (int64_t)a.I * a.rows * a.tw;
   raster_fwd_kernel<CH><<<(unsigned)tiles, block, smem, s>>>(a, rc, ra, li);
-  raster_fix_kernel<CH><<<fix_grid(a), kWalk, 0, s>>>(a, rc, ra, li);
+  launch_fix<CH>(a, rc, ra, li, s);
   return launch_status("rasterize_fwd");
 }
 
@@ -1384,6 +1400,14 @@ __device__ __forceinline__ int slot_cost(const RArgs& a, const int32_t* cost, in
 // Slots whose buckets the kernel keeps in shared memory between its passes
 // (more are recomputed in the second pass).
 constexpr int kOrderKeep = 32768;
+
+// Whether a rasterizer call follows its tile_order: grids of more tiles than
+// kOrderKeep (about 14 waves of the 16x16 kernels) keep slot order -- their
+// last wave is a small share of the work, and one CTA would take longer to
+// order them than the balance gains.
+inline bool scheduled(const RArgs& a) {
+  return a.tile_order && (int64_t)a.I * a.rows * a.tw <= kOrderKeep;
+}
 constexpr int kOrderUnroll = 4;
 
 __global__ void __launch_bounds__(kOrderThreads) tile_order_kernel(RArgs a,
@@ -1464,12 +1488,13 @@ extern "C" int gs_rasterize_fwd(const gs_raster_params* p, const float* means2d,
   if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_fwd: means2d must be 8-byte aligned");
   if (reinterpret_cast<uintptr_t>(p->sigma_bounds) % 8)
     return invalid("rasterize_fwd: sigma_bounds must be 8-byte aligned");
-  const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
-                            flatten_ids);
+  RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                      flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
   cudaStream_t s = as_stream(stream);
   // the schedule: longest tile lists first
-  if (p->tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, nullptr, p->tile_order);
+  if (!scheduled(a)) a.tile_order = nullptr;
+  if (a.tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, nullptr, p->tile_order);
   switch (p->channels) {
     case 1: return launch_fwd<1>(a, block, render_colors, render_alphas, last_ids, s);
     case 2: return launch_fwd<2>(a, block, render_colors, render_alphas, last_ids, s);
@@ -1516,13 +1541,14 @@ extern "C" int gs_rasterize_bwd(const gs_raster_params* p, const float* means2d,
   if (reinterpret_cast<uintptr_t>(means2d) % 8) return invalid("rasterize_bwd: means2d must be 8-byte aligned");
   if (reinterpret_cast<uintptr_t>(p->sigma_bounds) % 8)
     return invalid("rasterize_bwd: sigma_bounds must be 8-byte aligned");
-  const RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
-                            flatten_ids);
+  RArgs a = make_args(p, means2d, conics, colors, opacities, backgrounds, masks, tile_offsets,
+                      flatten_ids);
   const int block = ((p->tile_size * p->tile_size + 31) / 32) * 32;
   float* vbg = p->use_backgrounds ? v_backgrounds : nullptr;
   // the schedule: costliest tiles (by the forward's record, else by list
   // length) first
-  if (p->tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, p->tile_cost, p->tile_order);
+  if (!scheduled(a)) a.tile_order = nullptr;
+  if (a.tile_order) tile_order_kernel<<<1, kOrderThreads, 0, s>>>(a, p->tile_cost, p->tile_order);
   switch (p->channels) {
     case 1: return launch_bwd<1>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);
     case 2: return launch_bwd<2>(a, block, render_alphas, last_ids, v_render_colors, v_render_alphas, p->absgrad, v_means2d_abs, v_means2d, v_conics, v_colors, v_opacities, vbg, s);

@@ -453,7 +453,9 @@ typedef struct {
                                 (gs_raster_tile_order: the forward by list
                                 length, the backward by tile_cost when given)
                                 -- so that no long tile is left to run alone
-                                at the end of the grid.  The outputs do not
+                                at the end of the grid.  Grids of more than
+                                32768 tiles keep slot order (the scratch is
+                                then left untouched).  The outputs do not
                                 depend on it.  No reference counterpart. */
   int32_t* tile_cost;        /* optional [slots]: gs_rasterize_fwd writes per
                                 tile the number of its list entries that its
