@@ -1059,8 +1059,9 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
 
 // Reverse step of one pixel for one Gaussian (gsplat_rasterize.cpp:503-562);
 // adds the pixel's contributions to the Gaussian's gradient terms g[]:
-// [0,1] v_xy, [2,3,4] v_conic, [5] v_opacity, then with ABS [6,7] |v_xy|
-// and [8..8+CH) v_colors, without ABS [6..6+CH) v_colors.
+// [0,1] v_xy, [2,3,4] v_conic (terms 2 and 4 doubled, halved once at the
+// flush), [5] v_opacity, then with ABS [6,7] |v_xy| and [8..8+CH)
+// v_colors, without ABS [6..6+CH) v_colors.
 //
 // The reference's per-channel terms are folded into scalars per pixel:
 //   v_alpha = sum_c (col_c T - buf_c ra) vrc_c + ra T_final (v_ra - bg.vrc)
@@ -1081,7 +1082,9 @@ __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, co
   const float vis = __expf(-sg.s);
   const float ov = __fmul_rn(B.y, vis);
   const float alpha = clamped ? kMaxAlpha : fminf(kMaxAlpha, ov);
-  const float ra = __fdividef(1.0f, fmaxf(kMinOneMinusAlpha, 1.0f - alpha));
+  // alpha <= 0.99, so 1 - alpha >= 0.01 and the reference's max(1e-6, .)
+  // never binds
+  const float ra = __fdividef(1.0f, 1.0f - alpha);
   Tr *= ra;
   const float fac = alpha * Tr;
   float cdot = col[0] * v_rc[0];
@@ -1098,9 +1101,9 @@ __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, co
     const float vy = fmaf(A.w, vsdx, v_sigma * sg.cdy);   // v_sigma (c1 dx + c2 dy)
     g[0] += vx;
     g[1] += vy;
-    g[2] = fmaf(0.5f * vsdx, dx, g[2]);
+    g[2] = fmaf(vsdx, dx, g[2]);  // halved at the flush (exact: a power of two)
     g[3] = fmaf(vsdx, dy, g[3]);
-    g[4] = fmaf(0.5f * vsdy, dy, g[4]);
+    g[4] = fmaf(vsdy, dy, g[4]);  // halved at the flush
     g[5] = fmaf(vis, v_alpha, g[5]);
     if (ABS) {
       g[6] += fabsf(vx);
@@ -1244,7 +1247,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
       const int j = i / NT, k = i - j * NT;
       const int64_t gg = s_gid[j];
       if (k < 2) atomicAdd(v_means2d + gg * 2 + k, v);
-      else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), v);
+      else if (k < 5) atomicAdd(v_conics + gg * 3 + (k - 2), k == 3 ? v : 0.5f * v);
       else if (k == 5) atomicAdd(v_opacities + opac_index(a, gg, image), v);
       else if (k < CB) atomicAdd(v_means2d_abs + gg * 2 + (k - 6), v);  // ABS only
       else atomicAdd(v_colors + gg * CH + (k - CB), v);
