@@ -970,3 +970,23 @@ def test_rasterize_fwd_tile_cost_and_ordered_backward(gs, oracle, golden, cuda):
                                                W, H, ts)
     for k, v in out.items():
         assert_grad_close(to_np(v), to_np(ref[k]), "ordered " + k, atol_frac=1e-5)
+
+
+def test_rasterize_nonfinite_opacities(gs, oracle, golden, cuda):
+    """NaN and infinite opacities decide as the reference does (its
+    std::min(0.99f, NaN) is 0.99: such a Gaussian is composited and clamped
+    everywhere; -inf is never composited).  The oracle agrees with the
+    reference's own eval_cpu on this case bit for bit."""
+    d = golden("chain_cfg1")
+    W, H, ts, inp = _raster_case(oracle, "chain_cfg1", d)
+    op = inp["opacities"].copy()
+    idx = np.random.default_rng(3).choice(op.size, 40, replace=False)
+    op.reshape(-1)[idx[:15]] = np.nan
+    op.reshape(-1)[idx[15:30]] = np.inf
+    op.reshape(-1)[idx[30:]] = -np.inf
+    inp["opacities"] = op
+    e = oracle.raster_fwd(width=W, height=H, tile_size=ts, **inp)
+    g = gs.rasterize_to_pixels_3dgs_forward({k: T(v) for k, v in inp.items()}, W, H, ts)
+    assert_exact(to_np(g["last_ids"]), e["last_ids"], "last_ids")
+    assert_fwd_close(to_np(g["render_alphas"]), e["render_alphas"], "alphas")
+    assert_fwd_close(to_np(g["render_colors"]), e["render_colors"], "colors")

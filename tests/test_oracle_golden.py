@@ -241,6 +241,28 @@ def test_oracle_against_live_reference(oracle):
     assert_exact(oracle.isect_offset(ids, 2, 64, 64), ref.isect_offset(ids, 2, 64, 64), "offsets")
 
 
+def test_oracle_nonfinite_opacities_match_reference(oracle, golden):
+    """NaN / +inf / -inf opacities: the oracle's rasterizer forward decides
+    as the reference's eval_cpu (std::min(0.99f, NaN) is 0.99)."""
+    from oracle.oracle import Reference
+    if not Reference.available():
+        pytest.skip("oracle/_ref not built in this checkout")
+    ref = Reference()
+    d = golden("chain_cfg1")
+    W, H, ts = int(d["width"]), int(d["height"]), int(d["tile_size"])
+    op = d["opacities"].copy()
+    idx = np.random.default_rng(3).choice(op.size, 40, replace=False)
+    op[idx[:15]], op[idx[15:30]], op[idx[30:]] = np.nan, np.inf, -np.inf
+    inp = dict(means2d=d["proj_means2d"].reshape(1, -1, 2),
+               conics=d["proj_conics"].reshape(1, -1, 3), colors=d["colors"],
+               opacities=op[None], tile_offsets=d["tile_offsets"],
+               flatten_ids=d["isect_flatten_ids"])
+    a = oracle.raster_fwd(width=W, height=H, tile_size=ts, threads=1, **inp)
+    b = ref.raster_fwd(width=W, height=H, tile_size=ts, **inp)
+    for k in a:
+        assert_exact(a[k], b[k], "non-finite opacities " + k)
+
+
 def _densify_cfg(d):
     cfg = {k: float(d[k]) for k in ("grow_grad2d", "grow_scale3d", "grow_scale2d", "prune_opa",
                                     "prune_scale3d", "prune_scale2d", "scene_scale")}
