@@ -457,9 +457,26 @@ class ReferenceOnDevice(Reference):
 
     @staticmethod
     def available(path: str = REF_CUDA_SO) -> bool:
-        return os.path.exists(path)
+        """Built, and against the current C ABI header: a build from an older
+        header would pass the library parameter structs of another layout."""
+        return os.path.exists(path) and ReferenceOnDevice.abi_current(path)
+
+    @staticmethod
+    def abi_current(path: str = REF_CUDA_SO) -> bool:
+        import hashlib
+        header = os.path.join(os.path.dirname(_HERE), "include", "gsplat_b200.h")
+        try:
+            with open(path + ".abi") as f:
+                built = f.read().strip()
+            with open(header, "rb") as f:
+                return built == hashlib.sha256(f.read()).hexdigest()
+        except OSError:
+            return False
 
     def __init__(self, path: str = REF_CUDA_SO):
+        if not self.abi_current(path):
+            raise RuntimeError(f"{path} was built against another gsplat_b200.h "
+                               "(make -C oracle ref_cuda)")
         super().__init__(path)
         self.lib.ref_b200_sort.argtypes = [_i64, _i, _vp, _vp, _vp, _vp]
 

@@ -27,7 +27,8 @@ def T(x, dev="cuda"):
 def dev(cuda):
     from oracle.oracle import ReferenceOnDevice
     if not ReferenceOnDevice.available():
-        pytest.skip("adapter build absent (make -C oracle ref_cuda REF=<reference tree>)")
+        pytest.skip("adapter build absent or built against another gsplat_b200.h "
+                    "(make -C oracle ref_cuda REF=<reference tree>)")
     return ReferenceOnDevice()
 
 
