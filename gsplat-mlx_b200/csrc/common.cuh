@@ -69,12 +69,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 // rounding of the per-pixel sigma and of __expf; such a Gaussian would be
 // skipped by every pixel of the tile (alpha < 1/255), so dropping it
 // changes no output bit.  Conics that are not positive definite are kept,
-// and so are NaN and +inf opacities (the reference's std::min(0.99f, NaN)
-// is 0.99: such a Gaussian is composited wherever sigma >= 0).
+// and so are non-finite opacities (the reference's std::min(0.99f, NaN) is
+// 0.99: a NaN or +inf opacity is composited wherever sigma >= 0, a -inf one
+// where its exponential underflows and -inf * 0 is NaN).
 __device__ __forceinline__ bool tile_may_hit(float mx, float my, float c0, float c1, float c2,
                                              float o, float x0, float y0,
                                              float span = 15.0f) {
-  if (!(o < INFINITY)) return true;
+  if (!(fabsf(o) < INFINITY)) return true;
   if (!(c0 > 0.0f && c2 > 0.0f && c0 * c2 - c1 * c1 > 0.0f)) return true;
   const float dxl = mx - (x0 + span), dxh = mx - x0;
   const float dyl = my - (y0 + span), dyh = my - y0;

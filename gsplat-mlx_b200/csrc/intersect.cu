@@ -956,7 +956,9 @@ __device__ __forceinline__ float fast_sqrt(float x) {
 
 __device__ __forceinline__ uint32_t bin_hit_mask(uint32_t m, float mx, float my, float c0,
                                                  float c1, float c2, float o, int ts) {
-  if (!(c0 > 0.0f && c2 > 0.0f) || !(o < INFINITY)) return m;  // NaN / +inf: alpha 0.99
+  // non-finite opacities reach alpha 0.99 somewhere (NaN, +inf: everywhere;
+  // -inf: where the exponential underflows): kept
+  if (!(c0 > 0.0f && c2 > 0.0f) || !(fabsf(o) < INFINITY)) return m;
   const float pc = c1 * c1;
   const float det = __fadd_rn(__fmaf_rn(c0, c2, -pc), -__fmaf_rn(c1, c1, -pc));
   if (!(det > 0.0f)) return m;

@@ -95,8 +95,20 @@ __device__ __forceinline__ float root_up(double m) {  // smallest float s with e
   return s;
 }
 
+// The smallest float sigma with CR(e^-sigma) == 0: e^-sigma <= 2^-150 (which
+// rounds to zero, ties to even), i.e. sigma >= 150 ln 2 = 103.9720770...
+// rounded up.  glibc's expf agrees at this boundary (0 at -S, the smallest
+// subnormal one float below).
+constexpr float kUnderflowSigma = 0x1.9fe36ap+6f;  // 103.972084
+
+// An opacity of -inf: -inf (x) e is -inf (skipped) while e > 0 and NaN once
+// the exponential underflows, which the reference's std::min(0.99f, NaN)
+// turns into alpha 0.99.  Its bounds are (-kUnderflowSigma, +inf): a negative
+// finite keep bound marks the composited range [kUnderflowSigma, +inf] (see
+// keep_range), always clamped.
 __device__ __noinline__ float2 sigma_bounds(float o) {
   if (!(o < INFINITY)) return make_float2(INFINITY, INFINITY);
+  if (o == -INFINITY) return make_float2(-kUnderflowSigma, INFINITY);
   float2 b = make_float2(-INFINITY, -INFINITY);
   if (!(o > 0.0f)) return b;
   // smallest e with o (x) e >= 1/255
@@ -161,9 +173,23 @@ __device__ __forceinline__ Sigma gauss_sigma(float dx, float dy, float c0, float
   return r;
 }
 
-// Composited (reference: !(sigma < 0 || alpha < 1/255)) for keep bound sk.
-__device__ __forceinline__ bool composited(float sigma, float sk) {
-  return !(sigma < 0.0f) && !(sigma > sk);
+// The sigma range [lo, hi] in which an entry's pairs are composited, from
+// its keep bound: [0, keep] (keep >= 0, or -inf: never), or for the -inf
+// opacity marker (a negative finite keep, -kUnderflowSigma) [-keep, +inf].
+// Worked out once per entry, outside the pixel loops.
+struct Range {
+  float lo, hi;
+};
+__device__ __forceinline__ Range keep_range(float keep) {
+  const bool under = keep < 0.0f && keep > -INFINITY;
+  return Range{under ? -keep : 0.0f, under ? INFINITY : keep};
+}
+
+// Composited (reference: !(sigma < 0 || alpha < 1/255)) for the entry's
+// range; a NaN sigma is composited, as the reference's min(0.99, NaN) is
+// 0.99.
+__device__ __forceinline__ bool composited(float sigma, Range r) {
+  return !(sigma < r.lo) && !(sigma > r.hi);
 }
 
 struct RArgs {
@@ -317,7 +343,7 @@ __device__ __forceinline__ void exact_walk(const RArgs& a, int start, int end, i
     if (idx < end) {
       const float sigma = gauss_sigma(__fsub_rn(m.x, px), __fsub_rn(m.y, py), c0, c1, c2).s;
       if (!a.sbounds) sb = sigma_bounds(o);
-      take = composited(sigma, sb.x);
+      take = composited(sigma, keep_range(sb.x));
       if (take) al = sigma < sb.y ? kMaxAlpha : fminf(kMaxAlpha, __fmul_rn(o, exp_cr(-sigma)));
     }
     if (cb + kWalk < end) load(cb + kWalk);  // in flight during the fold
@@ -491,7 +517,7 @@ __global__ void raster_fwd_kernel(RArgs a, float* __restrict__ render_colors,
       const float2 sb = s_sb[j];
       const float dx = m.x - px, dy = m.y - py;
       const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
-      if (!composited(sigma, sb.x)) continue;
+      if (!composited(sigma, keep_range(sb.x))) continue;
       const bool clamped = !(sigma >= sb.y);  // o e^-sigma > 0.99 (or NaN)
       const float alpha = fast_alpha(sigma, co.w, clamped);
       const float vis = alpha * Tr;
@@ -782,7 +808,7 @@ __global__ void raster_bwd_kernel(RArgs a, const float* __restrict__ render_alph
         dx = m.x - px;
         dy = m.y - py;
         const float sigma = gauss_sigma(dx, dy, co.x, co.y, co.z).s;
-        valid = composited(sigma, sb.x);
+        valid = composited(sigma, keep_range(sb.x));
         clamped = !(sigma >= sb.y);  // the reference's !(o * vis <= 0.99)
         vis = __expf(-sigma);
         alpha = clamped ? kMaxAlpha : fminf(kMaxAlpha, __fmul_rn(co.w, vis));
@@ -875,12 +901,14 @@ constexpr int kT16SmallPixels = 1;
 // loads entry b0 + t, tests it against the tile, and the kept entries are
 // compacted in list order into the packed shared arrays.  Returns the
 // number kept.  Entries: a = (mean x, mean y, conic0, conic1),
-// b = (conic2, opacity, col0, col1), c = (col2, col3), the intersection
-// index and the Gaussian id.
+// b = (conic2, opacity, col0, col1), c = (col2, col3), d = (upper end of
+// the composited sigma range, clamp bound), its lower end, the
+// intersection index and the Gaussian id.
 template <int CH, int THREADS>
 __device__ __forceinline__ int stage16(const RArgs& a, int image, int b0, int end, float x0,
                                        float y0,
-                                       float4* sa, float4* sb, float2* sc, float2* sd, int* sidx,
+                                       float4* sa, float4* sb, float2* sc, float2* sd,
+                                       float* slo, int* sidx,
                                        int* sgid, int* swcnt) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int idx = b0 + tid;
@@ -916,7 +944,12 @@ __device__ __forceinline__ int stage16(const RArgs& a, int image, int b0, int en
     sa[slot] = make_float4(m.x, m.y, __ldg(con), __ldg(con + 1));
     sb[slot] = make_float4(__ldg(con + 2), o, cc[0], cc[1]);
     sc[slot] = make_float2(cc[2], cc[3]);
-    sd[slot] = entry_bounds(a, g, image, o);
+    // the composited range's upper end and the clamp bound; the lower end
+    // apart (0 but for the -inf opacity marker)
+    const float2 bnd = entry_bounds(a, g, image, o);
+    const Range rg = keep_range(bnd.x);
+    sd[slot] = make_float2(rg.hi, bnd.y);
+    slo[slot] = rg.lo;
     sidx[slot] = idx;
     if (sgid) sgid[slot] = g;
   }
@@ -928,10 +961,11 @@ __device__ __forceinline__ int stage16(const RArgs& a, int image, int b0, int en
 // decision is left to the exact walk.
 template <int CH>
 __device__ __forceinline__ int composite16(float dx, float dy, const float4& A, const float4& B,
-                                           float2 sb, float dg, const float* col, float& Tr,
+                                           float2 sb, Range r, float dg, const float* col,
+                                           float& Tr,
                                            float& E, float* acc, int& cur, int idx) {
   const float sigma = gauss_sigma(dx, dy, A.z, A.w, B.x).s;
-  if (!composited(sigma, sb.x)) return 0;
+  if (!composited(sigma, r)) return 0;
   const bool clamped = !(sigma >= sb.y);  // o e^-sigma > 0.99 (or NaN)
   const float alpha = fast_alpha(sigma, B.y, clamped);
   const float vis = alpha * Tr;
@@ -958,6 +992,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   __shared__ float4 s_b[THREADS];
   __shared__ float2 s_c[THREADS];
   __shared__ float2 s_d[THREADS];
+  __shared__ float s_lo[THREADS];
   __shared__ int s_idx[THREADS];
   __shared__ int s_wcnt[THREADS / 32];
   __shared__ int s_cost;
@@ -1007,7 +1042,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
   for (int b0 = start; b0 < end; b0 += THREADS) {
     if (__syncthreads_count(!all_done()) == 0) break;
     const int cnt = stage16<CH, THREADS>(a, image, b0, end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f, s_a,
-                                         s_b, s_c, s_d, s_idx, nullptr, s_wcnt);
+                                         s_b, s_c, s_d, s_lo, s_idx, nullptr, s_wcnt);
     for (int j = 0; j < cnt; ++j) {
       if (all_done()) break;
       const float4 A = s_a[j];
@@ -1022,10 +1057,11 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
       const float dx = A.x - px;
       const int idx = s_idx[j];
       const float dg = alpha_err(sb.x);
+      const Range r{s_lo[j], sb.x};
 #pragma unroll
       for (int q = 0; q < P; ++q)
         if (!(dn >> q & 1u)) {
-          const int st = composite16<CH>(dx, A.y - py[q], A, B, sb, dg, col, Tr[q], tb[q],
+          const int st = composite16<CH>(dx, A.y - py[q], A, B, sb, r, dg, col, Tr[q], tb[q],
                                          acc[q], cur[q], idx);
           if (st) {
             dn |= 1u << q;
@@ -1072,12 +1108,12 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_fwd16_kernel(
 // argument in [0.01, 1]).
 template <int CH, bool ABS>
 __device__ __forceinline__ bool backward16(bool in_range, float dx, float dy, const float4& A,
-                                           const float4& B, float2 sb, const float* col,
+                                           const float4& B, float2 sb, Range r, const float* col,
                                            float& Tr, float& bufdot, float K, const float* v_rc,
                                            float* g) {
   if (!in_range) return false;
   const Sigma sg = gauss_sigma(dx, dy, A.z, A.w, B.x);
-  if (!composited(sg.s, sb.x)) return false;
+  if (!composited(sg.s, r)) return false;
   const bool clamped = !(sg.s >= sb.y);  // the reference's !(o * vis <= 0.99)
   const float vis = __expf(-sg.s);
   const float ov = __fmul_rn(B.y, vis);
@@ -1127,6 +1163,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
   __shared__ float4 s_b[THREADS];
   __shared__ float2 s_c[THREADS];
   __shared__ float2 s_d[THREADS];
+  __shared__ float s_lo[THREADS];
   __shared__ int s_idx[THREADS];
   __shared__ int s_gid[THREADS];
   __shared__ int s_wcnt[THREADS / 32];
@@ -1192,7 +1229,7 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
     const int b0 = max(start, b_end - THREADS);
     __syncthreads();
     const int cnt = stage16<CH, THREADS>(a, image, b0, b_end, tile_x * 16 + 0.5f, tile_y * 16 + 0.5f,
-                                         s_a, s_b, s_c, s_d, s_idx, s_gid, s_wcnt);
+                                         s_a, s_b, s_c, s_d, s_lo, s_idx, s_gid, s_wcnt);
     for (int i = tid; i < cnt * NT; i += THREADS) s_acc[i] = 0.0f;
     __syncthreads();
     for (int j = cnt - 1; j >= 0; --j) {
@@ -1210,10 +1247,11 @@ __global__ void __launch_bounds__(256 / P, 4 * P) raster_bwd16_kernel(
       for (int i = 0; i < 16; ++i) g[i] = 0.0f;
       const float dx = A.x - px;
       const float2 sb = s_d[j];
+      const Range r{s_lo[j], sb.x};
       bool any = false;
 #pragma unroll
       for (int q = 0; q < P; ++q)
-        any |= backward16<CH, ABS>(idx <= last[q], dx, A.y - py[q], A, B, sb, col, Tr[q],
+        any |= backward16<CH, ABS>(idx <= last[q], dx, A.y - py[q], A, B, sb, r, col, Tr[q],
                                    bufdot[q], K[q], vrc[q], g);
       const unsigned active = __ballot_sync(0xffffffffu, any);
       if (!active) continue;

@@ -482,7 +482,10 @@ int gs_raster_tile_order(const gs_raster_params* p, const int32_t* tile_offsets,
  * reaches alpha >= 1/255, bounds[2i+1] = the smallest sigma at which
  * o e^-sigma <= 0.99 (alpha not clamped), both with the correctly rounded
  * exponential and the reference's float multiply (-inf: never composited /
- * never clamped; NaN or +inf opacity: +inf, +inf).  Pass them through
+ * never clamped; NaN or +inf opacity: +inf, +inf; a -inf opacity, which the
+ * reference composites at alpha 0.99 exactly where e^-sigma underflows to 0
+ * (-inf * 0 is NaN, min(0.99, NaN) is 0.99): -103.972084, +inf, a negative
+ * keep bound marking the range [103.972084, +inf]).  Pass them through
  * gs_raster_params.sigma_bounds.  With radii ([cameras, n, 2], 8-byte
  * aligned) only the entries some camera sees (both radii > 0) are written:
  * the others have no intersections, so no rasterizer reads them.  No

@@ -973,9 +973,10 @@ def test_rasterize_fwd_tile_cost_and_ordered_backward(gs, oracle, golden, cuda):
 
 
 def test_rasterize_nonfinite_opacities(gs, oracle, golden, cuda):
-    """NaN and infinite opacities decide as the reference does (its
-    std::min(0.99f, NaN) is 0.99: such a Gaussian is composited and clamped
-    everywhere; -inf is never composited).  The oracle agrees with the
+    """NaN and infinite opacities decide as the reference does: its
+    std::min(0.99f, NaN) is 0.99, so a NaN or +inf opacity is composited and
+    clamped wherever sigma >= 0, and a -inf one exactly where its
+    exponential underflows (-inf * 0 is NaN).  The oracle agrees with the
     reference's own eval_cpu on this case bit for bit."""
     d = golden("chain_cfg1")
     W, H, ts, inp = _raster_case(oracle, "chain_cfg1", d)
