@@ -213,10 +213,10 @@ def algorithmic_bytes(stage, N, C, visible, m, pixels, K, slots, kept=None):
 # `ncu --metrics gpu__time_duration.sum,smsp__inst_executed.sum`,
 # profiles/config3_step_launch_list.md): their roofline is the SMs' instruction issue,
 # 148 SMs x 4 schedulers x the sampled SM clock, not HBM.
-PROFILED_INSTS = {"rasterize_bwd": 363_260_217 + 9_720,  # + its tile-order kernel
+PROFILED_INSTS = {"rasterize_bwd": 356_746_241 + 9_720,  # + its tile-order kernel
                   # the forward kernel, its tile-order kernel and the exact
                   # fix-up kernel
-                  "rasterize_fwd": 198_175_693 + 9_720 + 6_878_520}
+                  "rasterize_fwd": 199_708_576 + 9_720 + 6_687_814}
 
 
 def bin_count(cameras, tw, th):
