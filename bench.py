@@ -113,8 +113,13 @@ def scene_for(rank, world, seed, workload="cfg3"):
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the
-    timed region runs."""
+    """Clocks and throttle reasons while the timed region runs: nvidia-smi
+    every 200 ms, and NVML (read-only queries) every 5 ms from a thread, so
+    that a timed region shorter than nvidia-smi's interval is sampled too."""
+
+    # NVML clock event reason bits
+    NVML_REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40,
+                    "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -124,8 +129,45 @@ class ClockSampler:
         self.gpu = gpu_id
         self.proc = None
         self.lines = []
+        self.nvml = []  # (sm MHz, max sm MHz, reason bits), inside begin() .. end()
+        self._stop = threading.Event()
+        self._active = threading.Event()
+        self.nt = None
+
+    def begin(self):
+        """The timed region starts: NVML samples are kept from here on."""
+        self._active.set()
+
+    def end(self):
+        self._active.clear()
+
+    def _nvml_loop(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+        except Exception:  # no NVML binding or library: nvidia-smi alone
+            return
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(self.gpu)
+            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while True:
+                if self._active.is_set():
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.nvml.append((float(sm), float(smax), int(bits)))
+                if self._stop.wait(0.005):
+                    break
+        except Exception:
+            pass
+        finally:
+            try:
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def start(self):
+        self.nt = threading.Thread(target=self._nvml_loop, daemon=True)
+        self.nt.start()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -141,14 +183,24 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        self._stop.set()
+        if self.nt is not None:
+            self.nt.join(timeout=5)
         sm, smax, reasons = [], [], set()
+        for c, cm, bits in self.nvml:
+            sm.append(c)
+            smax.append(cm)
+            reasons.update(nm for nm, b in self.NVML_REASONS.items() if bits & b)
+        if self.proc is None:
+            if not sm:
+                return {"sm_mhz": None, "sm_max_mhz": None,
+                        "reasons": ["nvidia-smi unavailable"]}
+        else:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
@@ -164,7 +216,8 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": float(np.median(sm)) if sm else None,
                 "sm_max_mhz": float(max(smax)) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "nvml_samples": len(self.nvml)}
 
 
 # ------------------------------------------------------------------ helpers
@@ -368,11 +421,13 @@ def run_fit(args):
     clocks.start()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    clocks.begin()
     t0.record()
     for _ in range(args.steps):
         losses.append(float(fit.run().item()))   # the trainer's per-step loss read
     t1.record()
     torch.cuda.synchronize()
+    clocks.end()
     clk = clocks.stop()
     t = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
     if world > 1:
@@ -454,6 +509,7 @@ def run_ours(args):
     stage_ms = {}
     step_ms = []
     m = 0
+    clocks.begin()
     for _ in range(args.steps):
         flush.fill_(1.0)
         s_ev = torch.cuda.Event(enable_timing=True)
@@ -475,6 +531,7 @@ def run_ours(args):
         for k, v in this.items():
             stage_ms.setdefault(k, []).append(v)
     step.events = None
+    clocks.end()
     clk = clocks.stop()
     local_ms = float(np.sum(step_ms))
     t = torch.tensor([local_ms], dtype=torch.float64, device=dev)
