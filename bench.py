@@ -133,41 +133,50 @@ class ClockSampler:
         self._stop = threading.Event()
         self._active = threading.Event()
         self.nt = None
+        self._h = None
+        self._smax = 0.0
 
     def begin(self):
-        """The timed region starts: NVML samples are kept from here on."""
+        """The timed region starts: NVML samples are kept from here on (one
+        is taken at once, one more at end())."""
+        self._sample()
         self._active.set()
 
     def end(self):
         self._active.clear()
+        self._sample()
 
-    def _nvml_loop(self):
+    def _sample(self):
+        if self._h is None:
+            return
+        try:
+            import pynvml
+            sm = pynvml.nvmlDeviceGetClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            self.nvml.append((float(sm), self._smax, int(bits)))
+        except Exception:
+            pass
+
+    def _nvml_open(self):
+        self._h = None
         try:
             import pynvml
             pynvml.nvmlInit()
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(self.gpu)
+            self._smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
         except Exception:  # no NVML binding or library: nvidia-smi alone
-            return
-        try:
-            h = pynvml.nvmlDeviceGetHandleByUUID(self.gpu)
-            smax = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
-            while True:
-                if self._active.is_set():
-                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-                    self.nvml.append((float(sm), float(smax), int(bits)))
-                if self._stop.wait(0.005):
-                    break
-        except Exception:
-            pass
-        finally:
-            try:
-                pynvml.nvmlShutdown()
-            except Exception:
-                pass
+            self._h = None
+
+    def _nvml_loop(self):
+        while not self._stop.wait(0.005):
+            if self._active.is_set():
+                self._sample()
 
     def start(self):
-        self.nt = threading.Thread(target=self._nvml_loop, daemon=True)
-        self.nt.start()
+        self._nvml_open()
+        if self._h is not None:
+            self.nt = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.nt.start()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -186,6 +195,12 @@ class ClockSampler:
         self._stop.set()
         if self.nt is not None:
             self.nt.join(timeout=5)
+        if self._h is not None:
+            try:
+                import pynvml
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
         sm, smax, reasons = [], [], set()
         for c, cm, bits in self.nvml:
             sm.append(c)
