@@ -6,7 +6,7 @@ benchmark scene (gsplat_core.pipeline.TrainingStep): projection, SH colour
 glue, tile intersection (count, scan, encode, radix sort, offsets),
 rasterize forward and backward, projection backward, SH backward.
 
-Default workload (N=1): BASELINE config 3 -- 1M Gaussians, SH degree 3,
+Default workload (N=1): benchmark config 3 -- 1M Gaussians, SH degree 3,
 one 1297x840 camera.  With --gpus N (torchrun, one rank per GPU) every rank
 renders its own camera of the same scene (weak scaling) and the
 per-Gaussian gradients are summed with one NCCL all-reduce per step.
@@ -40,7 +40,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # measured peer copy per direction per GPU on this pool (NVLink 5; 900 nominal)
 LINK_GBS = 770.0
 # DRAM bytes (read + write) per launch of each stage's dominant kernel from
-# one ncu capture of this benchmark (profiles/*_config3.md); None = not
+# one ncu capture of this benchmark (the committed ncu summaries); None = not
 # captured.  Valid for the config-3 workload only.
 PROFILED_TRAFFIC = {"rasterize_bwd": 47.1e6, "rasterize_fwd": 19.0e6,
                     "sh_bwd": 120.0e6 + 151.8e6, "projection_bwd": 86.4e6 + 13.7e6}
@@ -279,7 +279,7 @@ def algorithmic_bytes(stage, N, C, visible, m, pixels, K, slots, kept=None):
 
 # Warp instructions per launch of the rasterizers at config 3 (one pass of
 # `ncu --metrics gpu__time_duration.sum,smsp__inst_executed.sum`,
-# profiles/config3_step_launch_list.md): their roofline is the SMs' instruction issue,
+# the committed launch-list summary): their roofline is the SMs' instruction issue,
 # 148 SMs x 4 schedulers x the sampled SM clock, not HBM.
 PROFILED_INSTS = {"rasterize_bwd": 356_746_241 + 9_720,  # + its tile-order kernel
                   # the forward kernel, its tile-order kernel and the exact
@@ -393,7 +393,7 @@ def run_reference_arm(args):
            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
            "ms_per_step": round(ms, 3), "higher_is_better": True,
            "scaling": WORKLOADS[args.workload][1], "vs_baseline": None, "dtype": "f32",
-           "data": f"synthetic (seeded, BASELINE {args.workload} shapes)",
+           "data": f"synthetic (seeded, benchmark {args.workload} shapes)",
            "config": {"workload": WORKLOADS[args.workload][0], "cameras": cams,
                       "gaussians": sc.n, "isects_per_camera": m},
            "intersections_sorted_per_s": round(m / t_isect, 1),
@@ -408,7 +408,7 @@ def run_reference_arm(args):
 # ------------------------------------------------------------------ GPU arm
 
 def run_fit(args):
-    """the image-fitting trainer's step on device
+    """benchmark config 2: the image-fitting trainer's step on device
     (gsplat_core.fitting), the loss read back every step as the trainer
     does; with N GPUs every rank fits its own copy (replicas)."""
     import torch
@@ -452,7 +452,7 @@ def run_fit(args):
         out = {"metric": METRIC, "value": round(sc.width * sc.height * world / ms / 1e3, 3),
                "unit": "Mpix/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-               "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE cfg2)",
+               "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, benchmark cfg2)",
                "config": {"workload": WORKLOADS["cfg2"][0], "gaussians": sc.n,
                           "isects_last_step": fit.step.m,
                           "loss_first": losses[0], "loss_last": losses[-1],
@@ -687,7 +687,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
-            "data": f"synthetic (seeded, BASELINE {args.workload} distributions)",
+            "data": f"synthetic (seeded, benchmark {args.workload} distributions)",
             "config": {"workload": desc, "cameras": C_total,
                        "gaussians": sc.n, "visible": visible, "visible_any": visible_any,
                        "isects": m,
@@ -733,7 +733,7 @@ def main():
                     help="full reference steps timed for the cpu_baseline field")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg3",
-                    help="BASELINE config (cfg3 is the headline; the others fill the "
+                    help="benchmark config (cfg3 is the headline; the others fill the "
                          "per-config records)")
     ap.add_argument("--exchange", choices=["auto", "allreduce", "gather", "shard"], default="auto",
                     help="gradient exchange of the camera-sharded step (N > 1)")

@@ -124,7 +124,7 @@ def _clustered_means(rng, n, clusters=64, half_box=5.0):
 
 def config1(seed=0) -> Scene:
     """N=10k random Gaussians, SH0 colours fed straight to rasterize, one
-    256x256 camera at (0,0,-3) looking down +z."""
+    256x256 camera at (0,0,-3) looking down +z (benchmark config 1)."""
     rng = np.random.default_rng(seed)
     n = 10_000
     means = rng.uniform(-1.0, 1.0, size=(n, 3)).astype(np.float32)
@@ -140,7 +140,7 @@ def config1(seed=0) -> Scene:
 
 def config2(seed=0) -> Scene:
     """N=100k near-planar Gaussians for 2D image fitting at 512x512
-    (BASELINE config 2)."""
+    (benchmark config 2)."""
     rng = np.random.default_rng(seed)
     n = 100_000
     means = np.empty((n, 3), np.float32)
@@ -186,7 +186,7 @@ def _scene_sh3(name, rng, n, log_scale_range, viewmats, K, width, height, seed):
 def config3(seed=0, n=1_000_000) -> Scene:
     """N=1M SH3 Gaussians in 64 anisotropic clusters inside a 10 m box; one
     1297x840 camera (fx=fy=1150) 4 m from the box centre facing it
-    (the single-GPU headline)."""
+    (benchmark config 3, the single-GPU headline)."""
     rng = np.random.default_rng(seed)
     view = look_at((0.0, -1.0, -3.87298))[None]  # |p| = 4 m
     return _scene_sh3("cfg3", rng, n, (-6.0, -2.0), view,
@@ -195,7 +195,7 @@ def config3(seed=0, n=1_000_000) -> Scene:
 
 def config4(seed=0, n=3_000_000, cameras=32) -> Scene:
     """N=3M SH3 Gaussians, 32 cameras 1920x1080 (fx=fy=1600) on a 5 m
-    orbit (camera-sharded multi-GPU step)."""
+    orbit (benchmark config 4, camera-sharded multi-GPU step)."""
     rng = np.random.default_rng(seed)
     return _scene_sh3("cfg4", rng, n, (-6.0, -2.0), orbit(cameras, 5.0),
                       intrinsics(1600, 1600, 960.0, 540.0), 1920, 1080, seed)
@@ -203,7 +203,7 @@ def config4(seed=0, n=3_000_000, cameras=32) -> Scene:
 
 def config5(seed=0, n=6_000_000, cameras=8) -> Scene:
     """N=6M SH3 Gaussians with log-scales U[-3,-1] (heavy overdraw), 8
-    cameras 3840x2160 (fx=fy=3000) on a 3 m orbit."""
+    cameras 3840x2160 (fx=fy=3000) on a 3 m orbit (benchmark config 5)."""
     rng = np.random.default_rng(seed)
     return _scene_sh3("cfg5", rng, n, (-3.0, -1.0), orbit(cameras, 3.0),
                       intrinsics(3000, 3000, 1920.0, 1080.0), 3840, 2160, seed)

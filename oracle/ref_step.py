@@ -1,4 +1,4 @@
-"""The reference's CPU training step on every host thread (TEST / BASELINE
+"""The reference's CPU training step on every host thread (TEST / BENCHMARK
 INFRASTRUCTURE ONLY: bench.py's reference arm and CPU baseline use it; the
 product never does).
 

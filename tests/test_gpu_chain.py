@@ -1,6 +1,6 @@
 """The whole training step on the GPU (gsplat_core.pipeline.TrainingStep)
 against the oracle's composition of the same operators, element by
-element: at reduced sizes, at BASELINE config 3's full size, with config
+element: at reduced sizes, at benchmark config 3's full size, with config
 4's 32 cameras at 1920x1080, and with config 5's heavy overdraw in bands of
 tile rows.  Integer outputs (radii, sorted keys, flatten ids, tile offsets,
 last ids) are compared bit for bit on every entry, renders within 1e-5 abs
@@ -113,7 +113,7 @@ def test_training_step_matches_oracle(gs, oracle, cuda, n, cams):
 
 
 def test_full_size_config3_matches_oracle(gs, oracle, cuda):
-    """BASELINE config 3 at full size (1M Gaussians, SH3, 1297x840, 6.9M
+    """benchmark config 3 at full size (1M Gaussians, SH3, 1297x840, 6.9M
     intersections), every output element against the oracle; then the same
     step again gives the same lists and image bit for bit."""
     from gsplat_core import synthetic as S
@@ -134,7 +134,7 @@ def test_full_size_config3_matches_oracle(gs, oracle, cuda):
 
 
 def test_config4_cameras_match_oracle(gs, oracle, cuda):
-    """BASELINE config 4's batch (32 cameras at 1920x1080 on the 5 m orbit)
+    """benchmark config 4's batch (32 cameras at 1920x1080 on the 5 m orbit)
     over 100k Gaussians drawn from its 3M-Gaussian scene: every camera's
     lists, offsets, last ids and render, and the gradients summed over the
     32 cameras."""
@@ -150,7 +150,7 @@ def test_config4_cameras_match_oracle(gs, oracle, cuda):
 
 
 def test_config5_banded_matches_oracle(gs, oracle, cuda):
-    """BASELINE config 5's overdraw (log-scales U[-3,-1], one 3840x2160
+    """benchmark config 5's overdraw (log-scales U[-3,-1], one 3840x2160
     camera on the 3 m orbit) over 40k Gaussians of its 6M-Gaussian scene,
     rendered in bands of tile rows as the full config must be: each band's
     last ids are its own list's indices, i.e. the one-pass index minus the

@@ -137,7 +137,7 @@ def test_training_step_tile_cull(gs, cuda, full_size):
     """The training step with and without culling: the same renders bit for
     bit, gradients equal up to atomic order, fewer intersections walked;
     the culled keys sit sorted in the last places of the lists, with the
-    tile offsets pointing at their buckets.  full_size
+    tile offsets pointing at their buckets.  full_size: benchmark config 3
     (1M Gaussians, 1297x840)."""
     from gsplat_core import pipeline, synthetic as S
     if full_size:
