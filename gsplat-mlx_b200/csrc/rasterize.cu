@@ -587,11 +587,15 @@ __global__ void __launch_bounds__(kWalk) raster_fix_kernel(RArgs a,
   if (tid == 0) s_n = 0;
   __syncthreads();
   const int64_t p0 = (int64_t)blockIdx.x * kFixPixels;
+  const bool all_rows = y0 == 0 && y1 == a.H;  // then pixel p of the scan is pixel p
   for (int k = tid; k < kFixPixels; k += kWalk) {
     const int64_t p = p0 + k;
     if (p >= total) break;
-    const int64_t image = p / per_image, r = p - image * per_image;
-    const int64_t pix = (image * a.H + y0) * a.W + r;
+    int64_t pix = p;
+    if (!all_rows) {
+      const int64_t image = p / per_image, r = p - image * per_image;
+      pix = (image * a.H + y0) * a.W + r;
+    }
     if (__ldg(last_ids + pix) == kUndecided) s_list[atomicAdd(&s_n, 1)] = pix;
   }
   __syncthreads();
