@@ -671,6 +671,25 @@ def run_ours(args):
                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                         "peak_source": peak_kind, "traffic": PROFILED_TRAFFIC.get(top),
                         "algorithmic_bytes": int(bytes_of(top))}
+        # the step's roofline: the sum over its serial stages of each one's
+        # lower bound (algorithmic bytes at the HBM peak; for the rasterizers
+        # at config 3 the larger of that and their warp instructions at the
+        # issue peak; the exchange's bytes at the link rate) over the step time
+        t_min = 0.0
+        for k in avg:
+            if k == "sigma_bounds":  # on a side stream, beside the encode
+                continue
+            if k == "exchange":
+                t_min += exchange_bytes(sharded.exchange, sc.n, K, step.C, world) / (
+                    LINK_GBS * 1e9) * 1e3
+                continue
+            t = bytes_of(k) / (hbm * 1e9) * 1e3
+            if k in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+                t = max(t, PROFILED_INSTS[k] / (issue_peak * 1e9) * 1e3)
+            t_min += t
+        step_roofline = {"t_min_ms": round(t_min, 4), "frac": round(t_min / ms_step, 4),
+                         "how": "sum over the serial stages of max(algorithmic bytes / HBM "
+                                "peak, warp instructions / issue peak), exchange bytes / link"}
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             checker, kind = make_checker()
@@ -704,6 +723,7 @@ def run_ours(args):
             "intersections_sorted_per_s": round(m / (avg["isect_encode_sort"] / 1e3), 1),
             "stages_ms": stages,
             "roofline": roofline,
+            "step_roofline": step_roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h),
