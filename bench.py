@@ -651,11 +651,11 @@ def run_ours(args):
             b = bytes_of(k)
             stages[k] = {"ms": round(v, 4), "GBps": round(b / (v / 1e3) / 1e9, 1),
                          "frac_hbm": round(b / (v / 1e3) / 1e9 / hbm, 4)}
-            if k in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+            if k in PROFILED_INSTS and args.workload == "cfg3" and sharded.C == 1:
                 ginst = PROFILED_INSTS[k] / (v / 1e3) / 1e9
                 stages[k]["Ginst_per_s"] = round(ginst, 1)
                 stages[k]["frac_issue"] = round(ginst / issue_peak, 4)
-        if top in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+        if top in PROFILED_INSTS and args.workload == "cfg3" and sharded.C == 1:
             ginst = PROFILED_INSTS[top] / (avg[top] / 1e3) / 1e9
             roofline = {"kernel": top, "bound": "issue", "achieved": round(ginst, 1),
                         "peak": round(issue_peak, 1), "unit": "G warp-instructions/s",
@@ -684,7 +684,7 @@ def run_ours(args):
                     LINK_GBS * 1e9) * 1e3
                 continue
             t = bytes_of(k) / (hbm * 1e9) * 1e3
-            if k in PROFILED_INSTS and args.workload == "cfg3" and world == 1:
+            if k in PROFILED_INSTS and args.workload == "cfg3" and sharded.C == 1:
                 t = max(t, PROFILED_INSTS[k] / (issue_peak * 1e9) * 1e3)
             t_min += t
         step_roofline = {"t_min_ms": round(t_min, 4), "frac": round(t_min / ms_step, 4),
